@@ -90,6 +90,7 @@ def lib():
                 "or_ct_sub": (None, [C.c_void_p, U64P, U64P, U64P, U64P, C.c_uint32, U64P, U64P]),
                 "or_rescale": (C.c_int, [C.c_void_p, U64P, U64P, C.c_uint32, U64P, U64P]),
                 "or_u128_to_f64": (C.c_double, [C.c_uint64, C.c_uint64]),
+                "or_find_reject_seed": (C.c_uint64, [U64P, C.c_uint32, C.c_size_t, C.c_uint64, C.c_uint64, C.c_int]),
                 "or_lora_delta": (C.c_int, [C.c_void_p, U64P, F64P, C.c_uint32, F32P, F32P, C.c_uint32,
                                             C.c_uint64, C.c_int, F64P, F64P]),
             }
@@ -207,6 +208,14 @@ def chacha20_block(state):
     out = np.zeros(16, np.uint32)
     lib().or_chacha20_block(_p(st, U32P), _p(out, U32P))
     return out
+
+
+def find_reject_seed(moduli, n, start, count, kind):
+    """First seed in [start, start+count) whose encrypt (kind 0) or keygen
+    (kind 1) stream rejects a candidate, or None."""
+    m = np.asarray(moduli, dtype=np.uint64)
+    s = int(lib().or_find_reject_seed(_p(m, U64P), m.size, n, start, count, kind))
+    return None if s == 0xFFFFFFFFFFFFFFFF else s
 
 
 def u128_to_f64(v: int) -> float:

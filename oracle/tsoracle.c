@@ -1038,3 +1038,31 @@ int or_lora_delta(const or_ctx *c, const uint64_t *sk_ntt, const double *h,
     free(rep); free(c0); free(c1); free(p0); free(p1); free(pt); free(dec); free(ptn);
     return rc;
 }
+
+/* ======================================================================== */
+/* Test helper: find seeds whose stream exercises the rejection branches.   */
+/* ======================================================================== */
+/* kind 0: encrypt's uniform segments -- L x n range_u64(q_l) draws
+ *         (ciphertext.rs:185-191, rng.rs:124-133);
+ * kind 1: keygen's n range_u32(3) draws (sampling.rs:17-29, rng.rs:109-120).
+ * Returns the first seed in [start, start+count) that rejects at least one
+ * candidate, or UINT64_MAX. */
+uint64_t or_find_reject_seed(const uint64_t *moduli, uint32_t L, size_t n, uint64_t start,
+                             uint64_t count, int kind) {
+    for (uint64_t s = start; s < start + count; s++) {
+        or_rng r;
+        or_rng_from_seed(&r, s);
+        if (kind == 1) {
+            for (size_t i = 0; i < n; i++)
+                if (or_rng_next_u32(&r) < 1u) return s;
+            continue;
+        }
+        for (uint32_t l = 0; l < L; l++) {
+            uint64_t q = moduli[l];
+            uint64_t thr = (UINT64_MAX - q + 1) % q;
+            for (size_t i = 0; i < n; i++)
+                if (or_rng_next_u64(&r) < thr) return s;
+        }
+    }
+    return UINT64_MAX;
+}

@@ -166,6 +166,11 @@ int or_lora_delta(const or_ctx *c, const uint64_t *sk_ntt, const double *h,
                   uint32_t d, const float *lora_a, const float *lora_b, uint32_t r,
                   uint64_t enc_seed, int mode, double *delta, double *intermediate);
 
+/* Test helper: first seed in [start, start+count) whose encrypt (kind 0) or
+ * keygen (kind 1) stream hits a rejection; UINT64_MAX if none. */
+uint64_t or_find_reject_seed(const uint64_t *moduli, uint32_t L, size_t n, uint64_t start,
+                             uint64_t count, int kind);
+
 #ifdef __cplusplus
 }
 #endif

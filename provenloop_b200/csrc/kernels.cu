@@ -1,0 +1,820 @@
+// kernels.cu -- CUDA kernels of the tsgpu CKKS engine (sm_100a).
+//
+// Every kernel reproduces a step of tensafe-he-core (cited per kernel) with
+// exact integer arithmetic and, for the f64 FFT, the same rounding sequence,
+// so ciphertexts and NTT outputs are bit-identical to the reference's.
+#include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "kernels.cuh"
+
+namespace tsg {
+
+namespace {
+
+std::mutex g_attr_mu;
+std::set<std::pair<const void*, int>> g_attr_done;
+
+template <class K>
+cudaError_t ensure_smem(K* kernel, size_t bytes) {
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> g(g_attr_mu);
+    auto key = std::make_pair((const void*)kernel, dev);
+    if (g_attr_done.count(key)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) g_attr_done.insert(key);
+    return e;
+}
+
+// Candidate index of the i-th accepted draw given the ascending list of
+// rejected candidate indexes (the reference's rejection loops skip them).
+__device__ __forceinline__ uint32_t cand_index(uint32_t i, const uint32_t* rej, uint32_t nrej) {
+    uint32_t c = i;
+    for (uint32_t t = 0; t < nrej; t++)
+        if (rej[t] <= c) c++;
+    return c;
+}
+
+__device__ __forceinline__ uint64_t word64(uint64_t seed, uint64_t w) {
+    return (uint64_t)chacha_word(seed, w) | ((uint64_t)chacha_word(seed, w + 1) << 32);
+}
+
+// Block-wide exclusive scan of one int per thread (blockDim.x <= 1024).
+__device__ int block_exclusive_scan(int x, int* total) {
+    __shared__ int warp_sums[32];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sums[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+        const int nw = (blockDim.x + 31) >> 5;
+        int v = lane < nw ? warp_sums[lane] : 0;
+        int vi = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, vi, o);
+            if (lane >= o) vi += y;
+        }
+        if (lane < nw) warp_sums[lane] = vi - v;
+        if (lane == 31) warp_sums[31] = vi;  // total (nw <= 32)
+    }
+    __syncthreads();
+    const int res = incl - x + warp_sums[wid];
+    *total = warp_sums[31];
+    __syncthreads();
+    return res;
+}
+
+}  // namespace
+
+#define TSG_LOGN_SWITCH(logn, ...)                                \
+    switch (logn) {                                               \
+        case 10: { constexpr int LG = 10; __VA_ARGS__; } break;   \
+        case 11: { constexpr int LG = 11; __VA_ARGS__; } break;   \
+        case 12: { constexpr int LG = 12; __VA_ARGS__; } break;   \
+        case 13: { constexpr int LG = 13; __VA_ARGS__; } break;   \
+        case 14: { constexpr int LG = 14; __VA_ARGS__; } break;   \
+        default: return cudaErrorInvalidValue;                    \
+    }
+
+// ======================================================================
+// Plain batched NTT / INTT (ntt.rs:79-141)
+// ======================================================================
+template <int LOGN, bool INV>
+__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+    k_ntt(uint64_t* __restrict__ data, const LimbTab* __restrict__ tabs, int lmod, int l0) {
+    extern __shared__ __align__(16) uint64_t sm[];
+    const long long p = blockIdx.x;
+    const LimbTab T = tabs[l0 + (int)(p % lmod)];
+    uint64_t* a = data + (p << LOGN);
+    auto ld = [&](int j) { return a[j]; };
+    auto st = [&](int j, uint64_t x) { a[j] = x; };
+    if (INV)
+        ntt_inverse_block<LOGN>(sm, T, ld, st);
+    else
+        ntt_forward_block<LOGN>(sm, T, ld, st);
+}
+
+cudaError_t launch_ntt(const DevCtx& c, uint64_t* data, long long P, int lmod, int l0, bool inverse, cudaStream_t s) {
+    if (P <= 0) return cudaSuccess;
+    const size_t smem = (size_t)c.n * 8;
+    TSG_LOGN_SWITCH(c.logn, {
+        auto kern = inverse ? k_ntt<LG, true> : k_ntt<LG, false>;
+        cudaError_t e = ensure_smem(kern, smem);
+        if (e != cudaSuccess) return e;
+        kern<<<(unsigned)P, NttCfg<LG>::NT, smem, s>>>(data, c.tabs, lmod, l0);
+    });
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// Element-wise limb ops (rns.rs:217-253)
+// ======================================================================
+__global__ void k_elementwise(uint64_t* __restrict__ out, const uint64_t* __restrict__ a,
+                              const uint64_t* __restrict__ b, long long total, int logn, int L, int bcast, int op,
+                              const LimbTab* __restrict__ tabs) {
+    const long long stride = (long long)gridDim.x * blockDim.x * 2;
+    for (long long idx = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 2; idx < total; idx += stride) {
+        const long long p = idx >> logn;
+        const int limb = (int)(p % L);
+        const long long bi = bcast ? (((long long)limb << logn) + (idx & ((1LL << logn) - 1))) : idx;
+        const uint64_t q = __ldg(&tabs[limb].q);
+        const ulonglong2 av = *reinterpret_cast<const ulonglong2*>(a + idx);
+        const ulonglong2 bv = *reinterpret_cast<const ulonglong2*>(b + bi);
+        ulonglong2 o;
+        if (op == EW_MUL) {
+            const uint64_t mu = __ldg(&tabs[limb].bmu);
+            const int k = __ldg(&tabs[limb].bk);
+            o.x = mul_barrett(av.x, bv.x, q, mu, k);
+            o.y = mul_barrett(av.y, bv.y, q, mu, k);
+        } else if (op == EW_ADD) {
+            o.x = add_mod(av.x, bv.x, q);
+            o.y = add_mod(av.y, bv.y, q);
+        } else {
+            o.x = sub_mod(av.x, bv.x, q);
+            o.y = sub_mod(av.y, bv.y, q);
+        }
+        *reinterpret_cast<ulonglong2*>(out + idx) = o;
+    }
+}
+
+cudaError_t launch_elementwise(const DevCtx& c, uint64_t* out, const uint64_t* a, const uint64_t* b, long long P,
+                               int L, bool b_bcast, EwOp op, cudaStream_t s) {
+    const long long total = P << c.logn;
+    if (total <= 0) return cudaSuccess;
+    long long blocks = (total / 2 + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    k_elementwise<<<(unsigned)blocks, 256, 0, s>>>(out, a, b, total, c.logn, L, b_bcast ? 1 : 0, (int)op, c.tabs);
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// Key generation (ciphertext.rs:77-103, sampling.rs:17-29)
+// ======================================================================
+// Draw r (range_u32(3), word i of the stream) maps through sample_ternary
+// (q = 3) and then the per-limb match to the secret coefficient:
+// r = 0 -> +1, r = 1 -> -1 (q-1), r = 2 -> 0.
+__device__ __forceinline__ uint64_t ternary_coeff(uint32_t r, uint64_t q) {
+    const uint32_t v = r % 3u;
+    return v == 0 ? 1ULL : (v == 1 ? q - 1 : 0ULL);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+    k_keygen(uint64_t* __restrict__ sk, const uint64_t* __restrict__ seeds, const LimbTab* __restrict__ tabs, int L,
+             uint32_t* flags, const StreamPlan* __restrict__ plans, int plan_mode) {
+    extern __shared__ __align__(16) uint64_t sm[];
+    constexpr int N = 1 << LOGN, NT = NttCfg<LOGN>::NT;
+    const int limb = blockIdx.x, key = blockIdx.y, tid = threadIdx.x;
+    if (plan_mode && flags[key] == 0) return;
+    const LimbTab T = tabs[limb];
+    const uint64_t seed = seeds[key];
+    if (!plan_mode) {
+        // word i = sample i; block b holds samples 16b .. 16b+15
+        bool rej = false;
+        for (int b = tid; b < N / 16; b += NT) {
+            uint32_t w[16];
+            chacha_block(seed, (uint32_t)b, w);
+#pragma unroll
+            for (int c = 0; c < 16; c++) {
+                rej |= (w[c] == 0u);  // range_u32(3) threshold is 1 (rng.rs:112)
+                sm[swz(16 * b + c)] = ternary_coeff(w[c], T.q);
+            }
+        }
+        if (rej && limb == 0) atomicOr(flags + key, 1u);
+    } else {
+        const StreamPlan& P = plans[key];
+        for (int i = tid; i < N; i += NT) {
+            const uint32_t ci = cand_index((uint32_t)i, P.rej[0], P.nrej[0]);
+            sm[swz(i)] = ternary_coeff(chacha_word(seed, P.off[0] + ci), T.q);
+        }
+    }
+    __syncthreads();
+    uint64_t* out = sk + (((size_t)key * L + limb) << LOGN);
+    ntt_forward_block<LOGN>(
+        sm, T, [&](int j) { return sm[swz(j)]; }, [&](int j, uint64_t x) { out[j] = x; });
+}
+
+cudaError_t launch_keygen(const DevCtx& c, uint64_t* sk, const uint64_t* seeds, int nkeys, uint32_t* flags,
+                          StreamPlan* plans, cudaStream_t s) {
+    const size_t smem = (size_t)c.n * 8;
+    TSG_LOGN_SWITCH(c.logn, {
+        cudaError_t e = ensure_smem(k_keygen<LG>, smem);
+        if (e != cudaSuccess) return e;
+        k_keygen<LG><<<dim3(c.L, nkeys), NttCfg<LG>::NT, smem, s>>>(sk, seeds, c.tabs, c.L, flags, plans, 0);
+    });
+    return cudaGetLastError();
+}
+
+cudaError_t launch_keygen_fix(const DevCtx& c, uint64_t* sk, const uint64_t* seeds, int nkeys, const uint32_t* flags,
+                              const StreamPlan* plans, cudaStream_t s) {
+    const size_t smem = (size_t)c.n * 8;
+    TSG_LOGN_SWITCH(c.logn, {
+        cudaError_t e = ensure_smem(k_keygen<LG>, smem);
+        if (e != cudaSuccess) return e;
+        k_keygen<LG><<<dim3(c.L, nkeys), NttCfg<LG>::NT, smem, s>>>(sk, seeds, c.tabs, c.L,
+                                                                      const_cast<uint32_t*>(flags), plans, 1);
+    });
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// Encode (encoding.rs:173-207 + :250-278) and the encryption's Gaussian
+// ======================================================================
+__device__ __forceinline__ double slot_value(const SlotSrc& s, int v, int k) {
+    long long idx;
+    if (s.rep_cols > 0) {
+        if (k >= s.rep_cols * s.rep_d) return 0.0;
+        idx = (long long)v * s.stride + (k % s.rep_d);
+    } else {
+        if (k >= s.len) return 0.0;
+        idx = (long long)v * s.stride + k;
+    }
+    return s.is_f32 ? (double)__ldg(static_cast<const float*>(s.src) + idx)
+                    : __ldg(static_cast<const double*>(s.src) + idx);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(1024, 1) k_encode_a(SlotSrc src, FftTab T, double* scr) {
+    extern __shared__ __align__(16) double smd[];
+    using G = FftGeo<LOGN>;
+    const int v = blockIdx.y, blk = blockIdx.x;
+    constexpr int N = G::N, S = N / 2;
+    double* ore = scr + (size_t)v * 2 * N;
+    double* oim = ore + N;
+    // conjugate-symmetric real input: re[k] = re[N-1-k] = z[k], im = 0
+    auto gen = [&](int i, double& re, double& im) {
+        const int k = i < S ? i : N - 1 - i;
+        re = slot_value(src, v, k);
+        im = 0.0;
+    };
+    fft_pass_a<LOGN>(smd, smd + G::BLK, blk, gen, ore, oim, T);
+}
+
+// Pass B of the encode: final FFT stages, x 1/N, untwist, x Delta, round;
+// optionally the Gaussian error of the same encryption (rng.rs:152-157,
+// sampling.rs:51-58) from words gauss_off + 4j of the vector's stream.
+template <int LOGN>
+__global__ void __launch_bounds__(1024, 1)
+    k_encode_b(const double* __restrict__ scr, FftTab T, int64_t* __restrict__ m, int8_t* __restrict__ e,
+               const uint64_t* __restrict__ seeds, uint64_t gauss_off, unsigned long long* stats) {
+    using G = FftGeo<LOGN>;
+    constexpr int N = G::N;
+    const int v = blockIdx.x;
+    const double* ire = scr + (size_t)v * 2 * N;
+    const double* iim = ire + N;
+    const double inv_n = 1.0 / (double)N;
+    const double scale = 1099511627776.0;  // SCALE = 2^40
+    const uint64_t seed = e ? seeds[v] : 0;
+    int ties = 0;
+    for (int c0 = 4 * threadIdx.x; c0 < G::BLK; c0 += 4 * blockDim.x) {
+        double re[4][G::NB], im[4][G::NB];
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) {
+#pragma unroll
+            for (int b = 0; b < G::NB; b++) {
+                re[cc][b] = ire[c0 + cc + b * G::BLK];
+                im[cc][b] = iim[c0 + cc + b * G::BLK];
+            }
+            fft_pass_b_col<LOGN>(re[cc], im[cc], c0 + cc, T);
+        }
+#pragma unroll
+        for (int b = 0; b < G::NB; b++) {
+            const int j0 = c0 + b * G::BLK;
+            uint32_t w[16];
+            if (e) chacha_block(seed, (uint32_t)((gauss_off + 4ULL * j0) >> 4), w);
+#pragma unroll
+            for (int cc = 0; cc < 4; cc++) {
+                const int j = j0 + cc;
+                const double a_re = __dmul_rn(re[cc][b], inv_n);
+                const double a_im = __dmul_rn(im[cc][b], inv_n);
+                const double coeff =
+                    __dadd_rn(__dmul_rn(a_re, __ldg(T.twist_re + j)), __dmul_rn(a_im, __ldg(T.twist_im + j)));
+                m[(size_t)v * N + j] = f64_to_i64_sat(round(__dmul_rn(coeff, scale)));
+                if (e) {
+                    bool tie;
+                    const uint64_t u1 = (uint64_t)w[4 * cc] | ((uint64_t)w[4 * cc + 1] << 32);
+                    const uint64_t u2 = (uint64_t)w[4 * cc + 2] | ((uint64_t)w[4 * cc + 3] << 32);
+                    e[(size_t)v * N + j] = (int8_t)gaussian_round(u1, u2, 3.19, &tie);
+                    ties += tie ? 1 : 0;
+                }
+            }
+        }
+    }
+    if (ties && stats) atomicAdd(stats + STAT_NEAR_TIE, (unsigned long long)ties);
+}
+
+cudaError_t launch_encode(const DevCtx& c, const SlotSrc& src, int nvec, int64_t* m, int8_t* e,
+                          const uint64_t* seeds, uint64_t gauss_off, double* scratch, cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    if (e && (gauss_off & 15)) return cudaErrorInvalidValue;
+    TSG_LOGN_SWITCH(c.logn, {
+        using G = FftGeo<LG>;
+        const size_t smem = (size_t)2 * G::BLK * sizeof(double);
+        cudaError_t er = ensure_smem(k_encode_a<LG>, smem);
+        if (er != cudaSuccess) return er;
+        k_encode_a<LG><<<dim3(G::NB, nvec), 1024, smem, s>>>(src, c.fft, scratch);
+        k_encode_b<LG><<<nvec, 1024, 0, s>>>(scratch, c.fft, m, e, seeds, gauss_off, c.stats);
+    });
+    return cudaGetLastError();
+}
+
+// pt_ntt = NTT(encode(z)) (ciphertext.rs:539-545): signed residues per limb
+// (the residue can be q itself in the reference's negative branch; the lazy
+// NTT accepts it and reduces it like 0).
+template <int LOGN>
+__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+    k_ntt_signed(uint64_t* __restrict__ out, const int64_t* __restrict__ m, const LimbTab* __restrict__ tabs, int L) {
+    extern __shared__ __align__(16) uint64_t sm[];
+    const int limb = blockIdx.x, v = blockIdx.y;
+    const LimbTab T = tabs[limb];
+    const int64_t* mv = m + ((size_t)v << LOGN);
+    uint64_t* o = out + (((size_t)v * L + limb) << LOGN);
+    ntt_forward_block<LOGN>(
+        sm, T, [&](int j) { return signed_residue(mv[j], T.q, T.mu64); }, [&](int j, uint64_t x) { o[j] = x; });
+}
+
+cudaError_t launch_ntt_signed(const DevCtx& c, uint64_t* out, const int64_t* m, int nvec, cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    const size_t smem = (size_t)c.n * 8;
+    TSG_LOGN_SWITCH(c.logn, {
+        cudaError_t e = ensure_smem(k_ntt_signed<LG>, smem);
+        if (e != cudaSuccess) return e;
+        k_ntt_signed<LG><<<dim3(c.L, nvec), NttCfg<LG>::NT, smem, s>>>(out, m, c.tabs, c.L);
+    });
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// Encryption per (ciphertext, limb) (ciphertext.rs:167-229)
+// ======================================================================
+// c1 = NTT(a) with a = range_u64(q_l) draws (sampling.rs:62-64); then
+// c0 = NTT(m + e mod q_l) - c1 * s.  NTT(m) + NTT(e) of the reference equals
+// NTT(m + e) exactly (the transform is linear mod q and both are canonical).
+// Stream layout (speculative, no rejection): limb l's candidate i at words
+// 2*l*N + 2i, low word first; the Gaussian block follows at 2*L*N.
+template <int LOGN>
+__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+    k_encrypt_limb(uint64_t* __restrict__ ct, const int64_t* __restrict__ m, const int8_t* __restrict__ e,
+                   const uint64_t* __restrict__ sk, const int* __restrict__ sk_of, const uint64_t* __restrict__ seeds,
+                   const LimbTab* __restrict__ tabs, int L, uint32_t* flags, const StreamPlan* __restrict__ plans,
+                   int plan_mode) {
+    extern __shared__ __align__(16) uint64_t sm[];
+    constexpr int N = 1 << LOGN, NT = NttCfg<LOGN>::NT;
+    const int limb = blockIdx.x, v = blockIdx.y, tid = threadIdx.x;
+    if (plan_mode && flags[v] == 0) return;
+    const LimbTab T = tabs[limb];
+    const uint64_t seed = seeds[v];
+    uint64_t* c0 = ct + (((size_t)v * 2 * L + limb) << LOGN);
+    uint64_t* c1 = ct + (((size_t)v * 2 * L + L + limb) << LOGN);
+    const uint64_t* s = sk + (((size_t)(sk_of ? sk_of[v] : 0) * L + limb) << LOGN);
+    const int64_t* mv = m + ((size_t)v << LOGN);
+    const int8_t* ev = e + ((size_t)v << LOGN);
+
+    if (!plan_mode) {
+        const uint32_t blk0 = (uint32_t)limb * (N / 8);
+        bool rej = false;
+        for (int b = tid; b < N / 8; b += NT) {
+            uint32_t w[16];
+            chacha_block(seed, blk0 + (uint32_t)b, w);
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
+                rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
+                sm[swz(8 * b + c)] = mod_u64(u, T.q, T.mu64);
+            }
+        }
+        if (rej) atomicOr(flags + v, 1u);
+    } else {
+        const StreamPlan& P = plans[v];
+        for (int i = tid; i < N; i += NT) {
+            const uint32_t ci = cand_index((uint32_t)i, P.rej[limb], P.nrej[limb]);
+            sm[swz(i)] = mod_u64(word64(seed, P.off[limb] + 2ULL * ci), T.q, T.mu64);
+        }
+    }
+    __syncthreads();
+    ntt_forward_block<LOGN>(
+        sm, T, [&](int j) { return sm[swz(j)]; }, [&](int j, uint64_t x) { c1[j] = x; });
+    __syncthreads();
+    ntt_forward_block<LOGN>(
+        sm, T,
+        [&](int j) {
+            return add_mod(signed_residue(mv[j], T.q, T.mu64), signed_residue((int64_t)ev[j], T.q, T.mu64), T.q);
+        },
+        [&](int j, uint64_t x) {
+            // same thread wrote c1[j] in the previous transform's last pass
+            const uint64_t as = mul_barrett(c1[j], s[j], T.q, T.bmu, T.bk);
+            c0[j] = sub_mod(x, as, T.q);
+        });
+}
+
+cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m, const int8_t* e, const uint64_t* sk,
+                                 const int* sk_of, const uint64_t* seeds, int nvec, uint32_t* flags,
+                                 const StreamPlan* plans, bool plan_mode, cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    const size_t smem = (size_t)c.n * 8;
+    TSG_LOGN_SWITCH(c.logn, {
+        cudaError_t er = ensure_smem(k_encrypt_limb<LG>, smem);
+        if (er != cudaSuccess) return er;
+        k_encrypt_limb<LG><<<dim3(c.L, nvec), NttCfg<LG>::NT, smem, s>>>(ct, m, e, sk, sk_of, seeds, c.tabs, c.L,
+                                                                          flags, plans, plan_mode ? 1 : 0);
+    });
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// Exact stream plans for streams that hit a rejection (rng.rs:109-133)
+// ======================================================================
+__global__ void __launch_bounds__(1024, 1)
+    k_plan(const uint64_t* __restrict__ seeds, const uint32_t* __restrict__ flags, StreamPlan* plans, SegList segs,
+           const LimbTab* __restrict__ tabs, int N, unsigned long long* stats) {
+    const int v = blockIdx.x, tid = threadIdx.x;
+    if (flags[v] == 0) return;
+    __shared__ uint32_t s_nrej;
+    __shared__ uint32_t s_rej[kMaxRej + 1];
+    __shared__ uint32_t s_overflow;
+    StreamPlan& P = plans[v];
+    const uint64_t seed = seeds[v];
+    uint64_t off = 0;
+    if (tid == 0) s_overflow = 0;
+    for (int sg = 0; sg < segs.count; sg++) {
+        const int kind = segs.kind[sg];
+        if (tid == 0) {
+            P.off[sg] = off;
+            P.nrej[sg] = 0;
+            s_nrej = 0;
+        }
+        __syncthreads();
+        if (kind == SEG_GAUSS) {
+            off += 4ULL * N;
+            continue;
+        }
+        const int wpc = kind == SEG_UNIFORM ? 2 : 1;
+        const uint64_t thr = kind == SEG_UNIFORM ? tabs[segs.limb[sg]].thresh : 1ULL;
+        long long accepted = 0, base = 0;
+        // bounded: a segment that needs more than 4N candidates is reported
+        // as an overflow instead of scanning on
+        while (accepted < N && base < 4LL * N) {
+            int ok[8], cnt = 0;
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+                const uint64_t cidx = (uint64_t)base + (uint64_t)tid * 8 + t;
+                const uint64_t w = off + (uint64_t)wpc * cidx;
+                const uint64_t val = kind == SEG_UNIFORM ? word64(seed, w) : (uint64_t)chacha_word(seed, w);
+                ok[t] = val >= thr;
+                cnt += ok[t];
+            }
+            int total;
+            const int pre = block_exclusive_scan(cnt, &total);
+            int run = pre;
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+                if (!ok[t] && accepted + run < N) {
+                    const uint32_t slot = atomicAdd(&s_nrej, 1u);
+                    if (slot < kMaxRej) s_rej[slot] = (uint32_t)(base + (long long)tid * 8 + t);
+                    else s_overflow = 1;
+                }
+                run += ok[t];
+            }
+            accepted += total;
+            base += 8LL * blockDim.x;
+            __syncthreads();
+        }
+        if (tid == 0 && accepted < N) s_overflow = 1;
+        __syncthreads();
+        if (tid == 0) {
+            const uint32_t nr = s_nrej < kMaxRej ? s_nrej : kMaxRej;
+            // sort ascending (tiny list)
+            for (uint32_t a = 1; a < nr; a++) {
+                uint32_t x = s_rej[a];
+                int b = (int)a - 1;
+                while (b >= 0 && s_rej[b] > x) {
+                    s_rej[b + 1] = s_rej[b];
+                    b--;
+                }
+                s_rej[b + 1] = x;
+            }
+            for (uint32_t a = 0; a < nr; a++) P.rej[sg][a] = s_rej[a];
+            P.nrej[sg] = nr;
+        }
+        __syncthreads();
+        off += (uint64_t)wpc * ((uint64_t)N + s_nrej);
+        __syncthreads();
+    }
+    if (tid == 0) {
+        P.status = s_overflow;
+        if (stats) {
+            atomicAdd(stats + STAT_REJECT, 1ULL);
+            if (s_overflow) atomicAdd(stats + STAT_PLAN_FAIL, 1ULL);
+        }
+    }
+}
+
+cudaError_t launch_plan(const DevCtx& c, const uint64_t* seeds, int nstreams, const uint32_t* flags, StreamPlan* plans,
+                        const SegList& segs, cudaStream_t s) {
+    if (nstreams <= 0) return cudaSuccess;
+    k_plan<<<nstreams, 1024, 0, s>>>(seeds, flags, plans, segs, c.tabs, c.n, c.stats);
+    return cudaGetLastError();
+}
+
+__global__ void k_gauss_fix(int8_t* __restrict__ e, const uint64_t* __restrict__ seeds, int N,
+                            const uint32_t* __restrict__ flags, const StreamPlan* __restrict__ plans, int seg,
+                            unsigned long long* stats) {
+    const int v = blockIdx.x;
+    if (flags[v] == 0) return;
+    const uint64_t seed = seeds[v];
+    const uint64_t off = plans[v].off[seg];
+    int ties = 0;
+    for (int j = threadIdx.x; j < N; j += blockDim.x) {
+        const uint64_t w = off + 4ULL * j;
+        bool tie;
+        e[(size_t)v * N + j] = (int8_t)gaussian_round(word64(seed, w), word64(seed, w + 2), 3.19, &tie);
+        ties += tie;
+    }
+    if (ties && stats) atomicAdd(stats + STAT_NEAR_TIE, (unsigned long long)ties);
+}
+
+cudaError_t launch_gauss_fix(const DevCtx& c, int8_t* e, const uint64_t* seeds, int nvec, const uint32_t* flags,
+                             const StreamPlan* plans, int seg, cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    k_gauss_fix<<<nvec, 512, 0, s>>>(e, seeds, c.n, flags, plans, seg, c.stats);
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// Decrypt front half: (ct x pt) then c0 + c1*s, INTT (ciphertext.rs:327-349)
+// ======================================================================
+template <int LOGN>
+__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+    k_decrypt_limb(uint64_t* __restrict__ M, int nl, const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs,
+                   const uint64_t* __restrict__ sk, const int* __restrict__ sk_of, const uint64_t* __restrict__ pt,
+                   const int* __restrict__ pt_sel, int per_ct, const LimbTab* __restrict__ tabs, int L) {
+    extern __shared__ __align__(16) uint64_t sm[];
+    const int limb = blockIdx.x, v = blockIdx.y;
+    const LimbTab T = tabs[limb];
+    const int ci = v / per_ct;
+    const uint64_t* c0 = cts + (size_t)ci * ct_stride + ((size_t)limb << LOGN);
+    const uint64_t* c1 = cts + (size_t)ci * ct_stride + ((size_t)(ct_limbs + limb) << LOGN);
+    const uint64_t* s = sk + (((size_t)(sk_of ? sk_of[ci] : 0) * L + limb) << LOGN);
+    const uint64_t* p = nullptr;
+    if (pt) {
+        const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
+        p = pt + (((size_t)pv * L + limb) << LOGN);
+    }
+    uint64_t* out = M + (((size_t)v * nl + limb) << LOGN);
+    ntt_inverse_block<LOGN>(
+        sm, T,
+        [&](int j) {
+            uint64_t a0 = c0[j], a1 = c1[j];
+            if (p) {
+                const uint64_t pj = p[j];
+                a0 = mul_barrett(a0, pj, T.q, T.bmu, T.bk);
+                a1 = mul_barrett(a1, pj, T.q, T.bmu, T.bk);
+            }
+            return add_mod(a0, mul_barrett(a1, s[j], T.q, T.bmu, T.bk), T.q);
+        },
+        [&](int j, uint64_t x) { out[j] = x; });
+}
+
+cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uint64_t* cts, long long ct_stride,
+                                 int ct_limbs, const uint64_t* sk, const int* sk_of, const uint64_t* pt,
+                                 const int* pt_sel, int per_ct, int nvec, cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    const size_t smem = (size_t)c.n * 8;
+    TSG_LOGN_SWITCH(c.logn, {
+        cudaError_t er = ensure_smem(k_decrypt_limb<LG>, smem);
+        if (er != cudaSuccess) return er;
+        k_decrypt_limb<LG><<<dim3(nl, nvec), NttCfg<LG>::NT, smem, s>>>(M, nl, cts, ct_stride, ct_limbs, sk, sk_of, pt,
+                                                                        pt_sel, per_ct, c.tabs, c.L);
+    });
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// Decrypt back half: CRT / centring, / scale, canonical embedding
+// (ciphertext.rs:351-399, encoding.rs:219-239, :295-315)
+// ======================================================================
+__device__ __forceinline__ double crt_coeff(uint64_t m0, uint64_t m1, const CrtConst& K) {
+    const uint64_t m0q1 = mod_u64(m0, K.q1, K.mu64_1);
+    const uint64_t diff = m1 >= m0q1 ? m1 - m0q1 : K.q1 - m0q1 + m1;
+    const uint64_t k = mul_barrett(diff, K.q0inv, K.q1, K.bmu1, K.bk1);
+    // mu = m0 + k*q0 (< q0*q1 < 2^101)
+    uint64_t lo = k * K.q0;
+    uint64_t hi = mulhi64(k, K.q0);
+    lo += m0;
+    hi += (lo < m0) ? 1 : 0;
+    // (the reference's "mu >= Q -> mu % Q" branch cannot trigger: mu < Q)
+    const bool neg = (hi > K.H_hi) || (hi == K.H_hi && lo > K.H_lo);
+    if (neg) {
+        const uint64_t dlo = K.Q_lo - lo;
+        const uint64_t dhi = K.Q_hi - hi - (K.Q_lo < lo ? 1 : 0);
+        return -u128_to_f64(dhi, dlo);
+    }
+    return u128_to_f64(hi, lo);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(1024, 1)
+    k_decode_a(const uint64_t* __restrict__ M, int nl, int crt, double scale, CrtConst K, uint64_t q0, FftTab T,
+               double* scr) {
+    extern __shared__ __align__(16) double smd[];
+    using G = FftGeo<LOGN>;
+    constexpr int N = G::N;
+    const int v = blockIdx.y, blk = blockIdx.x;
+    const uint64_t* m0p = M + ((size_t)v * nl << LOGN);
+    const uint64_t* m1p = m0p + N;
+    double* ore = scr + (size_t)v * 2 * N;
+    double* oim = ore + N;
+    const uint64_t half_q = q0 / 2;
+    auto gen = [&](int i, double& re, double& im) {
+        double sgn;
+        if (crt) {
+            sgn = crt_coeff(m0p[i], m1p[i], K);
+        } else {
+            const uint64_t x = m0p[i];
+            sgn = x > half_q ? -__ull2double_rn(q0 - x) : __ull2double_rn(x);
+        }
+        const double coeff = __ddiv_rn(sgn, scale);
+        re = __dmul_rn(coeff, __ldg(T.twist_re + i));
+        im = __dmul_rn(-coeff, __ldg(T.twist_im + i));
+    };
+    fft_pass_a<LOGN>(smd, smd + G::BLK, blk, gen, ore, oim, T);
+}
+
+// Pass B of the decode: remaining stages; slot j < N/2 is Re(X[j]).  Either
+// store every slot or reduce `seg_cols` segments of `seg_d` slots (the
+// ZeRo-MOAI segment sums, inference_engine.py:1382-1386) deterministically.
+template <int LOGN>
+__global__ void __launch_bounds__(1024, 1)
+    k_decode_b(const double* __restrict__ scr, FftTab T, double* __restrict__ out_slots, double* __restrict__ seg_out,
+               int seg_d, int seg_cols) {
+    extern __shared__ __align__(16) double slots[];
+    using G = FftGeo<LOGN>;
+    constexpr int N = G::N, S = N / 2;
+    const int v = blockIdx.x;
+    const double* ire = scr + (size_t)v * 2 * N;
+    const double* iim = ire + N;
+    for (int c0 = 4 * threadIdx.x; c0 < G::BLK; c0 += 4 * blockDim.x) {
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) {
+            const int c = c0 + cc;
+            if (G::NS == 0) {
+                if (c < S) {
+                    const double x = ire[c];
+                    if (seg_out) slots[c] = x;
+                    else out_slots[(size_t)v * S + c] = x;
+                }
+                continue;
+            }
+            double re[G::NB], im[G::NB];
+#pragma unroll
+            for (int b = 0; b < G::NB; b++) {
+                re[b] = ire[c + b * G::BLK];
+                im[b] = iim[c + b * G::BLK];
+            }
+            fft_pass_b_col<LOGN>(re, im, c, T);
+#pragma unroll
+            for (int b = 0; b < G::NB; b++) {
+                const int j = c + b * G::BLK;
+                if (j < S) {
+                    if (seg_out) slots[j] = re[b];
+                    else out_slots[(size_t)v * S + j] = re[b];
+                }
+            }
+        }
+    }
+    if (!seg_out) return;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int sgi = wid; sgi < seg_cols; sgi += nw) {
+        double acc = 0.0;
+        for (int t = lane; t < seg_d; t += 32) acc += slots[sgi * seg_d + t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) seg_out[(size_t)v * seg_cols + sgi] = acc;
+    }
+}
+
+cudaError_t launch_decode(const DevCtx& c, const uint64_t* M, int nl, bool crt, double scale, int nvec,
+                          double* out_slots, double* seg_out, int seg_d, int seg_cols, double* scratch, cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    if (crt && nl < 2) return cudaErrorInvalidValue;
+    const CrtConst K = c.crt;
+    cudaError_t er;
+    TSG_LOGN_SWITCH(c.logn, {
+        using G = FftGeo<LG>;
+        const size_t smem_a = (size_t)2 * G::BLK * sizeof(double);
+        er = ensure_smem(k_decode_a<LG>, smem_a);
+        if (er != cudaSuccess) return er;
+        k_decode_a<LG><<<dim3(G::NB, nvec), 1024, smem_a, s>>>(M, nl, crt ? 1 : 0, scale, K, K.q0, c.fft, scratch);
+        const size_t smem_b = seg_out ? (size_t)(G::N / 2) * sizeof(double) : 0;
+        er = ensure_smem(k_decode_b<LG>, smem_b);
+        if (er != cudaSuccess) return er;
+        k_decode_b<LG><<<nvec, 1024, smem_b, s>>>(scratch, c.fft, out_slots, seg_out, seg_d, seg_cols);
+    });
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// ZeRo-MOAI tail: gather segment sums, B @ intermediate
+// ======================================================================
+__global__ void k_gather_inter(const double* __restrict__ seg, double* __restrict__ inter, int ndelta, int nb,
+                               int cols, int r) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (long long)ndelta * r) return;
+    const int i = (int)(t / r), k = (int)(t % r);
+    const int b = k / cols, c = k % cols;
+    inter[t] = seg[((size_t)i * nb + b) * cols + c];
+}
+
+cudaError_t launch_gather_inter(const double* seg, double* inter, int ndelta, int nb, int cols, int r, cudaStream_t s) {
+    const long long tot = (long long)ndelta * r;
+    if (tot <= 0) return cudaSuccess;
+    k_gather_inter<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(seg, inter, ndelta, nb, cols, r);
+    return cudaGetLastError();
+}
+
+__global__ void k_bmat(const float* __restrict__ B, const double* __restrict__ inter, double* __restrict__ delta,
+                       int nvec, int d, int r, const int* __restrict__ b_sel, long long b_stride) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (long long)nvec * d) return;
+    const int i = (int)(t / d), row = (int)(t % d);
+    const float* Bm = B + (b_sel ? (long long)b_sel[i] * b_stride : 0) + (long long)row * r;
+    const double* x = inter + (size_t)i * r;
+    double acc = 0.0;
+    for (int k = 0; k < r; k++) acc += (double)__ldg(Bm + k) * x[k];
+    delta[t] = acc;
+}
+
+cudaError_t launch_bmat(const float* B, const double* inter, double* delta, int nvec, int d, int r, const int* b_sel,
+                        long long b_stride, cudaStream_t s) {
+    const long long tot = (long long)nvec * d;
+    if (tot <= 0) return cudaSuccess;
+    k_bmat<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(B, inter, delta, nvec, d, r, b_sel, b_stride);
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// DP Gaussian noise (inference_engine.py:1436-1456)
+// ======================================================================
+__global__ void k_dp_noise(double* __restrict__ h, int d, double clip, double sigma, const uint64_t* __restrict__ seeds) {
+    __shared__ double red[32];
+    const int v = blockIdx.x;
+    double* x = h + (size_t)v * d;
+    double acc = 0.0;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) acc += x[j] * x[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double y = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
+        if (threadIdx.x == 0) red[0] = y;
+    }
+    __syncthreads();
+    const double norm = sqrt(red[0]);
+    const double f = norm > clip ? clip / norm : 1.0;
+    const uint64_t seed = seeds[v];
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        // Box-Muller draw j uses words 4j..4j+3 of the stream (rng.rs:152-157)
+        const uint64_t w = 4ULL * j;
+        uint32_t b[16];
+        chacha_block(seed, (uint32_t)(w >> 4), b);
+        const int o = (int)(w & 15);
+        uint32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+        for (int t = 0; t < 16; t += 4)
+            if (t == o) {
+                a0 = b[t];
+                a1 = b[t + 1];
+                a2 = b[t + 2];
+                a3 = b[t + 3];
+            }
+        const double u1 = u64_to_unit((uint64_t)a0 | ((uint64_t)a1 << 32));
+        const double u2 = u64_to_unit((uint64_t)a2 | ((uint64_t)a3 << 32));
+        const double z = sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2);
+        const double xv = norm > clip ? x[j] * f : x[j];
+        x[j] = xv + z * sigma;
+    }
+}
+
+cudaError_t launch_dp_noise(double* h, int nvec, int d, double clip, double sigma, const uint64_t* seeds,
+                            cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    k_dp_noise<<<nvec, 256, 0, s>>>(h, d, clip, sigma, seeds);
+    return cudaGetLastError();
+}
+
+}  // namespace tsg

@@ -1,0 +1,145 @@
+// kernels.cuh -- internal launcher interface between the host API
+// (tsgpu.cu) and the CUDA kernels (kernels.cu).  Not part of the public ABI.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "ntt.cuh"
+#include "fft.cuh"
+
+namespace tsg {
+
+// Random-stream segments consumed by one keygen / encrypt call, in the
+// reference's order (ciphertext.rs:77-103, :167-229, :114-154, :240-319).
+enum SegKind : int { SEG_UNIFORM = 0, SEG_TERNARY = 1, SEG_GAUSS = 2 };
+constexpr int kMaxSeg = 10;
+constexpr int kMaxRej = 16;
+
+struct SegList {
+    int count;
+    int kind[kMaxSeg];
+    int limb[kMaxSeg];  // modulus index for SEG_UNIFORM
+};
+
+// Exact stream layout of one call: word offset of each segment and the
+// candidate indexes the reference's rejection loops discarded.
+struct StreamPlan {
+    uint64_t off[kMaxSeg];
+    uint32_t nrej[kMaxSeg];
+    uint32_t rej[kMaxSeg][kMaxRej];
+    uint32_t status;  // 0 ok, 1 more than kMaxRej rejections in a segment
+    uint32_t pad;
+};
+
+// Device counters (unsigned long long each).
+enum Stat : int {
+    STAT_NEAR_TIE = 0,    // Gaussian samples within 1e-9 of a half-integer
+    STAT_REJECT = 1,      // streams that needed the exact-plan repair
+    STAT_PLAN_FAIL = 2,   // streams whose rejections exceeded kMaxRej
+    STAT_COUNT = 4
+};
+
+// CRT(q0, q1) constants of decrypt (ciphertext.rs:351-356).
+struct CrtConst {
+    uint64_t q0, q1, mu64_1, q0inv, bmu1;
+    int bk1;
+    int pad;
+    uint64_t Q_lo, Q_hi;  // q0*q1
+    uint64_t H_lo, H_hi;  // (q0*q1)/2
+};
+
+struct DevCtx {
+    int logn, n, L;
+    const LimbTab* tabs;  // device array [L]
+    FftTab fft;
+    double scale;         // Delta = 2^40 (params.rs:9-12)
+    CrtConst crt;
+    unsigned long long* stats;  // device [STAT_COUNT]
+};
+
+// Where slot values come from for an encode (one "vector" per encode):
+// slot k of vector v is
+//   rep_cols > 0 : (k < rep_cols*rep_d) ? src[v*stride + k % rep_d] : 0
+//   otherwise    : (k < len) ? src[v*stride + k] : 0
+struct SlotSrc {
+    const void* src;
+    int is_f32;
+    int len;
+    long long stride;
+    int rep_d;
+    int rep_cols;
+};
+
+// ---------------------------------------------------------------- launchers
+// In-place forward/inverse NTT of P poly-limbs of `data` ([P][n]); the limb of
+// poly-limb p is l0 + p % lmod.
+cudaError_t launch_ntt(const DevCtx& c, uint64_t* data, long long P, int lmod, int l0, bool inverse,
+                       cudaStream_t s);
+// out[p][i] = a[p][i] (*|+|-) b[bp][i] mod q_{p % L}, bp = b_bcast ? p % L : p.
+enum EwOp : int { EW_MUL = 0, EW_ADD = 1, EW_SUB = 2 };
+cudaError_t launch_elementwise(const DevCtx& c, uint64_t* out, const uint64_t* a, const uint64_t* b, long long P,
+                               int L, bool b_bcast, EwOp op, cudaStream_t s);
+
+// Secret keys: sk[k][L][n] from seeds[k] (ciphertext.rs:77-103).
+cudaError_t launch_keygen(const DevCtx& c, uint64_t* sk, const uint64_t* seeds, int nkeys, uint32_t* flags,
+                          StreamPlan* plans, cudaStream_t s);
+
+// Encode slot vectors -> rounded coefficients m[v][n] (int64); when e != null,
+// also the encryption's Gaussian e[v][n] (int8) at word offset gauss_off of
+// stream seeds[v] (speculative: assumes no earlier rejection).
+cudaError_t launch_encode(const DevCtx& c, const SlotSrc& src, int nvec, int64_t* m, int8_t* e,
+                          const uint64_t* seeds, uint64_t gauss_off, double* scratch_cplx, cudaStream_t s);
+
+// pt_ntt[v][L][n] = NTT(residues of m[v]) (ciphertext.rs:539-545).
+cudaError_t launch_ntt_signed(const DevCtx& c, uint64_t* out, const int64_t* m, int nvec, cudaStream_t s);
+
+// Secret-key encryption of nvec vectors into ct[v][2][L][n]
+// (ciphertext.rs:167-229).  sk_of[v] selects the key (sk + sk_of[v]*L*n);
+// when plan_mode, only streams with flags[v] != 0 are (re)computed using
+// plans[v].
+cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m, const int8_t* e,
+                                 const uint64_t* sk, const int* sk_of, const uint64_t* seeds, int nvec,
+                                 uint32_t* flags, const StreamPlan* plans, bool plan_mode, cudaStream_t s);
+
+// Exact plans for flagged streams (one CTA per stream).
+cudaError_t launch_plan(const DevCtx& c, const uint64_t* seeds, int nstreams, const uint32_t* flags,
+                        StreamPlan* plans, const SegList& segs, cudaStream_t s);
+// Recompute the Gaussian e[v] of flagged streams from plan segment `seg`.
+cudaError_t launch_gauss_fix(const DevCtx& c, int8_t* e, const uint64_t* seeds, int nvec, const uint32_t* flags,
+                             const StreamPlan* plans, int seg, cudaStream_t s);
+// Redo keygen of flagged keys using their plans.
+cudaError_t launch_keygen_fix(const DevCtx& c, uint64_t* sk, const uint64_t* seeds, int nkeys,
+                              const uint32_t* flags, const StreamPlan* plans, cudaStream_t s);
+
+// Decrypt front half: M[v][j][n] = INTT( c0 (+) c1*s ) for limbs j < nl, where
+// the ciphertext of vector v is cts + ct_of(v)*ct_stride and, when pt !=
+// null, both components are first multiplied by pt + pt_of(v)*L*n
+// (ct x pt fused into decrypt; ciphertext.rs:408-429 then :327-349).
+// ct_of(v) = v / per_ct, pt_of(v) = (pt_sel ? pt_sel[v / per_ct] : 0)*per_ct + v % per_ct.
+cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uint64_t* cts, long long ct_stride,
+                                 int ct_limbs, const uint64_t* sk, const int* sk_of, const uint64_t* pt,
+                                 const int* pt_sel, int per_ct, int nvec, cudaStream_t s);
+
+// Decrypt back half (ciphertext.rs:351-399 + encoding.rs:219-315): CRT of
+// limbs 0/1 (crt) or limb-0 centring, / scale, canonical embedding.
+// Outputs either all slots (out_slots[v][S]) or, when seg_out != null, sums of
+// `seg_cols` consecutive `seg_d`-slot segments: seg_out[v*seg_cols + c].
+cudaError_t launch_decode(const DevCtx& c, const uint64_t* M, int nl, bool crt, double scale, int nvec,
+                          double* out_slots, double* seg_out, int seg_d, int seg_cols, double* scratch_cplx,
+                          cudaStream_t s);
+
+// delta[i][d] = sum_k B[d][k] * inter[i][k] (inference_engine.py:1392).
+cudaError_t launch_bmat(const float* B, const double* inter, double* delta, int nvec, int d, int r,
+                        const int* b_sel, long long b_stride, cudaStream_t s);
+
+// Gather per-batch segment sums into intermediate[i][r].
+cudaError_t launch_gather_inter(const double* seg, double* inter, int ndelta, int nb, int cols, int r,
+                                cudaStream_t s);
+
+// DP noise (inference_engine.py:1436-1456): clip ||h||_2 <= C, add N(0, sigma^2)
+// from the stream of seeds[v]; h is [nvec][d] f64 (in place).
+cudaError_t launch_dp_noise(double* h, int nvec, int d, double clip, double sigma, const uint64_t* seeds,
+                            cudaStream_t s);
+
+}  // namespace tsg

@@ -1,0 +1,1249 @@
+// tsgpu.cu -- host side of the C ABI declared in include/tsgpu.h.
+//
+// Owns contexts (parameter set, tables on the device, stream, scratch),
+// key / ciphertext / plaintext objects, and drives the kernels of
+// kernels.cu.  Parameter and table construction restates
+// tensafe-he-core/src/params.rs, rns.rs and encoding.rs (cited inline); all
+// per-ciphertext arithmetic runs on the GPU.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/tsgpu.h"
+#include "kernels.cuh"
+
+using namespace tsg;
+typedef unsigned __int128 u128;
+
+// =====================================================================
+// errors
+// =====================================================================
+static thread_local std::string t_err;
+
+static int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_err = buf;
+    return code;
+}
+
+static bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+#define CU(expr)                                                                               \
+    do {                                                                                       \
+        cudaError_t _e = (expr);                                                               \
+        if (_e != cudaSuccess) {                                                               \
+            return fail(_e == cudaErrorMemoryAllocation ? TS_ERR_OOM : TS_ERR_CUDA, "%s: %s (%s:%d)", \
+                        #expr, cudaGetErrorString(_e), __FILE__, __LINE__);                    \
+        }                                                                                      \
+    } while (0)
+
+// =====================================================================
+// host number theory (params.rs, rns.rs)
+// =====================================================================
+static uint64_t mulmod(uint64_t a, uint64_t b, uint64_t q) { return (uint64_t)(((u128)a * b) % q); }
+
+static uint64_t powmod(uint64_t b, uint64_t e, uint64_t q) {  // rns.rs:99-110
+    uint64_t r = 1;
+    b %= q;
+    while (e) {
+        if (e & 1) r = mulmod(r, b, q);
+        e >>= 1;
+        b = mulmod(b, b, q);
+    }
+    return r;
+}
+
+// Deterministic Miller-Rabin for 64-bit n (bases 2..37 are exact below
+// 3.3e24).  Decides primality exactly, like the reference's trial division
+// (params.rs:308-326), so the prime search returns the same prime.
+static bool is_prime(uint64_t n) {
+    if (n < 2) return false;
+    static const uint64_t small[] = {2, 3, 5, 7, 11, 13, 17, 19, 23, 29, 31, 37};
+    for (uint64_t p : small) {
+        if (n % p == 0) return n == p;
+    }
+    uint64_t d = n - 1;
+    int s = 0;
+    while ((d & 1) == 0) {
+        d >>= 1;
+        s++;
+    }
+    for (uint64_t a : small) {
+        uint64_t x = powmod(a, d, n);
+        if (x == 1 || x == n - 1) continue;
+        bool comp = true;
+        for (int r = 1; r < s; r++) {
+            x = mulmod(x, x, n);
+            if (x == n - 1) {
+                comp = false;
+                break;
+            }
+        }
+        if (comp) return false;
+    }
+    return true;
+}
+
+// params.rs:169-193: largest `bits`-bit prime == 1 mod two_n, searching down.
+static uint64_t find_ntt_prime(uint32_t bits, uint64_t two_n) {
+    uint64_t upper = bits >= 64 ? UINT64_MAX : ((1ULL << bits) - 1);
+    uint64_t lower = 1ULL << (bits - 1);
+    uint64_t c = upper - (upper % two_n) + 1;
+    if (c > upper) c -= two_n;
+    while (c >= lower) {
+        if (is_prime(c)) return c;
+        c -= two_n;
+        if (c < lower) break;
+    }
+    return 0;
+}
+
+// rns.rs:124-154: smallest g >= 2 with psi = g^((q-1)/2N) != 1 and psi^N = -1.
+static uint64_t find_psi(uint64_t n, uint64_t q) {
+    if (q % (2 * n) != 1) return 0;
+    uint64_t e = (q - 1) / (2 * n);
+    for (uint64_t g = 2; g < 10000 && g < q; g++) {
+        uint64_t psi = powmod(g, e, q);
+        if (psi <= 1) continue;
+        if (powmod(psi, n, q) == q - 1) return psi;
+    }
+    return 0;
+}
+
+static uint32_t brv(uint32_t x, int bits) {
+    uint32_t r = 0;
+    for (int i = 0; i < bits; i++) {
+        r = (r << 1) | (x & 1);
+        x >>= 1;
+    }
+    return r;
+}
+
+static uint64_t shoup(uint64_t w, uint64_t q) { return (uint64_t)(((u128)w << 64) / q); }
+
+static const double kPi = 3.141592653589793;  // std::f64::consts::PI
+
+// fw[brv(i)] = psi^i, iw[brv(i)] = psi^-i (rns.rs:161-185, ntt.rs:38-65).
+static bool ntt_tables(uint32_t n, uint64_t q, uint64_t* fw, uint64_t* iw) {
+    const int logn = __builtin_ctz(n);
+    const uint64_t psi = find_psi(n, q);
+    if (!psi) return false;
+    const uint64_t psi_inv = powmod(psi, q - 2, q);
+    uint64_t pf = 1, pi = 1;
+    for (uint32_t i = 0; i < n; i++) {
+        const uint32_t r = brv(i, logn);
+        fw[r] = pf;
+        iw[r] = pi;
+        pf = mulmod(pf, psi, q);
+        pi = mulmod(pi, psi_inv, q);
+    }
+    return true;
+}
+
+// FFT tables (encoding.rs:38-80), same expressions and glibc cos/sin.
+static void fft_tables(uint32_t n, double* twist_re, double* twist_im, double* tw_re, double* tw_im) {
+    const int logn = __builtin_ctz(n);
+    for (uint32_t j = 0; j < n; j++) {
+        volatile double angle = kPi * (double)j / (double)n;
+        twist_re[j] = cos(angle);
+        twist_im[j] = sin(angle);
+    }
+    tw_re[0] = tw_im[0] = 0.0;
+    for (int s = 0; s < logn; s++) {
+        const uint32_t half = 1u << s;
+        for (uint32_t k = 0; k < half; k++) {
+            volatile double angle = -2.0 * kPi * (double)k / (double)(2 * half);
+            tw_re[half + k] = cos(angle);
+            tw_im[half + k] = sin(angle);
+        }
+    }
+}
+
+// =====================================================================
+// objects
+// =====================================================================
+struct ts_ctx {
+    std::mutex mu;
+    int device = 0;
+    uint32_t n = 0, slots = 0, L = 0, scale_bits = 40;
+    int logn = 0;
+    uint64_t q[kMaxLimbs] = {};
+    // host copies of the tables (tests / export)
+    std::vector<uint64_t> h_fw, h_iw;  // [L][n]
+    std::vector<double> h_twist_re, h_twist_im, h_tw_re, h_tw_im;
+    // device
+    uint64_t* d_tw = nullptr;  // [L][4][n]
+    LimbTab* d_tabs = nullptr;
+    double* d_fft = nullptr;   // [4][n]
+    unsigned long long* d_stats = nullptr;
+    DevCtx dc{};
+    cudaStream_t own = nullptr, stream = nullptr;
+    // grow-only scratch
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    void* pinned = nullptr;
+    size_t pinned_bytes = 0;
+};
+
+struct ts_sk {
+    ts_ctx* ctx;
+    uint32_t count;
+    uint64_t* d;  // [count][L][n]
+};
+
+struct ts_ct {
+    ts_ctx* ctx;
+    uint32_t count, limbs;
+    double scale;
+    uint64_t* d;  // [count][2][limbs][n]
+};
+
+struct ts_pt {
+    ts_ctx* ctx;
+    uint32_t count;
+    uint64_t* d;  // [count][L][n]
+};
+
+struct ts_lora {
+    ts_ctx* ctx;
+    uint32_t experts, r, d, cols, batches;
+    uint64_t* d_pt;  // [experts][batches][L][n]
+    float* d_b;      // [experts][d][r]
+};
+
+namespace {
+
+struct Lock {
+    std::lock_guard<std::mutex> g;
+    explicit Lock(ts_ctx* c) : g(c->mu) {}
+};
+
+int set_device(ts_ctx* c) {
+    CU(cudaSetDevice(c->device));
+    return TS_OK;
+}
+
+// Carve aligned sub-buffers out of the context's grow-only scratch.
+struct Carve {
+    std::vector<size_t> sizes;
+    size_t add(size_t bytes) {
+        sizes.push_back((bytes + 255) & ~(size_t)255);
+        return sizes.size() - 1;
+    }
+    size_t total() const {
+        size_t t = 0;
+        for (size_t s : sizes) t += s;
+        return t;
+    }
+    template <class T>
+    T* at(void* base, size_t idx) const {
+        size_t off = 0;
+        for (size_t i = 0; i < idx; i++) off += sizes[i];
+        return reinterpret_cast<T*>(static_cast<char*>(base) + off);
+    }
+};
+
+int ensure_scratch(ts_ctx* c, size_t bytes) {
+    if (bytes <= c->scratch_bytes) return TS_OK;
+    if (c->scratch) {
+        CU(cudaFreeAsync(c->scratch, c->stream));
+        c->scratch = nullptr;
+        c->scratch_bytes = 0;
+    }
+    size_t want = bytes + bytes / 4;
+    CU(cudaMallocAsync(&c->scratch, want, c->stream));
+    c->scratch_bytes = want;
+    return TS_OK;
+}
+
+int ensure_pinned(ts_ctx* c, size_t bytes) {
+    if (bytes <= c->pinned_bytes) return TS_OK;
+    if (c->pinned) {
+        CU(cudaStreamSynchronize(c->stream));
+        CU(cudaFreeHost(c->pinned));
+        c->pinned = nullptr;
+        c->pinned_bytes = 0;
+    }
+    CU(cudaMallocHost(&c->pinned, bytes));
+    c->pinned_bytes = bytes;
+    return TS_OK;
+}
+
+int dev_alloc(ts_ctx* c, void** p, size_t bytes) {
+    cudaError_t e = cudaMallocAsync(p, bytes, c->stream);
+    if (e != cudaSuccess) return fail(TS_ERR_OOM, "device allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
+    return TS_OK;
+}
+
+SegList encrypt_segs(uint32_t L) {
+    SegList s{};
+    for (uint32_t l = 0; l < L; l++) {
+        s.kind[s.count] = SEG_UNIFORM;
+        s.limb[s.count] = (int)l;
+        s.count++;
+    }
+    s.kind[s.count++] = SEG_GAUSS;
+    return s;
+}
+
+int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bits, int device, ts_ctx** out) {
+    if (!out) return fail(TS_ERR_ARG, "out is NULL");
+    *out = nullptr;
+    if (n < 1024 || n > 16384 || (n & (n - 1)))
+        return fail(TS_ERR_UNSUPPORTED, "Unsupported poly_mod_degree: %u (this build supports 1024..16384)", n);
+    if (L < 1 || L > (uint32_t)kMaxLimbs) return fail(TS_ERR_ARG, "num_limbs %u out of range [1, %d]", L, kMaxLimbs);
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(TS_ERR_NODEVICE, "no CUDA device");
+    if (device < 0 || device >= ndev) return fail(TS_ERR_ARG, "device %d out of range (%d devices)", device, ndev);
+    ts_ctx* c = new ts_ctx();
+    c->device = device;
+    c->n = n;
+    c->slots = n / 2;
+    c->L = L;
+    c->scale_bits = scale_bits;
+    c->logn = __builtin_ctz(n);
+    const int logn = c->logn;
+    std::vector<LimbTab> tabs(L);
+    std::vector<uint64_t> tw((size_t)L * 4 * n);
+    c->h_fw.assign((size_t)L * n, 0);
+    c->h_iw.assign((size_t)L * n, 0);
+    for (uint32_t l = 0; l < L; l++) {
+        const uint64_t q = moduli[l];
+        if (q < 3 || q >= (1ULL << 62) || q % (2 * n) != 1) {
+            delete c;
+            return fail(TS_ERR_ARG, "modulus %llu is not an NTT-friendly prime below 2^62 for N=%u",
+                        (unsigned long long)q, n);
+        }
+        c->q[l] = q;
+        uint64_t* fw = tw.data() + ((size_t)l * 4 + 0) * n;
+        uint64_t* fws = tw.data() + ((size_t)l * 4 + 1) * n;
+        uint64_t* iw = tw.data() + ((size_t)l * 4 + 2) * n;
+        uint64_t* iws = tw.data() + ((size_t)l * 4 + 3) * n;
+        if (!ntt_tables(n, q, fw, iw)) {
+            delete c;
+            return fail(TS_ERR_ARG, "no primitive 2N-th root for q=%llu", (unsigned long long)q);
+        }
+        for (uint32_t i = 0; i < n; i++) {
+            fws[i] = shoup(fw[i], q);
+            iws[i] = shoup(iw[i], q);
+        }
+        memcpy(c->h_fw.data() + (size_t)l * n, fw, n * 8);
+        memcpy(c->h_iw.data() + (size_t)l * n, iw, n * 8);
+        LimbTab& T = tabs[l];
+        T.q = q;
+        T.ninv = powmod(n, q - 2, q);  // ntt.rs:48
+        T.ninvs = shoup(T.ninv, q);
+        T.iw1n = mulmod(iw[1], T.ninv, q);
+        T.iw1ns = shoup(T.iw1n, q);
+        T.mu64 = UINT64_MAX / q;
+        T.bk = 64 - __builtin_clzll(q);
+        T.bmu = (uint64_t)(((u128)1 << (2 * T.bk)) / q);
+        T.thresh = (uint64_t)(((u128)1 << 64) % q);  // (u64::MAX - q + 1) % q, rng.rs:126
+    }
+    c->h_twist_re.assign(n, 0.0);
+    c->h_twist_im.assign(n, 0.0);
+    c->h_tw_re.assign(n, 0.0);
+    c->h_tw_im.assign(n, 0.0);
+    fft_tables(n, c->h_twist_re.data(), c->h_twist_im.data(), c->h_tw_re.data(), c->h_tw_im.data());
+    // CRT constants (ciphertext.rs:351-356)
+    CrtConst K{};
+    if (L >= 2) {
+        const uint64_t q0 = c->q[0], q1 = c->q[1];
+        K.q0 = q0;
+        K.q1 = q1;
+        K.mu64_1 = tabs[1].mu64;
+        K.bmu1 = tabs[1].bmu;
+        K.bk1 = tabs[1].bk;
+        K.q0inv = powmod(q0 % q1, q1 - 2, q1);
+        const u128 Q = (u128)q0 * q1;
+        const u128 H = Q / 2;
+        K.Q_lo = (uint64_t)Q;
+        K.Q_hi = (uint64_t)(Q >> 64);
+        K.H_lo = (uint64_t)H;
+        K.H_hi = (uint64_t)(H >> 64);
+    } else {
+        K.q0 = c->q[0];
+    }
+    // device upload
+    int rc = TS_OK;
+    do {
+        cudaError_t e = cudaSetDevice(device);
+        if (e != cudaSuccess) { rc = fail(TS_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(e)); break; }
+        // keep freed stream-ordered allocations in the pool for reuse
+        cudaMemPool_t pool;
+        if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+            uint64_t thr = UINT64_MAX;
+            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+        }
+        e = cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking);
+        if (e != cudaSuccess) { rc = fail(TS_ERR_CUDA, "stream: %s", cudaGetErrorString(e)); break; }
+        c->stream = c->own;
+        if (cudaMalloc(&c->d_tw, tw.size() * 8) != cudaSuccess || cudaMalloc(&c->d_tabs, L * sizeof(LimbTab)) != cudaSuccess ||
+            cudaMalloc(&c->d_fft, (size_t)4 * n * sizeof(double)) != cudaSuccess ||
+            cudaMalloc(&c->d_stats, STAT_COUNT * sizeof(unsigned long long)) != cudaSuccess) {
+            rc = fail(TS_ERR_OOM, "table allocation failed");
+            break;
+        }
+        for (uint32_t l = 0; l < L; l++) tabs[l].tw = c->d_tw + (size_t)l * 4 * n;
+        cudaMemcpy(c->d_tw, tw.data(), tw.size() * 8, cudaMemcpyHostToDevice);
+        cudaMemcpy(c->d_tabs, tabs.data(), L * sizeof(LimbTab), cudaMemcpyHostToDevice);
+        cudaMemcpy(c->d_fft, c->h_twist_re.data(), n * 8, cudaMemcpyHostToDevice);
+        cudaMemcpy(c->d_fft + n, c->h_twist_im.data(), n * 8, cudaMemcpyHostToDevice);
+        cudaMemcpy(c->d_fft + 2 * (size_t)n, c->h_tw_re.data(), n * 8, cudaMemcpyHostToDevice);
+        cudaMemcpy(c->d_fft + 3 * (size_t)n, c->h_tw_im.data(), n * 8, cudaMemcpyHostToDevice);
+        cudaMemset(c->d_stats, 0, STAT_COUNT * sizeof(unsigned long long));
+        e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) { rc = fail(TS_ERR_CUDA, "table upload: %s", cudaGetErrorString(e)); break; }
+    } while (0);
+    if (rc != TS_OK) {
+        ts_ctx_destroy(c);
+        return rc;
+    }
+    c->dc.logn = logn;
+    c->dc.n = (int)n;
+    c->dc.L = (int)L;
+    c->dc.tabs = c->d_tabs;
+    c->dc.fft.twist_re = c->d_fft;
+    c->dc.fft.twist_im = c->d_fft + n;
+    c->dc.fft.tw_re = c->d_fft + 2 * (size_t)n;
+    c->dc.fft.tw_im = c->d_fft + 3 * (size_t)n;
+    c->dc.scale = 1099511627776.0;
+    c->dc.crt = K;
+    c->dc.stats = c->d_stats;
+    *out = c;
+    return TS_OK;
+}
+
+// H2D of a row-strided host matrix (rows x len doubles) into dst [rows][len].
+int h2d_rows(ts_ctx* c, double* dst, const double* src, size_t rows, size_t len, size_t stride) {
+    if (rows == 0 || len == 0) return TS_OK;
+    CU(cudaMemcpy2DAsync(dst, len * 8, src, stride * 8, len * 8, rows, cudaMemcpyHostToDevice, c->stream));
+    return TS_OK;
+}
+
+template <class T>
+int h2d_small(ts_ctx* c, T* dst, const T* src, size_t count) {
+    if (count == 0) return TS_OK;
+    CU(cudaMemcpyAsync(dst, src, count * sizeof(T), cudaMemcpyHostToDevice, c->stream));
+    return TS_OK;
+}
+
+int check_stats(ts_ctx* c) {
+    unsigned long long st[STAT_COUNT];
+    CU(cudaMemcpyAsync(st, c->d_stats, sizeof(st), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    if (st[STAT_PLAN_FAIL])
+        return fail(TS_ERR_STATE, "a sampling stream rejected more than %d candidates in one segment", kMaxRej);
+    return TS_OK;
+}
+
+// Core of every secret-key encryption: `count` vectors already on the device
+// (SlotSrc), seeds / key indexes on the device, output ct [count][2][L][n].
+int encrypt_core(ts_ctx* c, const SlotSrc& src, size_t count, const uint64_t* d_seeds, const int* d_skof,
+                 const uint64_t* d_sk, uint64_t* d_ct) {
+    const size_t n = c->n;
+    const size_t CH = 256;  // vectors per pass: bounds the scratch
+    for (size_t v0 = 0; v0 < count; v0 += CH) {
+        const size_t nv = count - v0 < CH ? count - v0 : CH;
+        Carve cv;
+        const size_t i_m = cv.add(nv * n * 8), i_e = cv.add(nv * n), i_f = cv.add(nv * 2 * n * 8),
+                     i_fl = cv.add(nv * 4), i_pl = cv.add(nv * sizeof(StreamPlan));
+        int rc = ensure_scratch(c, cv.total());
+        if (rc) return rc;
+        int64_t* m = cv.at<int64_t>(c->scratch, i_m);
+        int8_t* e = cv.at<int8_t>(c->scratch, i_e);
+        double* f = cv.at<double>(c->scratch, i_f);
+        uint32_t* fl = cv.at<uint32_t>(c->scratch, i_fl);
+        StreamPlan* pl = cv.at<StreamPlan>(c->scratch, i_pl);
+        SlotSrc s = src;
+        s.src = static_cast<const char*>(src.src) + (size_t)v0 * src.stride * (src.is_f32 ? 4 : 8);
+        const uint64_t* seeds = d_seeds + v0;
+        const int* skof = d_skof ? d_skof + v0 : nullptr;
+        uint64_t* ct = d_ct + v0 * 2 * c->L * n;
+        CU(cudaMemsetAsync(fl, 0, nv * 4, c->stream));
+        CU(launch_encode(c->dc, s, (int)nv, m, e, seeds, 2ULL * c->L * n, f, c->stream));
+        CU(launch_encrypt_limbs(c->dc, ct, m, e, d_sk, skof, seeds, (int)nv, fl, pl, false, c->stream));
+        // exact repair of the (rare) streams that met a rejection
+        CU(launch_plan(c->dc, seeds, (int)nv, fl, pl, encrypt_segs(c->L), c->stream));
+        CU(launch_gauss_fix(c->dc, e, seeds, (int)nv, fl, pl, (int)c->L, c->stream));
+        CU(launch_encrypt_limbs(c->dc, ct, m, e, d_sk, skof, seeds, (int)nv, fl, pl, true, c->stream));
+    }
+    return TS_OK;
+}
+
+int new_ct(ts_ctx* c, uint32_t count, uint32_t limbs, double scale, ts_ct** out) {
+    ts_ct* ct = new ts_ct{c, count, limbs, scale, nullptr};
+    int rc = dev_alloc(c, (void**)&ct->d, (size_t)count * 2 * limbs * c->n * 8);
+    if (rc) {
+        delete ct;
+        return rc;
+    }
+    *out = ct;
+    return TS_OK;
+}
+
+}  // namespace
+
+// =====================================================================
+// C ABI
+// =====================================================================
+extern "C" {
+
+const char* ts_last_error(void) { return t_err.c_str(); }
+
+int ts_params_custom(uint32_t poly_degree, const uint32_t* bits, uint32_t L, uint64_t* out) {
+    if (!bits || !out || L == 0) return fail(TS_ERR_ARG, "bad arguments");
+    if (poly_degree == 0 || (poly_degree & (poly_degree - 1))) return fail(TS_ERR_ARG, "poly_degree must be a power of 2");
+    for (uint32_t i = 0; i < L; i++) {
+        if (bits[i] < 2 || bits[i] > 62) return fail(TS_ERR_ARG, "modulus width %u unsupported (2..62)", bits[i]);
+        out[i] = find_ntt_prime(bits[i], 2ULL * poly_degree);
+        if (!out[i]) return fail(TS_ERR_ARG, "No %u-bit NTT-friendly prime found for 2N=%u", bits[i], 2 * poly_degree);
+    }
+    return TS_OK;
+}
+
+int ts_host_tables(uint32_t n, uint64_t q, uint64_t* fw, uint64_t* iw, double* twr, double* twi, double* tr,
+                   double* ti) {
+    if (n < 4 || (n & (n - 1))) return fail(TS_ERR_ARG, "n must be a power of 2 >= 4");
+    if (fw || iw) {
+        std::vector<uint64_t> a(n), b(n);
+        if (!ntt_tables(n, q, a.data(), b.data()))
+            return fail(TS_ERR_ARG, "q=%llu is not NTT-friendly for N=%u", (unsigned long long)q, n);
+        if (fw) memcpy(fw, a.data(), n * 8);
+        if (iw) memcpy(iw, b.data(), n * 8);
+    }
+    if (twr || twi || tr || ti) {
+        std::vector<double> A(n), B(n), Cc(n), D(n);
+        fft_tables(n, A.data(), B.data(), Cc.data(), D.data());
+        if (twr) memcpy(twr, A.data(), n * 8);
+        if (twi) memcpy(twi, B.data(), n * 8);
+        if (tr) memcpy(tr, Cc.data(), n * 8);
+        if (ti) memcpy(ti, D.data(), n * 8);
+    }
+    return TS_OK;
+}
+
+int ts_version(void) { return 10000; }
+
+int ts_device_count(int* out) {
+    if (!out) return fail(TS_ERR_ARG, "out is NULL");
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) n = 0;
+    *out = n;
+    return TS_OK;
+}
+
+int ts_ctx_create(uint32_t poly_mod_degree, int device, ts_ctx** out) {
+    // params.rs:66-126
+    static const uint64_t p8192[4] = {1152921504606830593ULL, 1099511480321ULL, 1099510890497ULL,
+                                      1152921504606601217ULL};
+    static const uint64_t p16384[4] = {1152921504606748673ULL, 1099510054913ULL, 1099508121601ULL,
+                                       1152921504606683137ULL};
+    static const uint64_t p32768[4] = {1152921504606584833ULL, 1099507695617ULL, 1099506515969ULL,
+                                       1152921504598720513ULL};
+    const uint64_t* p = nullptr;
+    switch (poly_mod_degree) {
+        case 8192: p = p8192; break;
+        case 16384: p = p16384; break;
+        case 32768: p = p32768; break;
+        default:
+            return fail(TS_ERR_UNSUPPORTED, "Unsupported poly_mod_degree: %u. Use 8192, 16384, or 32768.",
+                        poly_mod_degree);
+    }
+    return build_ctx(poly_mod_degree, p, 4, 40, device, out);
+}
+
+int ts_ctx_create_custom(uint32_t poly_degree, const uint32_t* modulus_bits, uint32_t num_limbs, uint32_t scale_bits,
+                         int device, ts_ctx** out) {
+    if (!modulus_bits || num_limbs == 0 || num_limbs > (uint32_t)kMaxLimbs)
+        return fail(TS_ERR_ARG, "bad modulus_bits / num_limbs");
+    if (poly_degree == 0 || (poly_degree & (poly_degree - 1))) return fail(TS_ERR_ARG, "poly_degree must be a power of 2");
+    uint64_t q[kMaxLimbs];
+    for (uint32_t i = 0; i < num_limbs; i++) {
+        if (modulus_bits[i] < 2 || modulus_bits[i] > 62)
+            return fail(TS_ERR_ARG, "modulus width %u unsupported (2..62)", modulus_bits[i]);
+        q[i] = find_ntt_prime(modulus_bits[i], 2ULL * poly_degree);
+        if (!q[i])
+            return fail(TS_ERR_ARG, "No %u-bit NTT-friendly prime found for 2N=%u", modulus_bits[i], 2 * poly_degree);
+    }
+    return build_ctx(poly_degree, q, num_limbs, scale_bits, device, out);
+}
+
+int ts_ctx_create_moduli(uint32_t poly_degree, const uint64_t* moduli, uint32_t num_limbs, int device, ts_ctx** out) {
+    if (!moduli) return fail(TS_ERR_ARG, "moduli is NULL");
+    return build_ctx(poly_degree, moduli, num_limbs, 40, device, out);
+}
+
+int ts_ctx_destroy(ts_ctx* c) {
+    if (!c) return TS_OK;
+    cudaSetDevice(c->device);
+    if (c->own) cudaStreamSynchronize(c->own);
+    if (c->stream && c->stream != c->own) cudaStreamSynchronize(c->stream);
+    if (c->scratch) cudaFree(c->scratch);
+    if (c->pinned) cudaFreeHost(c->pinned);
+    cudaFree(c->d_tw);
+    cudaFree(c->d_tabs);
+    cudaFree(c->d_fft);
+    cudaFree(c->d_stats);
+    if (c->own) cudaStreamDestroy(c->own);
+    delete c;
+    return TS_OK;
+}
+
+int ts_ctx_info(const ts_ctx* c, uint32_t* n, uint32_t* slots, uint32_t* L, uint64_t* moduli) {
+    if (!c) return fail(TS_ERR_ARG, "ctx is NULL");
+    if (n) *n = c->n;
+    if (slots) *slots = c->slots;
+    if (L) *L = c->L;
+    if (moduli)
+        for (uint32_t l = 0; l < c->L; l++) moduli[l] = c->q[l];
+    return TS_OK;
+}
+
+int ts_ctx_get_stream(ts_ctx* c, void** s) {
+    if (!c || !s) return fail(TS_ERR_ARG, "NULL argument");
+    *s = (void*)c->stream;
+    return TS_OK;
+}
+
+int ts_ctx_set_stream(ts_ctx* c, void* s) {
+    if (!c) return fail(TS_ERR_ARG, "ctx is NULL");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    CU(cudaStreamSynchronize(c->stream));
+    c->stream = s ? (cudaStream_t)s : c->own;
+    return TS_OK;
+}
+
+int ts_ctx_synchronize(ts_ctx* c) {
+    if (!c) return fail(TS_ERR_ARG, "ctx is NULL");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    return check_stats(c);
+}
+
+int ts_ctx_stats(ts_ctx* c, uint64_t out[4]) {
+    if (!c || !out) return fail(TS_ERR_ARG, "NULL argument");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    unsigned long long st[STAT_COUNT];
+    CU(cudaMemcpyAsync(st, c->d_stats, sizeof(st), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    for (int i = 0; i < 4; i++) out[i] = st[i];
+    return TS_OK;
+}
+
+int ts_ctx_tables(const ts_ctx* c, uint32_t limb, uint64_t* fw, uint64_t* iw, double* twr, double* twi, double* tr,
+                  double* ti) {
+    if (!c || limb >= c->L) return fail(TS_ERR_ARG, "bad ctx / limb");
+    const size_t n = c->n;
+    if (fw) memcpy(fw, c->h_fw.data() + limb * n, n * 8);
+    if (iw) memcpy(iw, c->h_iw.data() + limb * n, n * 8);
+    if (twr) memcpy(twr, c->h_twist_re.data(), n * 8);
+    if (twi) memcpy(twi, c->h_twist_im.data(), n * 8);
+    if (tr) memcpy(tr, c->h_tw_re.data(), n * 8);
+    if (ti) memcpy(ti, c->h_tw_im.data(), n * 8);
+    return TS_OK;
+}
+
+// ------------------------------------------------------------------ keys
+int ts_keygen_batch(ts_ctx* c, const uint64_t* seeds, uint32_t count, ts_sk** out) {
+    if (!c || !seeds || !out || count == 0) return fail(TS_ERR_ARG, "bad arguments to ts_keygen_batch");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    ts_sk* sk = new ts_sk{c, count, nullptr};
+    rc = dev_alloc(c, (void**)&sk->d, (size_t)count * c->L * c->n * 8);
+    if (rc) {
+        delete sk;
+        return rc;
+    }
+    Carve cv;
+    const size_t i_s = cv.add(count * 8), i_f = cv.add(count * 4), i_p = cv.add(count * sizeof(StreamPlan));
+    rc = ensure_scratch(c, cv.total());
+    if (rc) {
+        cudaFreeAsync(sk->d, c->stream);
+        delete sk;
+        return rc;
+    }
+    uint64_t* ds = cv.at<uint64_t>(c->scratch, i_s);
+    uint32_t* fl = cv.at<uint32_t>(c->scratch, i_f);
+    StreamPlan* pl = cv.at<StreamPlan>(c->scratch, i_p);
+    SegList segs{};
+    segs.count = 1;
+    segs.kind[0] = SEG_TERNARY;
+    rc = h2d_small(c, ds, seeds, count);
+    if (!rc) {
+        cudaError_t e = cudaMemsetAsync(fl, 0, count * 4, c->stream);
+        if (e == cudaSuccess) e = launch_keygen(c->dc, sk->d, ds, (int)count, fl, pl, c->stream);
+        if (e == cudaSuccess) e = launch_plan(c->dc, ds, (int)count, fl, pl, segs, c->stream);
+        if (e == cudaSuccess) e = launch_keygen_fix(c->dc, sk->d, ds, (int)count, fl, pl, c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "keygen: %s", cudaGetErrorString(e));
+    }
+    if (rc) {
+        cudaFreeAsync(sk->d, c->stream);
+        delete sk;
+        return rc;
+    }
+    *out = sk;
+    return TS_OK;
+}
+
+int ts_keygen(ts_ctx* c, uint64_t seed, ts_sk** out) { return ts_keygen_batch(c, &seed, 1, out); }
+
+int ts_sk_destroy(ts_sk* sk) {
+    if (!sk) return TS_OK;
+    Lock lk(sk->ctx);
+    cudaSetDevice(sk->ctx->device);
+    cudaFreeAsync(sk->d, sk->ctx->stream);
+    delete sk;
+    return TS_OK;
+}
+
+int ts_sk_count(const ts_sk* sk, uint32_t* count) {
+    if (!sk || !count) return fail(TS_ERR_ARG, "NULL argument");
+    *count = sk->count;
+    return TS_OK;
+}
+
+int ts_sk_export(const ts_sk* sk, uint32_t index, uint64_t* host) {
+    if (!sk || !host || index >= sk->count) return fail(TS_ERR_ARG, "bad sk export arguments");
+    ts_ctx* c = sk->ctx;
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    const size_t words = (size_t)c->L * c->n;
+    CU(cudaMemcpyAsync(host, sk->d + index * words, words * 8, cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    return TS_OK;
+}
+
+// ------------------------------------------------------------------ encrypt
+static int encrypt_impl(ts_ctx* c, const ts_sk* sk, const double* data, size_t count, size_t len, size_t stride,
+                        const uint64_t* seeds, const int32_t* sk_index, int on_device, ts_ct** out) {
+    if (!c || !sk || !out || !seeds || count == 0 || (!data && len)) return fail(TS_ERR_ARG, "bad encrypt arguments");
+    if (sk->ctx != c) return fail(TS_ERR_ARG, "secret key belongs to another context");
+    if (len > c->slots) len = c->slots;  // lib.rs:124-126 pads / truncates
+    if (stride < len) stride = len;
+    if (on_device && !aligned(data, 8)) return fail(TS_ERR_ARG, "device data must be 8-byte aligned");
+    int rc = set_device(c);
+    if (rc) return rc;
+    if (sk_index)
+        for (size_t i = 0; i < count; i++)
+            if (sk_index[i] < 0 || (uint32_t)sk_index[i] >= sk->count) return fail(TS_ERR_ARG, "sk_index out of range");
+    ts_ct* ct = nullptr;
+    rc = new_ct(c, (uint32_t)count, c->L, c->dc.scale, &ct);
+    if (rc) return rc;
+    // inputs to the device (persistent buffer for this call)
+    void* buf = nullptr;
+    const size_t data_bytes = on_device ? 0 : count * (len ? len : 1) * 8;
+    const size_t bytes = data_bytes + count * 8 + count * 4 + 512;
+    rc = dev_alloc(c, &buf, bytes);
+    if (rc) {
+        cudaFreeAsync(ct->d, c->stream);
+        delete ct;
+        return rc;
+    }
+    double* d_data = on_device ? const_cast<double*>(data) : static_cast<double*>(buf);
+    uint64_t* d_seeds = reinterpret_cast<uint64_t*>(static_cast<char*>(buf) + ((data_bytes + 255) & ~(size_t)255));
+    int* d_skof = reinterpret_cast<int*>(d_seeds + count);
+    if (!on_device) rc = h2d_rows(c, d_data, data, count, len, stride);
+    if (!rc) rc = h2d_small(c, d_seeds, seeds, count);
+    if (!rc && sk_index) rc = h2d_small(c, d_skof, (const int*)sk_index, count);
+    SlotSrc src{d_data, 0, (int)len, (long long)(on_device ? stride : len), 0, 0};
+    if (!rc) rc = encrypt_core(c, src, count, d_seeds, sk_index ? d_skof : nullptr, sk->d, ct->d);
+    cudaFreeAsync(buf, c->stream);
+    if (!rc) rc = check_stats(c);
+    if (rc) {
+        cudaFreeAsync(ct->d, c->stream);
+        delete ct;
+        return rc;
+    }
+    *out = ct;
+    return TS_OK;
+}
+
+int ts_encrypt(ts_ctx* c, const ts_sk* sk, const double* data, size_t len, uint64_t seed, ts_ct** out) {
+    if (!c) return fail(TS_ERR_ARG, "ctx is NULL");
+    Lock lk(c);
+    return encrypt_impl(c, sk, data, 1, len, len, &seed, nullptr, 0, out);
+}
+
+int ts_encrypt_batch(ts_ctx* c, const ts_sk* sk, const double* data, size_t count, size_t len, size_t stride,
+                     const uint64_t* seeds, const int32_t* sk_index, int data_on_device, ts_ct** out) {
+    if (!c) return fail(TS_ERR_ARG, "ctx is NULL");
+    Lock lk(c);
+    return encrypt_impl(c, sk, data, count, len, stride, seeds, sk_index, data_on_device, out);
+}
+
+int ts_ct_destroy(ts_ct* ct) {
+    if (!ct) return TS_OK;
+    Lock lk(ct->ctx);
+    cudaSetDevice(ct->ctx->device);
+    cudaFreeAsync(ct->d, ct->ctx->stream);
+    delete ct;
+    return TS_OK;
+}
+
+int ts_ct_info(const ts_ct* ct, uint32_t* count, uint32_t* limbs, double* scale) {
+    if (!ct) return fail(TS_ERR_ARG, "ct is NULL");
+    if (count) *count = ct->count;
+    if (limbs) *limbs = ct->limbs;
+    if (scale) *scale = ct->scale;
+    return TS_OK;
+}
+
+int ts_ct_export(const ts_ct* ct, uint32_t index, uint64_t* c0, uint64_t* c1) {
+    if (!ct || index >= ct->count) return fail(TS_ERR_ARG, "bad ct export arguments");
+    ts_ctx* c = ct->ctx;
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    const size_t words = (size_t)ct->limbs * c->n;
+    const uint64_t* base = ct->d + (size_t)index * 2 * words;
+    if (c0) CU(cudaMemcpyAsync(c0, base, words * 8, cudaMemcpyDeviceToHost, c->stream));
+    if (c1) CU(cudaMemcpyAsync(c1, base + words, words * 8, cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    return TS_OK;
+}
+
+int ts_ct_import(ts_ctx* c, const uint64_t* c0, const uint64_t* c1, uint32_t limbs, double scale, ts_ct** out) {
+    if (!c || !c0 || !c1 || !out || limbs == 0 || limbs > c->L) return fail(TS_ERR_ARG, "bad ct import arguments");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    ts_ct* ct = nullptr;
+    rc = new_ct(c, 1, limbs, scale, &ct);
+    if (rc) return rc;
+    const size_t words = (size_t)limbs * c->n;
+    CU(cudaMemcpyAsync(ct->d, c0, words * 8, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaMemcpyAsync(ct->d + words, c1, words * 8, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    *out = ct;
+    return TS_OK;
+}
+
+int ts_ct_select(ts_ctx* c, const ts_ct* ct, uint32_t index, ts_ct** out) {
+    if (!c || !ct || !out || index >= ct->count) return fail(TS_ERR_ARG, "bad ct select arguments");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    ts_ct* o = nullptr;
+    rc = new_ct(c, 1, ct->limbs, ct->scale, &o);
+    if (rc) return rc;
+    const size_t words = (size_t)2 * ct->limbs * c->n;
+    CU(cudaMemcpyAsync(o->d, ct->d + index * words, words * 8, cudaMemcpyDeviceToDevice, c->stream));
+    *out = o;
+    return TS_OK;
+}
+
+// ------------------------------------------------------------------ decrypt
+static int decrypt_core(ts_ctx* c, const ts_ct* ct, const uint64_t* d_sk, const int* d_skof, double* d_out) {
+    const size_t n = c->n;
+    const bool crt = ct->scale > c->dc.scale * 1.5 && ct->limbs >= 2;  // ciphertext.rs:351
+    const int nl = crt ? 2 : 1;
+    const size_t CH = 256;
+    for (size_t v0 = 0; v0 < ct->count; v0 += CH) {
+        const size_t nv = ct->count - v0 < CH ? ct->count - v0 : CH;
+        Carve cv;
+        const size_t i_M = cv.add(nv * nl * n * 8), i_f = cv.add(nv * 2 * n * 8);
+        int rc = ensure_scratch(c, cv.total());
+        if (rc) return rc;
+        uint64_t* M = cv.at<uint64_t>(c->scratch, i_M);
+        double* f = cv.at<double>(c->scratch, i_f);
+        const long long stride = (long long)2 * ct->limbs * n;
+        CU(launch_decrypt_limbs(c->dc, M, nl, ct->d + v0 * stride, stride, (int)ct->limbs, d_sk,
+                                d_skof ? d_skof + v0 : nullptr, nullptr, nullptr, 1, (int)nv, c->stream));
+        CU(launch_decode(c->dc, M, nl, crt, ct->scale, (int)nv, d_out + v0 * c->slots, nullptr, 0, 0, f, c->stream));
+    }
+    return TS_OK;
+}
+
+int ts_decrypt(ts_ctx* c, const ts_ct* ct, const ts_sk* sk, const int32_t* sk_index, double* out, int out_on_device) {
+    if (!c || !ct || !sk || !out) return fail(TS_ERR_ARG, "bad decrypt arguments");
+    if (ct->ctx != c || sk->ctx != c) return fail(TS_ERR_ARG, "objects belong to another context");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    if (sk_index)
+        for (uint32_t i = 0; i < ct->count; i++)
+            if (sk_index[i] < 0 || (uint32_t)sk_index[i] >= sk->count) return fail(TS_ERR_ARG, "sk_index out of range");
+    const size_t out_bytes = (size_t)ct->count * c->slots * 8;
+    void* buf = nullptr;
+    rc = dev_alloc(c, &buf, (out_on_device ? 0 : out_bytes) + ct->count * 4 + 256);
+    if (rc) return rc;
+    double* d_out = out_on_device ? out : static_cast<double*>(buf);
+    int* d_skof = reinterpret_cast<int*>(static_cast<char*>(buf) + (out_on_device ? 0 : ((out_bytes + 255) & ~(size_t)255)));
+    if (sk_index) rc = h2d_small(c, d_skof, (const int*)sk_index, ct->count);
+    if (!rc) rc = decrypt_core(c, ct, sk->d, sk_index ? d_skof : nullptr, d_out);
+    if (!rc && !out_on_device) {
+        cudaError_t e = cudaMemcpyAsync(out, d_out, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "D2H: %s", cudaGetErrorString(e));
+    }
+    cudaFreeAsync(buf, c->stream);
+    if (!rc) {
+        cudaError_t e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "decrypt: %s", cudaGetErrorString(e));
+    }
+    return rc;
+}
+
+// ------------------------------------------------------------------ ct x pt
+static int encode_ntt_core(ts_ctx* c, const double* d_pts, size_t count, size_t len, size_t stride, uint64_t* d_out) {
+    const size_t n = c->n;
+    const size_t CH = 256;
+    for (size_t v0 = 0; v0 < count; v0 += CH) {
+        const size_t nv = count - v0 < CH ? count - v0 : CH;
+        Carve cv;
+        const size_t i_m = cv.add(nv * n * 8), i_f = cv.add(nv * 2 * n * 8);
+        int rc = ensure_scratch(c, cv.total());
+        if (rc) return rc;
+        int64_t* m = cv.at<int64_t>(c->scratch, i_m);
+        double* f = cv.at<double>(c->scratch, i_f);
+        SlotSrc s{d_pts + v0 * stride, 0, (int)len, (long long)stride, 0, 0};
+        CU(launch_encode(c->dc, s, (int)nv, m, nullptr, nullptr, 0, f, c->stream));
+        CU(launch_ntt_signed(c->dc, d_out + v0 * c->L * n, m, (int)nv, c->stream));
+    }
+    return TS_OK;
+}
+
+int ts_encode_ntt(ts_ctx* c, const double* pts, size_t count, size_t len, size_t stride, int on_device, ts_pt** out) {
+    if (!c || !out || count == 0 || (!pts && len)) return fail(TS_ERR_ARG, "bad encode arguments");
+    if (len > c->slots) return fail(TS_ERR_ARG, "Input length %zu exceeds slot count %u", len, c->slots);
+    if (stride < len) stride = len;
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    ts_pt* pt = new ts_pt{c, (uint32_t)count, nullptr};
+    rc = dev_alloc(c, (void**)&pt->d, count * c->L * c->n * 8);
+    if (rc) {
+        delete pt;
+        return rc;
+    }
+    double* d_in = nullptr;
+    size_t st = stride;
+    if (!on_device) {
+        rc = dev_alloc(c, (void**)&d_in, count * (len ? len : 1) * 8);
+        if (!rc) rc = h2d_rows(c, d_in, pts, count, len, stride);
+        st = len ? len : 1;
+    } else {
+        d_in = const_cast<double*>(pts);
+    }
+    if (!rc) rc = encode_ntt_core(c, d_in, count, len, st, pt->d);
+    if (!on_device && d_in) cudaFreeAsync(d_in, c->stream);
+    if (!rc) {
+        cudaError_t e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "encode: %s", cudaGetErrorString(e));
+    }
+    if (rc) {
+        cudaFreeAsync(pt->d, c->stream);
+        delete pt;
+        return rc;
+    }
+    *out = pt;
+    return TS_OK;
+}
+
+int ts_pt_destroy(ts_pt* pt) {
+    if (!pt) return TS_OK;
+    Lock lk(pt->ctx);
+    cudaSetDevice(pt->ctx->device);
+    cudaFreeAsync(pt->d, pt->ctx->stream);
+    delete pt;
+    return TS_OK;
+}
+
+int ts_pt_export(const ts_pt* pt, uint32_t index, uint64_t* host) {
+    if (!pt || !host || index >= pt->count) return fail(TS_ERR_ARG, "bad pt export arguments");
+    ts_ctx* c = pt->ctx;
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    const size_t words = (size_t)c->L * c->n;
+    CU(cudaMemcpyAsync(host, pt->d + index * words, words * 8, cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    return TS_OK;
+}
+
+static int ct_pt_mul_dev(ts_ctx* c, const ts_ct* ct, const uint64_t* d_pt, ts_ct** out) {
+    ts_ct* o = nullptr;
+    int rc = new_ct(c, ct->count, ct->limbs, ct->scale * ct->scale, &o);  // ciphertext.rs:427
+    if (rc) return rc;
+    cudaError_t e = launch_elementwise(c->dc, o->d, ct->d, d_pt, (long long)ct->count * 2 * ct->limbs,
+                                       (int)ct->limbs, true, EW_MUL, c->stream);
+    if (e != cudaSuccess) {
+        cudaFreeAsync(o->d, c->stream);
+        delete o;
+        return fail(TS_ERR_CUDA, "ct_pt_mul: %s", cudaGetErrorString(e));
+    }
+    *out = o;
+    return TS_OK;
+}
+
+int ts_ct_pt_mul_ntt(ts_ctx* c, const ts_ct* ct, const ts_pt* pt, uint32_t pt_index, ts_ct** out) {
+    if (!c || !ct || !pt || !out || pt_index >= pt->count) return fail(TS_ERR_ARG, "bad ct_pt_mul_ntt arguments");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    return ct_pt_mul_dev(c, ct, pt->d + (size_t)pt_index * c->L * c->n, out);
+}
+
+int ts_ct_pt_mul(ts_ctx* c, const ts_ct* ct, const double* pt, size_t len, ts_ct** out) {
+    if (!c || !ct || !out || (!pt && len)) return fail(TS_ERR_ARG, "bad ct_pt_mul arguments");
+    if (len > c->slots) len = c->slots;  // lib.rs:345-347 pads / truncates
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    void* buf = nullptr;
+    const size_t words = (size_t)c->L * c->n;
+    rc = dev_alloc(c, &buf, words * 8 + (len ? len : 1) * 8 + 256);
+    if (rc) return rc;
+    uint64_t* d_pt = static_cast<uint64_t*>(buf);
+    double* d_in = reinterpret_cast<double*>(d_pt + words);
+    rc = h2d_rows(c, d_in, pt, 1, len, len);
+    if (!rc) rc = encode_ntt_core(c, d_in, 1, len, len ? len : 1, d_pt);
+    if (!rc) rc = ct_pt_mul_dev(c, ct, d_pt, out);
+    cudaFreeAsync(buf, c->stream);
+    if (!rc) {
+        cudaError_t e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "ct_pt_mul: %s", cudaGetErrorString(e));
+    }
+    return rc;
+}
+
+static int ct_addsub(ts_ctx* c, const ts_ct* a, const ts_ct* b, ts_ct** out, bool sub) {
+    if (!c || !a || !b || !out) return fail(TS_ERR_ARG, "bad ct_add/ct_sub arguments");
+    if (std::fabs(a->scale - b->scale) >= 1.0)  // ciphertext.rs:436-441
+        return fail(TS_ERR_SCALE, "Scale mismatch in %s: %g vs %g", sub ? "ct_sub" : "ct_add", a->scale, b->scale);
+    if (a->count != b->count || a->limbs != b->limbs) return fail(TS_ERR_ARG, "ciphertext shapes differ");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    ts_ct* o = nullptr;
+    rc = new_ct(c, a->count, a->limbs, a->scale, &o);
+    if (rc) return rc;
+    cudaError_t e = launch_elementwise(c->dc, o->d, a->d, b->d, (long long)a->count * 2 * a->limbs, (int)a->limbs, false,
+                                       sub ? EW_SUB : EW_ADD, c->stream);
+    if (e != cudaSuccess) {
+        cudaFreeAsync(o->d, c->stream);
+        delete o;
+        return fail(TS_ERR_CUDA, "ct_add: %s", cudaGetErrorString(e));
+    }
+    *out = o;
+    return TS_OK;
+}
+
+int ts_ct_add(ts_ctx* c, const ts_ct* a, const ts_ct* b, ts_ct** out) { return ct_addsub(c, a, b, out, false); }
+int ts_ct_sub(ts_ctx* c, const ts_ct* a, const ts_ct* b, ts_ct** out) { return ct_addsub(c, a, b, out, true); }
+
+// ------------------------------------------------------------------ raw kernels
+int ts_ntt_forward(ts_ctx* c, uint64_t* data, size_t n_polys, uint32_t limb_count, uint32_t limb_offset) {
+    if (!c || !data || limb_count == 0 || limb_offset + limb_count > c->L) return fail(TS_ERR_ARG, "bad NTT arguments");
+    if (!aligned(data, 8)) return fail(TS_ERR_ARG, "data must be 8-byte aligned");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    CU(launch_ntt(c->dc, data, (long long)n_polys * limb_count, (int)limb_count, (int)limb_offset, false, c->stream));
+    return TS_OK;
+}
+
+int ts_ntt_inverse(ts_ctx* c, uint64_t* data, size_t n_polys, uint32_t limb_count, uint32_t limb_offset) {
+    if (!c || !data || limb_count == 0 || limb_offset + limb_count > c->L) return fail(TS_ERR_ARG, "bad NTT arguments");
+    if (!aligned(data, 8)) return fail(TS_ERR_ARG, "data must be 8-byte aligned");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    CU(launch_ntt(c->dc, data, (long long)n_polys * limb_count, (int)limb_count, (int)limb_offset, true, c->stream));
+    return TS_OK;
+}
+
+int ts_hadamard(ts_ctx* c, uint64_t* out, const uint64_t* a, const uint64_t* b, size_t n_polys, uint32_t limb_count,
+                int b_bcast) {
+    if (!c || !out || !a || !b || limb_count == 0 || limb_count > c->L) return fail(TS_ERR_ARG, "bad hadamard arguments");
+    if (!aligned(out, 16) || !aligned(a, 16) || !aligned(b, 16))
+        return fail(TS_ERR_ARG, "hadamard operands must be 16-byte aligned");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    CU(launch_elementwise(c->dc, out, a, b, (long long)n_polys * limb_count, (int)limb_count, b_bcast != 0, EW_MUL,
+                          c->stream));
+    return TS_OK;
+}
+
+// ------------------------------------------------------------------ ZeRo-MOAI
+int ts_lora_load(ts_ctx* c, const float* A, const float* B, uint32_t experts, uint32_t r, uint32_t d, ts_lora** out) {
+    if (!c || !A || !B || !out || experts == 0 || r == 0 || d == 0) return fail(TS_ERR_ARG, "bad lora_load arguments");
+    if (d > c->slots) return fail(TS_ERR_ARG, "d_model %u exceeds slot count %u", d, c->slots);
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    const uint32_t cols = c->slots / d > 0 ? c->slots / d : 1;  // inference_engine.py:1057
+    const uint32_t nb = (r + cols - 1) / cols;                 // :1058
+    // packed plaintext rows (inference_engine.py:1060-1068)
+    std::vector<double> packed((size_t)experts * nb * c->slots, 0.0);
+    for (uint32_t e = 0; e < experts; e++)
+        for (uint32_t b = 0; b < nb; b++) {
+            double* row = packed.data() + ((size_t)e * nb + b) * c->slots;
+            for (uint32_t i = 0; i < cols && b * cols + i < r; i++) {
+                const float* a_row = A + ((size_t)e * r + b * cols + i) * d;
+                for (uint32_t j = 0; j < d; j++) row[(size_t)i * d + j] = (double)a_row[j];
+            }
+        }
+    ts_lora* lo = new ts_lora{c, experts, r, d, cols, nb, nullptr, nullptr};
+    double* d_in = nullptr;
+    rc = dev_alloc(c, (void**)&lo->d_pt, (size_t)experts * nb * c->L * c->n * 8);
+    if (!rc) rc = dev_alloc(c, (void**)&lo->d_b, (size_t)experts * d * r * 4);
+    if (!rc) rc = dev_alloc(c, (void**)&d_in, packed.size() * 8);
+    if (!rc) rc = h2d_small(c, d_in, packed.data(), packed.size());
+    if (!rc) rc = h2d_small(c, lo->d_b, B, (size_t)experts * d * r);
+    if (!rc) rc = encode_ntt_core(c, d_in, (size_t)experts * nb, c->slots, c->slots, lo->d_pt);
+    if (d_in) cudaFreeAsync(d_in, c->stream);
+    if (!rc) {
+        cudaError_t e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "lora_load: %s", cudaGetErrorString(e));
+    }
+    if (rc) {
+        if (lo->d_pt) cudaFreeAsync(lo->d_pt, c->stream);
+        if (lo->d_b) cudaFreeAsync(lo->d_b, c->stream);
+        delete lo;
+        return rc;
+    }
+    *out = lo;
+    return TS_OK;
+}
+
+int ts_lora_destroy(ts_lora* lo) {
+    if (!lo) return TS_OK;
+    Lock lk(lo->ctx);
+    cudaSetDevice(lo->ctx->device);
+    cudaFreeAsync(lo->d_pt, lo->ctx->stream);
+    cudaFreeAsync(lo->d_b, lo->ctx->stream);
+    delete lo;
+    return TS_OK;
+}
+
+int ts_lora_info(const ts_lora* lo, uint32_t* experts, uint32_t* r, uint32_t* d, uint32_t* cols, uint32_t* batches) {
+    if (!lo) return fail(TS_ERR_ARG, "lora is NULL");
+    if (experts) *experts = lo->experts;
+    if (r) *r = lo->r;
+    if (d) *d = lo->d;
+    if (cols) *cols = lo->cols;
+    if (batches) *batches = lo->batches;
+    return TS_OK;
+}
+
+int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const double* h, uint32_t n,
+                        const int32_t* expert, const int32_t* sk_index, const uint64_t* seeds, double* delta,
+                        double* inter, int io_on_device) {
+    if (!c || !sk || !lo || !h || !seeds || !delta || n == 0) return fail(TS_ERR_ARG, "bad lora_delta arguments");
+    if (sk->ctx != c || lo->ctx != c) return fail(TS_ERR_ARG, "objects belong to another context");
+    if (io_on_device && (!aligned(h, 8) || !aligned(delta, 8) || !aligned(inter, 8)))
+        return fail(TS_ERR_ARG, "device buffers must be 8-byte aligned");
+    if (c->L < 2) return fail(TS_ERR_ARG, "the ct x pt decrypt needs at least 2 limbs (CRT)");
+    for (uint32_t i = 0; expert && i < n; i++)
+        if (expert[i] < 0 || (uint32_t)expert[i] >= lo->experts) return fail(TS_ERR_ARG, "expert index out of range");
+    for (uint32_t i = 0; sk_index && i < n; i++)
+        if (sk_index[i] < 0 || (uint32_t)sk_index[i] >= sk->count) return fail(TS_ERR_ARG, "sk_index out of range");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    const size_t N = c->n, L = c->L, d = lo->d, r = lo->r, cols = lo->cols, nb = lo->batches;
+    const size_t CH = 256;
+    const double scale2 = c->dc.scale * c->dc.scale;
+    for (size_t v0 = 0; v0 < n && !rc; v0 += CH) {
+        const size_t nv = n - v0 < CH ? n - v0 : CH;
+        Carve cv;
+        const size_t i_h = cv.add(io_on_device ? 0 : nv * d * 8), i_o = cv.add(io_on_device ? 0 : nv * d * 8),
+                     i_in = cv.add(nv * r * 8), i_s = cv.add(nv * 8), i_ex = cv.add(nv * 4), i_sk = cv.add(nv * 4),
+                     i_ct = cv.add(nv * 2 * L * N * 8), i_m = cv.add(nv * N * 8), i_e = cv.add(nv * N),
+                     i_fe = cv.add(nv * 2 * N * 8), i_fl = cv.add(nv * 4), i_pl = cv.add(nv * sizeof(StreamPlan)),
+                     i_M = cv.add(nv * nb * 2 * N * 8), i_fd = cv.add(nv * nb * 2 * N * 8),
+                     i_sg = cv.add(nv * nb * cols * 8);
+        rc = ensure_scratch(c, cv.total());
+        if (rc) break;
+        void* S = c->scratch;
+        double* dh = io_on_device ? const_cast<double*>(h) + v0 * d : cv.at<double>(S, i_h);
+        double* dout = io_on_device ? delta + v0 * d : cv.at<double>(S, i_o);
+        double* dinter = (io_on_device && inter) ? inter + v0 * r : cv.at<double>(S, i_in);
+        uint64_t* ds = cv.at<uint64_t>(S, i_s);
+        int* dex = cv.at<int>(S, i_ex);
+        int* dsk = cv.at<int>(S, i_sk);
+        uint64_t* ct = cv.at<uint64_t>(S, i_ct);
+        int64_t* m = cv.at<int64_t>(S, i_m);
+        int8_t* e = cv.at<int8_t>(S, i_e);
+        double* fe = cv.at<double>(S, i_fe);
+        uint32_t* fl = cv.at<uint32_t>(S, i_fl);
+        StreamPlan* pl = cv.at<StreamPlan>(S, i_pl);
+        uint64_t* M = cv.at<uint64_t>(S, i_M);
+        double* fd = cv.at<double>(S, i_fd);
+        double* sg = cv.at<double>(S, i_sg);
+        if (!io_on_device) rc = h2d_small(c, dh, h + v0 * d, nv * d);
+        if (!rc) rc = h2d_small(c, ds, seeds + v0, nv);
+        if (!rc && expert) rc = h2d_small(c, dex, (const int*)expert + v0, nv);
+        if (!rc && sk_index) rc = h2d_small(c, dsk, (const int*)sk_index + v0, nv);
+        if (rc) break;
+        // 1. encrypt the cols-fold replicated hidden states (:1267-1272)
+        SlotSrc src{dh, 0, (int)d, (long long)d, (int)d, (int)cols};
+        rc = encrypt_core(c, src, nv, ds, sk_index ? dsk : nullptr, sk->d, ct);
+        if (rc) break;
+        // 2. ct x packed_pt (limbs 0/1) fused with decrypt's c0 + c1*s, INTT (:1311-1315)
+        CU(launch_decrypt_limbs(c->dc, M, 2, ct, (long long)2 * L * N, (int)L, sk->d, sk_index ? dsk : nullptr,
+                                lo->d_pt, expert ? dex : nullptr, (int)nb, (int)(nv * nb), c->stream));
+        // 3. CRT, / Delta^2, canonical embedding, segment sums (:1382-1386)
+        CU(launch_decode(c->dc, M, 2, true, scale2, (int)(nv * nb), nullptr, sg, (int)d, (int)cols, fd, c->stream));
+        CU(launch_gather_inter(sg, dinter, (int)nv, (int)nb, (int)cols, (int)r, c->stream));
+        // 4. delta = B @ intermediate (:1392)
+        CU(launch_bmat(lo->d_b, dinter, dout, (int)nv, (int)d, (int)r, expert ? dex : nullptr, (long long)d * r,
+                       c->stream));
+        if (!io_on_device) {
+            CU(cudaMemcpyAsync(delta + v0 * d, dout, nv * d * 8, cudaMemcpyDeviceToHost, c->stream));
+            if (inter) CU(cudaMemcpyAsync(inter + v0 * r, dinter, nv * r * 8, cudaMemcpyDeviceToHost, c->stream));
+        }
+    }
+    if (rc) return rc;
+    if (!io_on_device) return check_stats(c);
+    return TS_OK;
+}
+
+int ts_dp_noise(ts_ctx* c, double* h, uint32_t n, uint32_t d, double clip, double sigma, const uint64_t* seeds,
+                int on_device) {
+    if (!c || !h || !seeds || n == 0 || d == 0) return fail(TS_ERR_ARG, "bad dp_noise arguments");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    void* buf = nullptr;
+    rc = dev_alloc(c, &buf, (on_device ? 0 : (size_t)n * d * 8) + n * 8 + 256);
+    if (rc) return rc;
+    double* dh = on_device ? h : static_cast<double*>(buf);
+    uint64_t* ds = reinterpret_cast<uint64_t*>(static_cast<char*>(buf) + (on_device ? 0 : (((size_t)n * d * 8 + 255) & ~(size_t)255)));
+    if (!on_device) rc = h2d_small(c, dh, h, (size_t)n * d);
+    if (!rc) rc = h2d_small(c, ds, seeds, n);
+    if (!rc) {
+        cudaError_t e = launch_dp_noise(dh, (int)n, (int)d, clip, sigma, ds, c->stream);
+        if (e == cudaSuccess && !on_device) e = cudaMemcpyAsync(h, dh, (size_t)n * d * 8, cudaMemcpyDeviceToHost, c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "dp_noise: %s", cudaGetErrorString(e));
+    }
+    cudaFreeAsync(buf, c->stream);
+    return rc;
+}
+
+int ts_encrypt_stream(ts_ctx* c, const ts_sk* sk, const double* data, size_t count, size_t len, size_t stride,
+                      uint64_t seed, ts_ct** out) {
+    (void)c; (void)sk; (void)data; (void)count; (void)len; (void)stride; (void)seed; (void)out;
+    return fail(TS_ERR_STATE, "ts_encrypt_stream: not built yet");
+}
+
+}  // extern "C"

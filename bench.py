@@ -1,0 +1,406 @@
+#!/usr/bin/env python
+"""Benchmark: encrypted ZeRo-MOAI LoRA deltas per second on B200.
+
+Workload (C1, batched): CKKS N = 16384 with the reference's 4-prime chain
+[60, 40, 40, 60] (params.rs:88-105), scale 2^40, ternary key (seed 0),
+hidden size d = 1536, LoRA rank r = 16 (cols = 5 rows per plaintext, 4
+plaintext batches), one expert.  A step encrypts `batch` independent hidden
+states (5-fold slot replication), multiplies each by the 4 packed LoRA-A
+plaintexts, decrypts, segment-sums and applies B -- one call of
+ts_lora_delta_batch.  Synthetic data: h ~ N(0,1) (fp32 values), A, B ~
+N(0, 0.02^2), numpy default_rng(0); fresh encryption seeds every step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank holds `batch` hidden states of its own
+users (weak scaling) and rank 0 gathers the decrypted deltas over NCCL.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_POLY, D, R = 16384, 1536, 16
+METRIC = "encrypted LoRA deltas/sec (CKKS N=16384, d=1536, r=16, ZeRo-MOAI)"
+UNIT = "deltas/s"
+C2_PRIMES = [1125899904679937, 1125899903991809, 1125899903827969]
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=2048, help="hidden states per GPU per step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-micro", action="store_true", help="skip the NTT / Hadamard microbenchmarks")
+    return ap.parse_args()
+
+
+def inputs(batch: int, rank: int = 0):
+    rng = np.random.default_rng(0)
+    A = (rng.standard_normal((R, D)) * 0.02).astype(np.float32)
+    B = (rng.standard_normal((D, R)) * 0.02).astype(np.float32)
+    H = np.random.default_rng(1000 + rank).standard_normal((batch, D)).astype(np.float32).astype(np.float64)
+    return H, A, B
+
+
+def workload(batch, world):
+    return {
+        "workload": "C1 batched: encrypt -> 4x ct*pt -> batched decrypt -> segment sums -> B matmul per hidden state",
+        "poly_degree": N_POLY, "limbs": 4, "moduli_bits": [60, 40, 40, 60], "scale_bits": 40,
+        "d": D, "r": R, "cols_per_ct": 5, "pt_batches": 4, "experts": 1,
+        "batch_per_gpu": batch, "global_batch": batch * world,
+        "l2": "flushed between timed steps (256 MiB write); per-step ciphertext working set >> 126 MB L2",
+        "parallelism": ("replicas" if world == 1 else f"users sharded over {world} ranks, NCCL gather of deltas"),
+    }
+
+
+# ----------------------------------------------------------------- helpers
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- CPU legs
+def cpu_deltas(n_deltas: int, threads: int):
+    """Time the oracle restatement (fastest CPU form: cached NTT(pt),
+    ct_pt_mul_ntt) on `threads` host threads; returns (deltas/s, wall s)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as O
+
+    H, A, B = inputs(max(n_deltas, 1))
+    octx = O.Ctx(N_POLY)
+    osk = octx.keygen(0)
+    pc = octx.lora_pack(A)
+
+    def one(i):
+        octx.lora_delta(osk, H[i % len(H)], A, B, enc_seed=10_000 + i, mode=0, pt_cache=pc)
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(one, range(n_deltas)))
+    wall = time.perf_counter() - t0
+    return n_deltas / wall, wall
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_model():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def cpu_baseline_leg(seconds: float = 15.0):
+    threads = cpu_threads()
+    per, _ = cpu_deltas(threads, threads)              # calibration round
+    n = max(threads, int(per * seconds))
+    rate, wall = cpu_deltas(n, threads)
+    return {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} C1 deltas ({wall:.1f} s wall) on {threads} threads of {cpu_model()}; C oracle "
+                      "restating tensafe-he-core, cached NTT(pt) (its fastest form)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = cpu_threads()
+    per_step = threads  # one delta per host thread per step
+    for _ in range(args.warmup):
+        cpu_deltas(per_step, threads)
+    total_wall = 0.0
+    for _ in range(args.steps):
+        _, wall = cpu_deltas(per_step, threads)
+        total_wall += wall
+    value = per_step * args.steps / total_wall
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total_wall / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+        "config": workload(per_step, 1) | {"batch_per_gpu": per_step, "global_batch": per_step},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{per_step} C1 deltas per step on {threads} threads of {cpu_model()} "
+                                   "(C restatement of tensafe-he-core; the Rust crate cannot be built here)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+# ----------------------------------------------------------------- GPU leg
+# Algorithmic HBM bytes per unit of work of each kernel (N = 16384 words of
+# 8 bytes per poly-limb):
+#   enc_a         per (ct, limb):        write c1 (8N)
+#   enc_u         per (ct, limb):        read m (8N) + e (N) + s (8N) + c1 (8N), write c0 (8N) = 33N
+#   decrypt_limb  per (ct, batch, limb): read c0, c1 (16N) + s (8N) + NTT(pt) (8N), write M (8N) = 40N
+#   decode_a      per (ct, batch):       read M (2 x 8N), write 16N = 32N
+#   decode_b      per (ct, batch):       read 16N
+#   encode_a      per ct:                write 16N (+ d*8 read)
+#   encode_b      per ct:                read 16N, write m (8N) + e (N) = 25N
+#   ntt_*         per poly-limb:         read 8N + write 8N = 16N
+def kernel_bytes_per_delta(name: str, L: int = 4, nb: int = 4) -> float:
+    n = N_POLY
+    table = {
+        "enc_a": 8 * n * L,
+        "enc_u": 33 * n * L,
+        "decrypt_limb": 40 * n * nb * 2,
+        "decode_a": 32 * n * nb,
+        "decode_b": 16 * n * nb,
+        "encode_a": 16 * n + D * 8,
+        "encode_b": 25 * n,
+    }
+    return float(table.get(name, 0))
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from provenloop_b200 import _lib, tensafe_he
+    from provenloop_b200.backend import ZeroMoaiLora
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    batch = args.batch
+    H, A, B = inputs(batch, rank)
+
+    ctx = tensafe_he.CkksContext(N_POLY, device=local)
+    # one dedicated stream for the library, the L2 flush and the timing events
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    _lib.check(_lib.lib().ts_ctx_set_stream(ctx.handle, stream.cuda_stream), "set_stream")
+    sk = ctx.keygen(0)
+    lora = ZeroMoaiLora(ctx, A, B)
+    h_dev = torch.from_numpy(H).to(dev)
+    delta_dev = torch.empty((batch, D), dtype=torch.float64, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    gather = None
+    if world > 1 and rank == 0:
+        gather = [torch.empty((batch, D), dtype=torch.float64, device=dev) for _ in range(world)]
+    seed_base = 1 + rank * 1_000_000_000
+
+    def step(i):
+        seeds = np.arange(seed_base + i * batch, seed_base + (i + 1) * batch, dtype=np.uint64)
+        lora.delta_device(sk, h_dev, seeds, delta_dev)
+        if world > 1:
+            dist.gather(delta_dev, gather_list=gather, dst=0)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    # ---- timed region
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = _lib.launch_count()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for k in range(args.steps):
+        flush.zero_()
+        ev[k][0].record(stream)
+        step(args.warmup + k)
+        ev[k][1].record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    launches = _lib.launch_count() - launches0
+    clk = clocks.stop()
+    total_ms = sum(a.elapsed_time(b) for a, b in ev)
+
+    # ---- the same K steps again with every kernel launch bracketed by CUDA
+    # events on the library's stream: per-kernel time for the roofline
+    _lib.profile_reset()
+    _lib.profile_enable(True)
+    for k in range(args.steps):
+        flush.zero_()
+        step(args.warmup + args.steps + k)
+    torch.cuda.synchronize(dev)
+    _lib.profile_enable(False)
+    kern = {}
+    for name in ("encode_a", "encode_b", "enc_a", "enc_u", "plan", "gauss_fix", "enc_a_fix", "enc_u_fix",
+                 "decrypt_limb", "decode_a", "decode_b", "dec_fused", "gather_inter", "bmat"):
+        ms, n = _lib.profile_read(name)
+        if n:
+            kern[name] = (ms, n)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    value = world * batch * args.steps / (max_ms / 1000.0)
+
+    # ---- end to end through the public host API (pinned host buffers)
+    h_pin = torch.from_numpy(H).pin_memory()
+    d_pin = torch.empty((batch, D), dtype=torch.float64).pin_memory()
+    hv, dv = h_pin.numpy(), d_pin.numpy()
+    for i in range(2):
+        lora.delta(sk, hv, np.arange(i * batch, (i + 1) * batch, dtype=np.uint64) + 7, out=dv, want_inter=False)
+    if world > 1:
+        dist.barrier()
+    e2e_ms = 0.0
+    for k in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        seeds = np.arange(seed_base + (100 + k) * batch, seed_base + (101 + k) * batch, dtype=np.uint64)
+        lora.delta(sk, hv, seeds, out=dv, want_inter=False)   # H2D, GPU pipeline, D2H, sync
+        e2e_ms += (time.perf_counter() - t0) * 1000.0
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * batch * args.steps / (float(t.item()) / 1000.0)
+
+    # ---- roofline of the dominant kernel (event-timed inside the timed region)
+    peak, peak_kind = measured_peaks()
+    dom = max(kern, key=lambda k: kern[k][0]) if kern else None
+    roof = None
+    if dom and kernel_bytes_per_delta(dom) > 0:
+        ms, n = kern[dom]
+        total_bytes = kernel_bytes_per_delta(dom) * batch * args.steps
+        achieved = total_bytes / (ms / 1000.0) / 1e9
+        traffic = None
+        try:
+            tr = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
+            if dom in tr:
+                # ncu dram bytes per delta for this kernel, scaled to one launch
+                traffic = tr[dom]["dram_bytes_per_delta"] * batch * args.steps / n
+        except Exception:
+            traffic = None
+        roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
+                "measured" else "fallback 6650 GB/s", "traffic": traffic,
+                "algorithmic_bytes_per_launch": total_bytes / n, "avg_launch_ms": ms / n}
+
+    micro = None
+    if rank == 0 and not args.no_micro:
+        micro = ntt_micro(dev, peak)
+
+    base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        base = cpu_baseline_leg()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+            "config": workload(batch, world),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": batch * D * 8,
+                    "d2h_bytes_per_step": batch * D * 8},
+            "roofline": roof, "cpu_baseline": base, "clocks": clk,
+            "gpu_launches": launches,
+            "kernels_ms_per_step": {k: v[0] / args.steps for k, v in kern.items()},
+        }
+        if micro:
+            line["ntt_c2"] = micro
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def ntt_micro(dev, peak):
+    """C2 microbenchmarks: NTT round trip of 1024 x 3 x N=16384 and 4096
+    pointwise products of 3-limb polys (provenloop_b200.microbench)."""
+    from provenloop_b200 import microbench
+
+    out = microbench.ntt(1024, 10, dev.index, peak)
+    out["hadamard"] = microbench.hadamard(1024, 4, dev.index, peak)
+    return out
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

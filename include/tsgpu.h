@@ -53,6 +53,16 @@ const char* ts_last_error(void);
 int ts_version(void);
 int ts_device_count(int* out);
 
+/* Diagnostics: kernels this library launched in the process so far, and
+ * optional CUDA-event timing of every launch by kernel name ("encrypt_limb",
+ * "decrypt_limb", "ntt_forward", "decode_a", ...). */
+int ts_launch_count(uint64_t* out);
+int ts_profile_enable(int on);
+int ts_profile_reset(void);
+/* Total event-timed ms and launches of `kernel` since the last reset;
+ * TS_ERR_ARG if it was not launched. */
+int ts_profile_read(const char* kernel, double* ms, uint64_t* launches);
+
 /* ------------------------------------------------------------ host-only */
 /* CkksParams::custom prime chain (params.rs:142-193) without a device. */
 int ts_params_custom(uint32_t poly_degree, const uint32_t* modulus_bits, uint32_t num_limbs, uint64_t* moduli_out);
@@ -79,8 +89,11 @@ int ts_ctx_destroy(ts_ctx* ctx);
 int ts_ctx_info(const ts_ctx* ctx, uint32_t* poly_degree, uint32_t* num_slots, uint32_t* num_limbs,
                 uint64_t* moduli);
 int ts_ctx_get_stream(ts_ctx* ctx, void** cuda_stream);
-/* Use an external cudaStream_t (NULL restores the context's own stream). */
+/* Issue all work on an external cudaStream_t from now on (0 is the legacy
+ * default stream); ts_ctx_reset_stream returns to the context's own
+ * non-blocking stream. */
 int ts_ctx_set_stream(ts_ctx* ctx, void* cuda_stream);
+int ts_ctx_reset_stream(ts_ctx* ctx);
 int ts_ctx_synchronize(ts_ctx* ctx);
 /* Device counters: [0] near-tie Gaussian samples, [1] streams repaired after
  * a rejection, [2] plan overflows, [3] reserved. */

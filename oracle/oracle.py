@@ -93,6 +93,9 @@ def lib():
                 "or_find_reject_seed": (C.c_uint64, [U64P, C.c_uint32, C.c_size_t, C.c_uint64, C.c_uint64, C.c_int]),
                 "or_lora_delta": (C.c_int, [C.c_void_p, U64P, F64P, C.c_uint32, F32P, F32P, C.c_uint32,
                                             C.c_uint64, C.c_int, F64P, F64P]),
+                "or_lora_pack": (C.c_int, [C.c_void_p, F32P, C.c_uint32, C.c_uint32, U64P]),
+                "or_lora_delta_cached": (C.c_int, [C.c_void_p, U64P, F64P, C.c_uint32, F32P, F32P, C.c_uint32,
+                                                   C.c_uint64, C.c_int, U64P, F64P, F64P]),
             }
             for name, (res, args) in sig.items():
                 f = getattr(L, name)
@@ -382,8 +385,22 @@ class Ctx:
             raise ValueError("Cannot rescale: only 1 limb left")
         return o0.reshape(nl - 1, self.n), o1.reshape(nl - 1, self.n)
 
-    def lora_delta(self, sk, h, lora_a, lora_b, enc_seed: int, mode: int = 0):
-        """ZeRo-MOAI delta (inference_engine.py:1244-1392). Returns (delta, intermediate)."""
+    def lora_pack(self, lora_a):
+        """NTT(encode(packed A rows)) per batch: [n_batches, L, n]."""
+        A = np.ascontiguousarray(lora_a, dtype=np.float32)
+        r, d = A.shape
+        cols = max(1, self.S // d)
+        nb = -(-r // cols)
+        out = np.zeros((nb, self.L, self.n), np.uint64)
+        if lib().or_lora_pack(self._h, _p(A, F32P), r, d, _p(out, U64P)):
+            raise ValueError("or_lora_pack failed")
+        return out
+
+    def lora_delta(self, sk, h, lora_a, lora_b, enc_seed: int, mode: int = 0, pt_cache=None):
+        """ZeRo-MOAI delta (inference_engine.py:1244-1392). Returns (delta, intermediate).
+
+        mode 0 + pt_cache: cached NTT(pt) (fastest CPU form); mode 0: encode
+        per call; mode 1: as the PyO3 binding invokes it."""
         sk = _u64(sk)
         h = np.ascontiguousarray(h, dtype=np.float64)
         A = np.ascontiguousarray(lora_a, dtype=np.float32)
@@ -391,8 +408,10 @@ class Ctx:
         r, d = A.shape
         delta = np.zeros(d)
         inter = np.zeros(r)
-        rc = lib().or_lora_delta(self._h, _p(sk, U64P), _p(h, F64P), d, _p(A, F32P), _p(B, F32P), r,
-                                 enc_seed, mode, _p(delta, F64P), _p(inter, F64P))
+        pc = None if pt_cache is None else _u64(pt_cache)
+        rc = lib().or_lora_delta_cached(self._h, _p(sk, U64P), _p(h, F64P), d, _p(A, F32P), _p(B, F32P), r,
+                                        enc_seed, mode, None if pc is None else _p(pc, U64P), _p(delta, F64P),
+                                        _p(inter, F64P))
         if rc:
             raise ValueError(f"or_lora_delta rc={rc}")
         return delta, inter

@@ -976,9 +976,43 @@ int or_rescale(const or_ctx *c, const uint64_t *c0, const uint64_t *c1,
 /* ZeRo-MOAI delta: inference_engine.py:1244-1392                           */
 /* ======================================================================== */
 
+int or_lora_delta_cached(const or_ctx *c, const uint64_t *sk_ntt, const double *h,
+                         uint32_t d, const float *lora_a, const float *lora_b, uint32_t r,
+                         uint64_t enc_seed, int mode, const uint64_t *pt_cache, double *delta,
+                         double *intermediate);
+
+/* _precompute_he_cache (inference_engine.py:1037-1074) taken one step
+ * further, as ct_pt_mul_ntt's cached-plaintext fast path intends
+ * (ciphertext.rs:420-429): NTT(encode(packed_pt_b)) for each batch b,
+ * out [n_batches][L][n]. */
+int or_lora_pack(const or_ctx *c, const float *lora_a, uint32_t r, uint32_t d, uint64_t *out) {
+    size_t S = c->num_slots;
+    if (d == 0 || d > S || r == 0) return -1;
+    size_t cols = S / d, nb = (r + cols - 1) / cols;
+    double *pt = (double *)malloc(S * sizeof(double));
+    int rc = 0;
+    for (size_t b = 0; b < nb && !rc; b++) {
+        size_t r0 = b * cols, r1 = r0 + cols < r ? r0 + cols : r;
+        memset(pt, 0, S * sizeof(double));
+        for (size_t i = 0; i < r1 - r0; i++)
+            for (size_t j = 0; j < d; j++) pt[i * d + j] = (double)lora_a[(r0 + i) * d + j];
+        rc = or_encode_to_ntt(c, pt, S, out + b * (size_t)c->num_limbs * c->n);
+    }
+    free(pt);
+    return rc;
+}
+
 int or_lora_delta(const or_ctx *c, const uint64_t *sk_ntt, const double *h,
                   uint32_t d, const float *lora_a, const float *lora_b, uint32_t r,
                   uint64_t enc_seed, int mode, double *delta, double *intermediate) {
+    return or_lora_delta_cached(c, sk_ntt, h, d, lora_a, lora_b, r, enc_seed, mode, NULL, delta,
+                                intermediate);
+}
+
+int or_lora_delta_cached(const or_ctx *c, const uint64_t *sk_ntt, const double *h,
+                         uint32_t d, const float *lora_a, const float *lora_b, uint32_t r,
+                         uint64_t enc_seed, int mode, const uint64_t *pt_cache, double *delta,
+                         double *intermediate) {
     size_t n = c->n, S = c->num_slots;
     uint32_t L = c->num_limbs;
     if (d == 0 || d > S || r == 0) return -1;
@@ -1015,6 +1049,8 @@ int or_lora_delta(const or_ctx *c, const uint64_t *sk_ntt, const double *h,
             for (size_t j = 0; j < d; j++) pt[i * d + j] = (double)lora_a[(r0 + i) * d + j];
         if (mode == 1) {
             rc = or_ct_pt_mul(obj_ctx, c0, c1, L, pt, S, p0, p1); /* :1311 */
+        } else if (pt_cache) {
+            or_ct_pt_mul_ntt(c, c0, c1, L, pt_cache + b * poly, p0, p1);
         } else {
             rc = or_encode_to_ntt(c, pt, S, ptn);
             if (!rc) or_ct_pt_mul_ntt(c, c0, c1, L, ptn, p0, p1);

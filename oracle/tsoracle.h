@@ -166,6 +166,15 @@ int or_lora_delta(const or_ctx *c, const uint64_t *sk_ntt, const double *h,
                   uint32_t d, const float *lora_a, const float *lora_b, uint32_t r,
                   uint64_t enc_seed, int mode, double *delta, double *intermediate);
 
+/* NTT(plaintext) of each packed LoRA-A batch: out [n_batches][L][n]. */
+int or_lora_pack(const or_ctx *c, const float *lora_a, uint32_t r, uint32_t d, uint64_t *out);
+/* or_lora_delta with an optional pt cache from or_lora_pack (mode 0 only):
+ * the fastest CPU form, ct_pt_mul_ntt on cached plaintexts. */
+int or_lora_delta_cached(const or_ctx *c, const uint64_t *sk_ntt, const double *h,
+                         uint32_t d, const float *lora_a, const float *lora_b, uint32_t r,
+                         uint64_t enc_seed, int mode, const uint64_t *pt_cache, double *delta,
+                         double *intermediate);
+
 /* Test helper: first seed in [start, start+count) whose encrypt (kind 0) or
  * keygen (kind 1) stream hits a rejection; UINT64_MAX if none. */
 uint64_t or_find_reject_seed(const uint64_t *moduli, uint32_t L, size_t n, uint64_t start,

@@ -36,6 +36,10 @@ SIGNATURES = {
     "ts_last_error": (C.c_char_p, []),
     "ts_version": (cint, []),
     "ts_device_count": (cint, [P(cint)]),
+    "ts_launch_count": (cint, [P(u64)]),
+    "ts_profile_enable": (cint, [cint]),
+    "ts_profile_reset": (cint, []),
+    "ts_profile_read": (cint, [C.c_char_p, P(f64), P(u64)]),
     "ts_params_custom": (cint, [u32, P(u32), u32, P(u64)]),
     "ts_host_tables": (cint, [u32, u64, P(u64), P(u64), P(f64), P(f64), P(f64), P(f64)]),
     "ts_ctx_create": (cint, [u32, cint, pvp]),
@@ -45,6 +49,7 @@ SIGNATURES = {
     "ts_ctx_info": (cint, [vp, P(u32), P(u32), P(u32), P(u64)]),
     "ts_ctx_get_stream": (cint, [vp, pvp]),
     "ts_ctx_set_stream": (cint, [vp, vp]),
+    "ts_ctx_reset_stream": (cint, [vp]),
     "ts_ctx_synchronize": (cint, [vp]),
     "ts_ctx_stats": (cint, [vp, P(u64)]),
     "ts_ctx_tables": (cint, [vp, u32, P(u64), P(u64), P(f64), P(f64), P(f64), P(f64)]),
@@ -131,3 +136,26 @@ def device_count() -> int:
     n = C.c_int(0)
     check(lib().ts_device_count(C.byref(n)), "ts_device_count")
     return int(n.value)
+
+
+def launch_count() -> int:
+    v = C.c_uint64(0)
+    check(lib().ts_launch_count(C.byref(v)), "ts_launch_count")
+    return int(v.value)
+
+
+def profile_enable(on: bool = True):
+    check(lib().ts_profile_enable(1 if on else 0), "ts_profile_enable")
+
+
+def profile_reset():
+    check(lib().ts_profile_reset(), "ts_profile_reset")
+
+
+def profile_read(kernel: str):
+    """(total_ms, launches) of `kernel` since the last reset, or (0.0, 0)."""
+    ms, n = C.c_double(0.0), C.c_uint64(0)
+    rc = lib().ts_profile_read(kernel.encode(), C.byref(ms), C.byref(n))
+    if rc != TS_OK:
+        return 0.0, 0
+    return float(ms.value), int(n.value)

@@ -113,10 +113,11 @@ class ZeroMoaiLora:
     def handle(self):
         return self._hd._h
 
-    def delta(self, sk, h, seeds, expert=None, sk_index=None):
+    def delta(self, sk, h, seeds, expert=None, sk_index=None, out=None, out_inter=None, want_inter=True):
         """Encrypted deltas for hidden states h [n, d] (host arrays).
 
-        Returns (delta [n, d] f64, intermediate [n, r] f64)."""
+        ``out`` / ``out_inter`` may be preallocated (e.g. pinned) float64
+        arrays.  Returns (delta [n, d] f64, intermediate [n, r] f64 or None)."""
         H = np.ascontiguousarray(np.atleast_2d(np.asarray(h, dtype=np.float64)))
         n = H.shape[0]
         if H.shape[1] != self.d:
@@ -124,11 +125,16 @@ class ZeroMoaiLora:
         s = np.ascontiguousarray(np.broadcast_to(np.asarray(seeds, dtype=np.uint64), (n,)))
         ex = None if expert is None else np.ascontiguousarray(np.broadcast_to(np.asarray(expert, np.int32), (n,)))
         ski = None if sk_index is None else np.ascontiguousarray(np.broadcast_to(np.asarray(sk_index, np.int32), (n,)))
-        delta = np.zeros((n, self.d))
-        inter = np.zeros((n, self.r))
+        delta = np.zeros((n, self.d)) if out is None else out
+        if delta.shape != (n, self.d) or delta.dtype != np.float64 or not delta.flags.c_contiguous:
+            raise ValueError("out must be a C-contiguous float64 array of shape (n, d)")
+        inter = None
+        if want_inter or out_inter is not None:
+            inter = np.zeros((n, self.r)) if out_inter is None else out_inter
         check(lib().ts_lora_delta_batch(self._ctx.handle, sk.handle, self.handle, H.ctypes.data, n,
                                         ptr(ex, C.c_int32), ptr(ski, C.c_int32), ptr(s, C.c_uint64),
-                                        delta.ctypes.data, inter.ctypes.data, 0), "ts_lora_delta_batch")
+                                        delta.ctypes.data, None if inter is None else inter.ctypes.data, 0),
+              "ts_lora_delta_batch")
         return delta, inter
 
     def delta_device(self, sk, h_dev, seeds, delta_dev, expert=None, sk_index=None, inter_dev=None):

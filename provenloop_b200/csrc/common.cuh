@@ -34,6 +34,21 @@ __device__ __forceinline__ uint64_t mul_shoup_lazy(uint64_t a, uint64_t w, uint6
 
 __device__ __forceinline__ uint64_t reduce_2q(uint64_t x, uint64_t q) { return x >= q ? x - q : x; }
 
+// a*w mod q lazily reduced to [0, 4q), for any a < 2^64 (q < 2^62).
+// Shoup's quotient floor(a*wp / 2^64) is estimated from three of the four
+// 32x32 partial products (a1*w1 and the high halves of a1*w0, a0*w1); the
+// dropped terms (a0*w0 and the carry of the middle sum) each add less than
+// one to the exact quotient, so the estimate is low by at most 2 and the
+// remainder a*w - qh*q lies in [0, 4q).
+__device__ __forceinline__ uint64_t mul_shoup4(uint64_t a, uint64_t w, uint64_t wp, uint64_t q) {
+    const uint32_t a0 = (uint32_t)a, a1 = (uint32_t)(a >> 32);
+    const uint32_t w0 = (uint32_t)wp, w1 = (uint32_t)(wp >> 32);
+    uint64_t qh = (uint64_t)a1 * w1;
+    qh += __umulhi(a1, w0);
+    qh += __umulhi(a0, w1);
+    return a * w - qh * q;
+}
+
 // Per-limb constants for Barrett: mu = floor(2^(2k)/q), k = bitlen(q) <= 62.
 struct BarrettConst {
     uint64_t q;

@@ -4,9 +4,13 @@
 // exact integer arithmetic and, for the f64 FFT, the same rounding sequence,
 // so ciphertexts and NTT outputs are bit-identical to the reference's.
 #include <atomic>
+#include <cstring>
+#include <map>
 #include <mutex>
 #include <set>
+#include <string>
 #include <utility>
+#include <vector>
 
 #include "kernels.cuh"
 
@@ -29,6 +33,16 @@ cudaError_t ensure_smem(K* kernel, size_t bytes) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e == cudaSuccess) g_attr_done.insert(key);
     return e;
+}
+
+// Flag list of a batch of `count` streams: flags[0..count) per-stream
+// flags, flags[count] the number of flagged streams, flags[count+1 ..] their
+// indexes (each stream listed once).  Repair kernels walk only the list.
+__device__ __forceinline__ void flag_stream(uint32_t* flags, int count, int v) {
+    if (atomicOr(flags + v, 1u) == 0u) {
+        const uint32_t slot = atomicAdd(flags + count, 1u);
+        flags[count + 1 + slot] = (uint32_t)v;
+    }
 }
 
 // Candidate index of the i-th accepted draw given the ascending list of
@@ -75,7 +89,90 @@ __device__ int block_exclusive_scan(int x, int* total) {
     return res;
 }
 
+std::atomic<uint64_t> g_launches{0};
+std::atomic<bool> g_prof_on{false};
+std::mutex g_prof_mu;
+struct ProfEntry {
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
+    double ms = 0.0;
+    uint64_t launches = 0;
+};
+std::map<std::string, ProfEntry> g_prof;
+std::vector<cudaEvent_t> g_event_pool;
+
+cudaEvent_t pool_event() {
+    if (!g_event_pool.empty()) {
+        cudaEvent_t e = g_event_pool.back();
+        g_event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    return e;
+}
+
+// Counts the kernels launched in its scope and, when profiling is on,
+// brackets them with an event pair on the launch stream.
+struct KScope {
+    const char* name;
+    cudaStream_t s;
+    int kernels;
+    cudaEvent_t a = nullptr, b = nullptr;
+    KScope(const char* n, cudaStream_t st, int k = 1) : name(n), s(st), kernels(k) {
+        if (g_prof_on.load(std::memory_order_relaxed)) {
+            std::lock_guard<std::mutex> g(g_prof_mu);
+            a = pool_event();
+            b = pool_event();
+            cudaEventRecord(a, s);
+        }
+    }
+    ~KScope() {
+        g_launches.fetch_add((uint64_t)kernels, std::memory_order_relaxed);
+        if (a) {
+            cudaEventRecord(b, s);
+            std::lock_guard<std::mutex> g(g_prof_mu);
+            g_prof[name].ev.emplace_back(a, b);
+        }
+    }
+};
+
 }  // namespace
+
+uint64_t launch_count() { return g_launches.load(); }
+
+void prof_enable(bool on) { g_prof_on.store(on); }
+
+void prof_reset() {
+    std::lock_guard<std::mutex> g(g_prof_mu);
+    for (auto& kv : g_prof) {
+        for (auto& pr : kv.second.ev) {
+            cudaEventSynchronize(pr.second);
+            g_event_pool.push_back(pr.first);
+            g_event_pool.push_back(pr.second);
+        }
+    }
+    g_prof.clear();
+}
+
+bool prof_read(const char* name, double* ms, uint64_t* launches) {
+    std::lock_guard<std::mutex> g(g_prof_mu);
+    auto it = g_prof.find(name);
+    if (it == g_prof.end()) return false;
+    ProfEntry& P = it->second;
+    for (auto& pr : P.ev) {
+        float t = 0.f;
+        cudaEventSynchronize(pr.second);
+        cudaEventElapsedTime(&t, pr.first, pr.second);
+        P.ms += t;
+        P.launches += 1;
+        g_event_pool.push_back(pr.first);
+        g_event_pool.push_back(pr.second);
+    }
+    P.ev.clear();
+    *ms = P.ms;
+    *launches = P.launches;
+    return true;
+}
 
 #define TSG_LOGN_SWITCH(logn, ...)                                \
     switch (logn) {                                               \
@@ -107,11 +204,12 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
 
 cudaError_t launch_ntt(const DevCtx& c, uint64_t* data, long long P, int lmod, int l0, bool inverse, cudaStream_t s) {
     if (P <= 0) return cudaSuccess;
-    const size_t smem = (size_t)c.n * 8;
+    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
         auto kern = inverse ? k_ntt<LG, true> : k_ntt<LG, false>;
         cudaError_t e = ensure_smem(kern, smem);
         if (e != cudaSuccess) return e;
+        KScope ks(inverse ? "ntt_inverse" : "ntt_forward", s);
         kern<<<(unsigned)P, NttCfg<LG>::NT, smem, s>>>(data, c.tabs, lmod, l0);
     });
     return cudaGetLastError();
@@ -154,6 +252,7 @@ cudaError_t launch_elementwise(const DevCtx& c, uint64_t* out, const uint64_t* a
     if (total <= 0) return cudaSuccess;
     long long blocks = (total / 2 + 255) / 256;
     if (blocks > 148 * 32) blocks = 148 * 32;
+    KScope ks(op == EW_MUL ? "hadamard" : "add_sub", s);
     k_elementwise<<<(unsigned)blocks, 256, 0, s>>>(out, a, b, total, c.logn, L, b_bcast ? 1 : 0, (int)op, c.tabs);
     return cudaGetLastError();
 }
@@ -172,58 +271,65 @@ __device__ __forceinline__ uint64_t ternary_coeff(uint32_t r, uint64_t q) {
 template <int LOGN>
 __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     k_keygen(uint64_t* __restrict__ sk, const uint64_t* __restrict__ seeds, const LimbTab* __restrict__ tabs, int L,
-             uint32_t* flags, const StreamPlan* __restrict__ plans, int plan_mode) {
+             int nkeys, uint32_t* flags, const StreamPlan* __restrict__ plans, int plan_mode) {
     extern __shared__ __align__(16) uint64_t sm[];
     constexpr int N = 1 << LOGN, NT = NttCfg<LOGN>::NT;
-    const int limb = blockIdx.x, key = blockIdx.y, tid = threadIdx.x;
-    if (plan_mode && flags[key] == 0) return;
+    const int limb = blockIdx.x, tid = threadIdx.x;
     const LimbTab T = tabs[limb];
-    const uint64_t seed = seeds[key];
-    if (!plan_mode) {
-        // word i = sample i; block b holds samples 16b .. 16b+15
-        bool rej = false;
-        for (int b = tid; b < N / 16; b += NT) {
-            uint32_t w[16];
-            chacha_block(seed, (uint32_t)b, w);
+    const int nwork = plan_mode ? (int)flags[nkeys] : 1;
+    for (int it = blockIdx.y; it < (plan_mode ? nwork : (int)blockIdx.y + 1); it += gridDim.y) {
+        const int key = plan_mode ? (int)flags[nkeys + 1 + it] : it;
+        const uint64_t seed = seeds[key];
+        if (!plan_mode) {
+            // word i = sample i; block b holds samples 16b .. 16b+15
+            bool rej = false;
+            for (int b = tid; b < N / 16; b += NT) {
+                uint32_t w[16];
+                chacha_block(seed, (uint32_t)b, w);
 #pragma unroll
-            for (int c = 0; c < 16; c++) {
-                rej |= (w[c] == 0u);  // range_u32(3) threshold is 1 (rng.rs:112)
-                sm[swz(16 * b + c)] = ternary_coeff(w[c], T.q);
+                for (int c = 0; c < 16; c++) {
+                    rej |= (w[c] == 0u);  // range_u32(3) threshold is 1 (rng.rs:112)
+                    sm[pad(16 * b + c)] = ternary_coeff(w[c], T.q);
+                }
+            }
+            if (rej && limb == 0) flag_stream(flags, nkeys, key);
+        } else {
+            const StreamPlan& P = plans[key];
+            for (int i = tid; i < N; i += NT) {
+                const uint32_t ci = cand_index((uint32_t)i, P.rej[0], P.nrej[0]);
+                sm[pad(i)] = ternary_coeff(chacha_word(seed, P.off[0] + ci), T.q);
             }
         }
-        if (rej && limb == 0) atomicOr(flags + key, 1u);
-    } else {
-        const StreamPlan& P = plans[key];
-        for (int i = tid; i < N; i += NT) {
-            const uint32_t ci = cand_index((uint32_t)i, P.rej[0], P.nrej[0]);
-            sm[swz(i)] = ternary_coeff(chacha_word(seed, P.off[0] + ci), T.q);
-        }
+        __syncthreads();
+        uint64_t* out = sk + (((size_t)key * L + limb) << LOGN);
+        ntt_forward_block<LOGN>(
+            sm, T, [&](int j) { return sm[pad(j)]; }, [&](int j, uint64_t x) { out[j] = x; });
+        __syncthreads();
     }
-    __syncthreads();
-    uint64_t* out = sk + (((size_t)key * L + limb) << LOGN);
-    ntt_forward_block<LOGN>(
-        sm, T, [&](int j) { return sm[swz(j)]; }, [&](int j, uint64_t x) { out[j] = x; });
 }
 
 cudaError_t launch_keygen(const DevCtx& c, uint64_t* sk, const uint64_t* seeds, int nkeys, uint32_t* flags,
                           StreamPlan* plans, cudaStream_t s) {
-    const size_t smem = (size_t)c.n * 8;
+    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
         cudaError_t e = ensure_smem(k_keygen<LG>, smem);
         if (e != cudaSuccess) return e;
-        k_keygen<LG><<<dim3(c.L, nkeys), NttCfg<LG>::NT, smem, s>>>(sk, seeds, c.tabs, c.L, flags, plans, 0);
+        KScope ks("keygen", s);
+        k_keygen<LG><<<dim3(c.L, nkeys), NttCfg<LG>::NT, smem, s>>>(sk, seeds, c.tabs, c.L, nkeys, flags, plans, 0);
     });
     return cudaGetLastError();
 }
 
 cudaError_t launch_keygen_fix(const DevCtx& c, uint64_t* sk, const uint64_t* seeds, int nkeys, const uint32_t* flags,
                               const StreamPlan* plans, cudaStream_t s) {
-    const size_t smem = (size_t)c.n * 8;
+    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
         cudaError_t e = ensure_smem(k_keygen<LG>, smem);
         if (e != cudaSuccess) return e;
-        k_keygen<LG><<<dim3(c.L, nkeys), NttCfg<LG>::NT, smem, s>>>(sk, seeds, c.tabs, c.L,
-                                                                      const_cast<uint32_t*>(flags), plans, 1);
+        KScope ks("keygen_fix", s);
+        const int gy = nkeys < 8 ? nkeys : 8;
+        k_keygen<LG><<<dim3(c.L, gy), NttCfg<LG>::NT, smem, s>>>(sk, seeds, c.tabs, c.L, nkeys,
+                                                                   const_cast<uint32_t*>(flags), plans, 1);
     });
     return cudaGetLastError();
 }
@@ -323,7 +429,11 @@ cudaError_t launch_encode(const DevCtx& c, const SlotSrc& src, int nvec, int64_t
         const size_t smem = (size_t)2 * G::BLK * sizeof(double);
         cudaError_t er = ensure_smem(k_encode_a<LG>, smem);
         if (er != cudaSuccess) return er;
-        k_encode_a<LG><<<dim3(G::NB, nvec), 1024, smem, s>>>(src, c.fft, scratch);
+        {
+            KScope ks("encode_a", s);
+            k_encode_a<LG><<<dim3(G::NB, nvec), 1024, smem, s>>>(src, c.fft, scratch);
+        }
+        KScope ks("encode_b", s);
         k_encode_b<LG><<<nvec, 1024, 0, s>>>(scratch, c.fft, m, e, seeds, gauss_off, c.stats);
     });
     return cudaGetLastError();
@@ -346,10 +456,11 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
 
 cudaError_t launch_ntt_signed(const DevCtx& c, uint64_t* out, const int64_t* m, int nvec, cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
-    const size_t smem = (size_t)c.n * 8;
+    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
         cudaError_t e = ensure_smem(k_ntt_signed<LG>, smem);
         if (e != cudaSuccess) return e;
+        KScope ks("ntt_signed", s);
         k_ntt_signed<LG><<<dim3(c.L, nvec), NttCfg<LG>::NT, smem, s>>>(out, m, c.tabs, c.L);
     });
     return cudaGetLastError();
@@ -358,76 +469,104 @@ cudaError_t launch_ntt_signed(const DevCtx& c, uint64_t* out, const int64_t* m, 
 // ======================================================================
 // Encryption per (ciphertext, limb) (ciphertext.rs:167-229)
 // ======================================================================
-// c1 = NTT(a) with a = range_u64(q_l) draws (sampling.rs:62-64); then
-// c0 = NTT(m + e mod q_l) - c1 * s.  NTT(m) + NTT(e) of the reference equals
-// NTT(m + e) exactly (the transform is linear mod q and both are canonical).
-// Stream layout (speculative, no rejection): limb l's candidate i at words
-// 2*l*N + 2i, low word first; the Gaussian block follows at 2*L*N.
+// Two single-transform kernels (each fits in registers):
+//   k_enc_a: c1 = NTT(a), a = range_u64(q_l) draws (sampling.rs:62-64);
+//   k_enc_u: c0 = NTT(m + e mod q_l) - c1 * s.
+// NTT(m) + NTT(e) of the reference equals NTT(m + e) exactly (the transform
+// is linear mod q and both results are canonical).  Stream layout
+// (speculative, no rejection): limb l's candidate i at words 2*l*N + 2i, low
+// word first; the Gaussian block follows at 2*L*N.  In list mode the CTAs
+// walk the flagged streams only, using their exact plans.
 template <int LOGN>
 __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
-    k_encrypt_limb(uint64_t* __restrict__ ct, const int64_t* __restrict__ m, const int8_t* __restrict__ e,
-                   const uint64_t* __restrict__ sk, const int* __restrict__ sk_of, const uint64_t* __restrict__ seeds,
-                   const LimbTab* __restrict__ tabs, int L, uint32_t* flags, const StreamPlan* __restrict__ plans,
-                   int plan_mode) {
+    k_enc_a(uint64_t* __restrict__ ct, const uint64_t* __restrict__ seeds, const LimbTab* __restrict__ tabs, int L,
+            int nvec, uint32_t* flags, const StreamPlan* __restrict__ plans, int plan_mode) {
     extern __shared__ __align__(16) uint64_t sm[];
     constexpr int N = 1 << LOGN, NT = NttCfg<LOGN>::NT;
-    const int limb = blockIdx.x, v = blockIdx.y, tid = threadIdx.x;
-    if (plan_mode && flags[v] == 0) return;
+    const int limb = blockIdx.x, tid = threadIdx.x;
     const LimbTab T = tabs[limb];
-    const uint64_t seed = seeds[v];
-    uint64_t* c0 = ct + (((size_t)v * 2 * L + limb) << LOGN);
-    uint64_t* c1 = ct + (((size_t)v * 2 * L + L + limb) << LOGN);
-    const uint64_t* s = sk + (((size_t)(sk_of ? sk_of[v] : 0) * L + limb) << LOGN);
-    const int64_t* mv = m + ((size_t)v << LOGN);
-    const int8_t* ev = e + ((size_t)v << LOGN);
-
-    if (!plan_mode) {
-        const uint32_t blk0 = (uint32_t)limb * (N / 8);
-        bool rej = false;
-        for (int b = tid; b < N / 8; b += NT) {
-            uint32_t w[16];
-            chacha_block(seed, blk0 + (uint32_t)b, w);
+    const int nwork = plan_mode ? (int)flags[nvec] : 1;
+    for (int it = blockIdx.y; it < (plan_mode ? nwork : (int)blockIdx.y + 1); it += gridDim.y) {
+        const int v = plan_mode ? (int)flags[nvec + 1 + it] : it;
+        const uint64_t seed = seeds[v];
+        uint64_t* c1 = ct + (((size_t)v * 2 * L + L + limb) << LOGN);
+        if (!plan_mode) {
+            const uint32_t blk0 = (uint32_t)limb * (N / 8);
+            bool rej = false;
+            for (int b = tid; b < N / 8; b += NT) {
+                uint32_t w[16];
+                chacha_block(seed, blk0 + (uint32_t)b, w);
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
-                const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
-                rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
-                sm[swz(8 * b + c)] = mod_u64(u, T.q, T.mu64);
+                for (int c = 0; c < 8; c++) {
+                    const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
+                    rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
+                    sm[pad(8 * b + c)] = mod_u64(u, T.q, T.mu64);
+                }
+            }
+            if (rej) flag_stream(flags, nvec, v);
+        } else {
+            const StreamPlan& P = plans[v];
+            for (int i = tid; i < N; i += NT) {
+                const uint32_t ci = cand_index((uint32_t)i, P.rej[limb], P.nrej[limb]);
+                sm[pad(i)] = mod_u64(word64(seed, P.off[limb] + 2ULL * ci), T.q, T.mu64);
             }
         }
-        if (rej) atomicOr(flags + v, 1u);
-    } else {
-        const StreamPlan& P = plans[v];
-        for (int i = tid; i < N; i += NT) {
-            const uint32_t ci = cand_index((uint32_t)i, P.rej[limb], P.nrej[limb]);
-            sm[swz(i)] = mod_u64(word64(seed, P.off[limb] + 2ULL * ci), T.q, T.mu64);
-        }
+        __syncthreads();
+        ntt_forward_block<LOGN>(
+            sm, T, [&](int j) { return sm[pad(j)]; }, [&](int j, uint64_t x) { c1[j] = x; });
+        __syncthreads();
     }
-    __syncthreads();
-    ntt_forward_block<LOGN>(
-        sm, T, [&](int j) { return sm[swz(j)]; }, [&](int j, uint64_t x) { c1[j] = x; });
-    __syncthreads();
-    ntt_forward_block<LOGN>(
-        sm, T,
-        [&](int j) {
-            return add_mod(signed_residue(mv[j], T.q, T.mu64), signed_residue((int64_t)ev[j], T.q, T.mu64), T.q);
-        },
-        [&](int j, uint64_t x) {
-            // same thread wrote c1[j] in the previous transform's last pass
-            const uint64_t as = mul_barrett(c1[j], s[j], T.q, T.bmu, T.bk);
-            c0[j] = sub_mod(x, as, T.q);
-        });
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+    k_enc_u(uint64_t* __restrict__ ct, const int64_t* __restrict__ m, const int8_t* __restrict__ e,
+            const uint64_t* __restrict__ sk, const int* __restrict__ sk_of, const LimbTab* __restrict__ tabs, int L,
+            int nvec, const uint32_t* __restrict__ flags, int list_mode) {
+    extern __shared__ __align__(16) uint64_t sm[];
+    const int limb = blockIdx.x;
+    const LimbTab T = tabs[limb];
+    const int nwork = list_mode ? (int)flags[nvec] : 1;
+    for (int it = blockIdx.y; it < (list_mode ? nwork : (int)blockIdx.y + 1); it += gridDim.y) {
+        const int v = list_mode ? (int)flags[nvec + 1 + it] : it;
+        uint64_t* c0 = ct + (((size_t)v * 2 * L + limb) << LOGN);
+        const uint64_t* c1 = ct + (((size_t)v * 2 * L + L + limb) << LOGN);
+        const uint64_t* s = sk + (((size_t)(sk_of ? sk_of[v] : 0) * L + limb) << LOGN);
+        const int64_t* mv = m + ((size_t)v << LOGN);
+        const int8_t* ev = e + ((size_t)v << LOGN);
+        ntt_forward_block<LOGN>(
+            sm, T,
+            [&](int j) {
+                return add_mod(signed_residue(mv[j], T.q, T.mu64), signed_residue((int64_t)ev[j], T.q, T.mu64),
+                               T.q);
+            },
+            [&](int j, uint64_t x) {
+                const uint64_t as = mul_barrett(c1[j], s[j], T.q, T.bmu, T.bk);
+                c0[j] = sub_mod(x, as, T.q);
+            });
+        __syncthreads();
+    }
 }
 
 cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m, const int8_t* e, const uint64_t* sk,
                                  const int* sk_of, const uint64_t* seeds, int nvec, uint32_t* flags,
                                  const StreamPlan* plans, bool plan_mode, cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
-    const size_t smem = (size_t)c.n * 8;
+    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
-        cudaError_t er = ensure_smem(k_encrypt_limb<LG>, smem);
+        cudaError_t er = ensure_smem(k_enc_a<LG>, smem);
         if (er != cudaSuccess) return er;
-        k_encrypt_limb<LG><<<dim3(c.L, nvec), NttCfg<LG>::NT, smem, s>>>(ct, m, e, sk, sk_of, seeds, c.tabs, c.L,
-                                                                          flags, plans, plan_mode ? 1 : 0);
+        er = ensure_smem(k_enc_u<LG>, smem);
+        if (er != cudaSuccess) return er;
+        const int gy = plan_mode ? (nvec < 16 ? nvec : 16) : nvec;
+        {
+            KScope ks(plan_mode ? "enc_a_fix" : "enc_a", s);
+            k_enc_a<LG><<<dim3(c.L, gy), NttCfg<LG>::NT, smem, s>>>(ct, seeds, c.tabs, c.L, nvec, flags, plans,
+                                                                     plan_mode ? 1 : 0);
+        }
+        KScope ks(plan_mode ? "enc_u_fix" : "enc_u", s);
+        k_enc_u<LG><<<dim3(c.L, gy), NttCfg<LG>::NT, smem, s>>>(ct, m, e, sk, sk_of, c.tabs, c.L, nvec, flags,
+                                                                 plan_mode ? 1 : 0);
     });
     return cudaGetLastError();
 }
@@ -435,11 +574,8 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
 // ======================================================================
 // Exact stream plans for streams that hit a rejection (rng.rs:109-133)
 // ======================================================================
-__global__ void __launch_bounds__(1024, 1)
-    k_plan(const uint64_t* __restrict__ seeds, const uint32_t* __restrict__ flags, StreamPlan* plans, SegList segs,
-           const LimbTab* __restrict__ tabs, int N, unsigned long long* stats) {
-    const int v = blockIdx.x, tid = threadIdx.x;
-    if (flags[v] == 0) return;
+__device__ void plan_one(const uint64_t* __restrict__ seeds, int v, StreamPlan* plans, const SegList& segs,
+                         const LimbTab* __restrict__ tabs, int N, unsigned long long* stats, int tid) {
     __shared__ uint32_t s_nrej;
     __shared__ uint32_t s_rej[kMaxRej + 1];
     __shared__ uint32_t s_overflow;
@@ -518,36 +654,51 @@ __global__ void __launch_bounds__(1024, 1)
             if (s_overflow) atomicAdd(stats + STAT_PLAN_FAIL, 1ULL);
         }
     }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(1024, 1)
+    k_plan(const uint64_t* __restrict__ seeds, int nstreams, const uint32_t* __restrict__ flags, StreamPlan* plans,
+           SegList segs, const LimbTab* __restrict__ tabs, int N, unsigned long long* stats) {
+    const int tid = threadIdx.x;
+    const int nwork = (int)flags[nstreams];
+    for (int it = blockIdx.x; it < nwork; it += gridDim.x) {
+        plan_one(seeds, (int)flags[nstreams + 1 + it], plans, segs, tabs, N, stats, tid);
+    }
 }
 
 cudaError_t launch_plan(const DevCtx& c, const uint64_t* seeds, int nstreams, const uint32_t* flags, StreamPlan* plans,
                         const SegList& segs, cudaStream_t s) {
     if (nstreams <= 0) return cudaSuccess;
-    k_plan<<<nstreams, 1024, 0, s>>>(seeds, flags, plans, segs, c.tabs, c.n, c.stats);
+    KScope ks("plan", s);
+    k_plan<<<nstreams < 32 ? nstreams : 32, 1024, 0, s>>>(seeds, nstreams, flags, plans, segs, c.tabs, c.n, c.stats);
     return cudaGetLastError();
 }
 
-__global__ void k_gauss_fix(int8_t* __restrict__ e, const uint64_t* __restrict__ seeds, int N,
+__global__ void k_gauss_fix(int8_t* __restrict__ e, const uint64_t* __restrict__ seeds, int N, int nvec,
                             const uint32_t* __restrict__ flags, const StreamPlan* __restrict__ plans, int seg,
                             unsigned long long* stats) {
-    const int v = blockIdx.x;
-    if (flags[v] == 0) return;
-    const uint64_t seed = seeds[v];
-    const uint64_t off = plans[v].off[seg];
-    int ties = 0;
-    for (int j = threadIdx.x; j < N; j += blockDim.x) {
-        const uint64_t w = off + 4ULL * j;
-        bool tie;
-        e[(size_t)v * N + j] = (int8_t)gaussian_round(word64(seed, w), word64(seed, w + 2), 3.19, &tie);
-        ties += tie;
+    const int nwork = (int)flags[nvec];
+    for (int it = blockIdx.x; it < nwork; it += gridDim.x) {
+        const int v = (int)flags[nvec + 1 + it];
+        const uint64_t seed = seeds[v];
+        const uint64_t off = plans[v].off[seg];
+        int ties = 0;
+        for (int j = threadIdx.x; j < N; j += blockDim.x) {
+            const uint64_t w = off + 4ULL * j;
+            bool tie;
+            e[(size_t)v * N + j] = (int8_t)gaussian_round(word64(seed, w), word64(seed, w + 2), 3.19, &tie);
+            ties += tie;
+        }
+        if (ties && stats) atomicAdd(stats + STAT_NEAR_TIE, (unsigned long long)ties);
     }
-    if (ties && stats) atomicAdd(stats + STAT_NEAR_TIE, (unsigned long long)ties);
 }
 
 cudaError_t launch_gauss_fix(const DevCtx& c, int8_t* e, const uint64_t* seeds, int nvec, const uint32_t* flags,
                              const StreamPlan* plans, int seg, cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
-    k_gauss_fix<<<nvec, 512, 0, s>>>(e, seeds, c.n, flags, plans, seg, c.stats);
+    KScope ks("gauss_fix", s);
+    k_gauss_fix<<<nvec < 32 ? nvec : 32, 512, 0, s>>>(e, seeds, c.n, nvec, flags, plans, seg, c.stats);
     return cudaGetLastError();
 }
 
@@ -590,10 +741,11 @@ cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uin
                                  int ct_limbs, const uint64_t* sk, const int* sk_of, const uint64_t* pt,
                                  const int* pt_sel, int per_ct, int nvec, cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
-    const size_t smem = (size_t)c.n * 8;
+    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
         cudaError_t er = ensure_smem(k_decrypt_limb<LG>, smem);
         if (er != cudaSuccess) return er;
+        KScope ks("decrypt_limb", s);
         k_decrypt_limb<LG><<<dim3(nl, nvec), NttCfg<LG>::NT, smem, s>>>(M, nl, cts, ct_stride, ct_limbs, sk, sk_of, pt,
                                                                         pt_sel, per_ct, c.tabs, c.L);
     });
@@ -716,10 +868,14 @@ cudaError_t launch_decode(const DevCtx& c, const uint64_t* M, int nl, bool crt, 
         const size_t smem_a = (size_t)2 * G::BLK * sizeof(double);
         er = ensure_smem(k_decode_a<LG>, smem_a);
         if (er != cudaSuccess) return er;
+        {
+        KScope ks("decode_a", s);
         k_decode_a<LG><<<dim3(G::NB, nvec), 1024, smem_a, s>>>(M, nl, crt ? 1 : 0, scale, K, K.q0, c.fft, scratch);
+        }
         const size_t smem_b = seg_out ? (size_t)(G::N / 2) * sizeof(double) : 0;
         er = ensure_smem(k_decode_b<LG>, smem_b);
         if (er != cudaSuccess) return er;
+        KScope ks("decode_b", s);
         k_decode_b<LG><<<nvec, 1024, smem_b, s>>>(scratch, c.fft, out_slots, seg_out, seg_d, seg_cols);
     });
     return cudaGetLastError();
@@ -740,6 +896,7 @@ __global__ void k_gather_inter(const double* __restrict__ seg, double* __restric
 cudaError_t launch_gather_inter(const double* seg, double* inter, int ndelta, int nb, int cols, int r, cudaStream_t s) {
     const long long tot = (long long)ndelta * r;
     if (tot <= 0) return cudaSuccess;
+    KScope ks("gather_inter", s);
     k_gather_inter<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(seg, inter, ndelta, nb, cols, r);
     return cudaGetLastError();
 }
@@ -760,6 +917,7 @@ cudaError_t launch_bmat(const float* B, const double* inter, double* delta, int 
                         long long b_stride, cudaStream_t s) {
     const long long tot = (long long)nvec * d;
     if (tot <= 0) return cudaSuccess;
+    KScope ks("bmat", s);
     k_bmat<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(B, inter, delta, nvec, d, r, b_sel, b_stride);
     return cudaGetLastError();
 }
@@ -813,6 +971,7 @@ __global__ void k_dp_noise(double* __restrict__ h, int d, double clip, double si
 cudaError_t launch_dp_noise(double* h, int nvec, int d, double clip, double sigma, const uint64_t* seeds,
                             cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
+    KScope ks("dp_noise", s);
     k_dp_noise<<<nvec, 256, 0, s>>>(h, d, clip, sigma, seeds);
     return cudaGetLastError();
 }

@@ -71,6 +71,16 @@ struct SlotSrc {
     int rep_cols;
 };
 
+// ---------------------------------------------------------------- profiling
+// Process-wide count of kernels launched by this library, and optional
+// per-kernel CUDA-event timing of every launch (diagnostics for the bench).
+uint64_t launch_count();
+void prof_enable(bool on);
+void prof_reset();
+// Sum of event-timed milliseconds and number of launches of kernel `name`
+// (waits for the recorded events).  Returns false if `name` was not seen.
+bool prof_read(const char* name, double* ms, uint64_t* launches);
+
 // ---------------------------------------------------------------- launchers
 // In-place forward/inverse NTT of P poly-limbs of `data` ([P][n]); the limb of
 // poly-limb p is l0 + p % lmod.
@@ -102,7 +112,9 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
                                  const uint64_t* sk, const int* sk_of, const uint64_t* seeds, int nvec,
                                  uint32_t* flags, const StreamPlan* plans, bool plan_mode, cudaStream_t s);
 
-// Exact plans for flagged streams (one CTA per stream).
+// Flag buffers hold (2*count + 1) uint32: per-stream flags, the number of
+// flagged streams, and their indexes; zero them before the speculative pass.
+// Exact plans for flagged streams (CTAs walk the flagged list).
 cudaError_t launch_plan(const DevCtx& c, const uint64_t* seeds, int nstreams, const uint32_t* flags,
                         StreamPlan* plans, const SegList& segs, cudaStream_t s);
 // Recompute the Gaussian e[v] of flagged streams from plan segment `seg`.

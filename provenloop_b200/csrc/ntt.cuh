@@ -10,16 +10,23 @@
 // canonical outputs, so the results are bit-identical to the reference.
 //
 // B200 layout: the whole poly-limb (N u64, 128 KiB at N = 16384) lives in
-// one CTA's shared memory; N/E threads each own E = 16 (N <= 8192) or 32
-// (N = 16384) values in registers and run radix-16 passes (4 butterfly stages per pass) with one shared-memory
-// exchange between passes.  The shared-memory address of element j is
-// swizzled so that every pass's access pattern is bank-conflict free.
-// Butterflies use Harvey's lazy reduction (values kept in [0, 4q) forward,
-// [0, 2q) inverse) with Shoup twiddle products; N^-1 is folded into the last
-// inverse stage.  The first pass reads through a caller functor (global
-// memory, or shared memory a sampler filled) and the last pass writes through
-// a caller functor, so fused kernels can transform on load and combine on
-// store without extra passes over HBM.
+// one CTA's shared memory, padded to element j -> j + j/16 (136 KiB), which
+// keeps every pass's access pattern bank-conflict free and turns each
+// thread's 2^R addresses into one base plus compile-time offsets.  N/E
+// threads each own E values in registers (E = 32 from N = 8192, else 16) and
+// run radix-2^R passes (R up to log2 E: 5, 5, 4 stages at N = 16384) with one
+// shared-memory exchange between passes.  Global memory is touched only in
+// coalesced order j = tid + k*(N/E): the forward transform reads its input
+// straight into the first pass and stages its bit-reversed output through
+// shared memory; the inverse stages its input and writes its last pass
+// straight out.  Callers supply the element loader and storer, so fused
+// kernels transform on load and combine on store.
+//
+// Butterflies: Harvey-style lazy reduction with Shoup twiddle products whose
+// quotient comes from three 32x32 partial products (remainder in [0, 4q));
+// values stay in [0, 8q) forward and [0, 4q) inverse, which needs q < 2^61
+// (the reference's primes are <= 60 bits).  Each twiddle and its companion
+// are one 16-byte load.  N^-1 is folded into the last inverse stage.
 #pragma once
 #include "common.cuh"
 
@@ -27,7 +34,7 @@ namespace tsg {
 
 // Per-limb device constants (one entry per RNS limb, in global memory).
 struct LimbTab {
-    const uint64_t* tw;  // [4][n]: fw, fw', iw, iw'  (x' = Shoup companion)
+    const uint64_t* tw;  // [2][n][2]: (fw, fw') pairs then (iw, iw') pairs, x' = Shoup companion
     uint64_t q;
     uint64_t ninv, ninvs;  // N^-1 mod q and companion
     uint64_t iw1n, iw1ns;  // iw[1] * N^-1 mod q and companion
@@ -38,232 +45,226 @@ struct LimbTab {
     int pad;
 };
 
-__device__ __forceinline__ int swz(int j) { return j ^ ((((j >> 6) & 3) << 2) | ((j >> 4) & 3)); }
+// Padded shared-memory index of element j.
+__device__ __forceinline__ int pad(int j) { return j + (j >> 4); }
 
-// Geometry of a radix-2^R pass whose smallest butterfly span is TL = 2^TLOG:
-// set sigma = (g, o), g = sigma >> TLOG, o = sigma & (TL-1); its k-th element
-// is j = (g << (TLOG + R)) + o + (k << TLOG).  Thread tid owns sets
-// sigma = tid + NT*u, u < SETS.
-// Values per thread: 16 up to N = 8192, 32 at N = 16384 (512 threads with
-// up to 128 registers each).
 template <int LOGN>
 struct NttCfg {
     static constexpr int N = 1 << LOGN;
-    static constexpr int E = LOGN >= 14 ? 32 : 16;
-    static constexpr int NT = N / E;
+    static constexpr int E = LOGN >= 13 ? 32 : 16;  // values per thread
+    static constexpr int NT = N / E;                // threads per CTA
+    static constexpr int RMAX = E == 32 ? 5 : 4;    // stages per pass
+    static constexpr int SMEM_WORDS = N + N / 16;   // padded poly-limb
+    static constexpr int NPASS = (LOGN + RMAX - 1) / RMAX;
+    // stages of forward pass p: RMAX each, the last pass the remainder
+    __host__ __device__ static constexpr int fwd_r(int p) { return p < NPASS - 1 ? RMAX : LOGN - RMAX * (NPASS - 1); }
+    __host__ __device__ static constexpr int fwd_s0(int p) { return p * RMAX; }
 };
 
+// Geometry of a radix-2^R pass whose smallest butterfly span is 2^TLOG:
+// set sigma = (g, o), g = sigma >> TLOG, o = sigma & (2^TLOG - 1); its k-th
+// element is j = j0 + (k << TLOG) with j0 = (g << (TLOG + R)) + o.  Thread
+// tid owns sets sigma = tid + NT*u, u < SETS.  j0 and k << TLOG occupy
+// disjoint bits, so pad(j0 + (k << TLOG)) = pad(j0) + K + K/16 with
+// K = k << TLOG: one base register plus a compile-time offset.
 template <int LOGN, int R, int TLOG>
 struct Geo {
     static constexpr int N = 1 << LOGN;
     static constexpr int NT = NttCfg<LOGN>::NT;
     static constexpr int SETS = NttCfg<LOGN>::E >> R;
     __device__ __forceinline__ static int sigma(int tid, int u) { return tid + NT * u; }
-    __device__ __forceinline__ static int elem(int sg, int k) {
-        return ((sg >> TLOG) << (TLOG + R)) + (sg & ((1 << TLOG) - 1)) + (k << TLOG);
+    __device__ __forceinline__ static int pbase(int sg) {
+        return pad(((sg >> TLOG) << (TLOG + R)) + (sg & ((1 << TLOG) - 1)));
     }
+    __host__ __device__ static constexpr int koff(int k) { return (k << TLOG) + ((k << TLOG) >> 4); }
 };
 
 template <int LOGN, int R, int TLOG>
 __device__ __forceinline__ void smem_load(const uint64_t* sm, uint64_t* v, int tid) {
     using G = Geo<LOGN, R, TLOG>;
 #pragma unroll
-    for (int u = 0; u < G::SETS; u++)
+    for (int u = 0; u < G::SETS; u++) {
+        const uint64_t* b = sm + G::pbase(G::sigma(tid, u));
 #pragma unroll
-        for (int k = 0; k < (1 << R); k++) v[u * (1 << R) + k] = sm[swz(G::elem(G::sigma(tid, u), k))];
+        for (int k = 0; k < (1 << R); k++) v[u * (1 << R) + k] = b[G::koff(k)];
+    }
 }
 
 template <int LOGN, int R, int TLOG>
 __device__ __forceinline__ void smem_store(uint64_t* sm, const uint64_t* v, int tid) {
     using G = Geo<LOGN, R, TLOG>;
 #pragma unroll
-    for (int u = 0; u < G::SETS; u++)
+    for (int u = 0; u < G::SETS; u++) {
+        uint64_t* b = sm + G::pbase(G::sigma(tid, u));
 #pragma unroll
-        for (int k = 0; k < (1 << R); k++) sm[swz(G::elem(G::sigma(tid, u), k))] = v[u * (1 << R) + k];
+        for (int k = 0; k < (1 << R); k++) b[G::koff(k)] = v[u * (1 << R) + k];
+    }
 }
 
 // One forward CT stage (sub-stage r of a radix-2^R pass starting at stage
 // S0) on the 2^R values x of set-group g.  Template recursion keeps every
 // loop bound a compile-time constant so x stays in registers.
 template <int R, int S0, int r>
-__device__ __forceinline__ void fwd_stage(uint64_t* x, int g, const uint64_t* __restrict__ fw,
-                                          const uint64_t* __restrict__ fws, uint64_t q, uint64_t q2) {
+__device__ __forceinline__ void fwd_stage(uint64_t* x, int g, const ulonglong2* __restrict__ fw, uint64_t q,
+                                          uint64_t q4) {
     constexpr int half = 1 << (R - 1 - r);
 #pragma unroll
     for (int gi = 0; gi < (1 << r); gi++) {
-        const int ti = (1 << (S0 + r)) + (g << r) + gi;
-        const uint64_t w = __ldg(fw + ti), wp = __ldg(fws + ti);
+        const ulonglong2 w = __ldg(fw + (1 << (S0 + r)) + (g << r) + gi);
 #pragma unroll
         for (int kk = 0; kk < half; kk++) {
             const int k = gi * 2 * half + kk;
             uint64_t X = x[k];
-            X = X >= q2 ? X - q2 : X;
-            const uint64_t T = mul_shoup_lazy(x[k + half], w, wp, q);
-            x[k] = X + T;
-            x[k + half] = X - T + q2;
+            X = X >= q4 ? X - q4 : X;                                 // [0, 4q)
+            const uint64_t T = mul_shoup4(x[k + half], w.x, w.y, q);  // [0, 4q)
+            x[k] = X + T;                                             // [0, 8q)
+            x[k + half] = X + q4 - T;                                 // (0, 8q)
         }
     }
-    if constexpr (r + 1 < R) fwd_stage<R, S0, r + 1>(x, g, fw, fws, q, q2);
+    if constexpr (r + 1 < R) fwd_stage<R, S0, r + 1>(x, g, fw, q, q4);
 }
 
-// Forward CT butterflies for stages S0 .. S0+R-1 on the thread's sets.
 template <int LOGN, int R, int S0>
-__device__ __forceinline__ void fwd_compute(uint64_t* v, const uint64_t* __restrict__ fw,
-                                            const uint64_t* __restrict__ fws, uint64_t q, int tid) {
+__device__ __forceinline__ void fwd_compute(uint64_t* v, const ulonglong2* __restrict__ fw, uint64_t q, int tid) {
     constexpr int TLOG = LOGN - S0 - R;
     using G = Geo<LOGN, R, TLOG>;
 #pragma unroll
-    for (int u = 0; u < G::SETS; u++)
-        fwd_stage<R, S0, 0>(v + u * (1 << R), G::sigma(tid, u) >> TLOG, fw, fws, q, 2 * q);
+    for (int u = 0; u < G::SETS; u++) fwd_stage<R, S0, 0>(v + u * (1 << R), G::sigma(tid, u) >> TLOG, fw, q, 4 * q);
 }
 
-// One inverse GS stage (span 2^(TLOG+r)); the stage of span N/2 folds N^-1.
+// One inverse GS stage (span 2^(TLOG+r)) on values in [0, 4q); the stage of
+// span N/2 folds N^-1 into both outputs.
 template <int LOGN, int R, int TLOG, int r>
-__device__ __forceinline__ void inv_stage(uint64_t* x, int g, const uint64_t* __restrict__ iw,
-                                          const uint64_t* __restrict__ iws, const LimbTab& T, uint64_t q2) {
+__device__ __forceinline__ void inv_stage(uint64_t* x, int g, const ulonglong2* __restrict__ iw, const LimbTab& T,
+                                          uint64_t q4) {
     constexpr int span = 1 << r;
     constexpr int m = 1 << (LOGN - TLOG - r - 1);
     constexpr bool last = (TLOG + r == LOGN - 1);
     const uint64_t q = T.q;
 #pragma unroll
     for (int gi = 0; gi < ((1 << R) >> (r + 1)); gi++) {
-        uint64_t w, wp;
+        ulonglong2 w;
         if constexpr (last) {
-            w = T.iw1n;
-            wp = T.iw1ns;
+            w.x = T.iw1n;
+            w.y = T.iw1ns;
         } else {
-            const int ti = m + (g << (R - r - 1)) + gi;
-            w = __ldg(iw + ti);
-            wp = __ldg(iws + ti);
+            w = __ldg(iw + m + (g << (R - r - 1)) + gi);
         }
 #pragma unroll
         for (int kk = 0; kk < span; kk++) {
             const int k = gi * 2 * span + kk;
             const uint64_t X = x[k], Y = x[k + span];
             if constexpr (last) {
-                x[k] = mul_shoup_lazy(X + Y, T.ninv, T.ninvs, q);
+                x[k] = mul_shoup4(X + Y, T.ninv, T.ninvs, q);
             } else {
                 const uint64_t s = X + Y;
-                x[k] = s >= q2 ? s - q2 : s;
+                x[k] = s >= q4 ? s - q4 : s;
             }
-            x[k + span] = mul_shoup_lazy(X - Y + q2, w, wp, q);
+            x[k + span] = mul_shoup4(X + q4 - Y, w.x, w.y, q);
         }
     }
-    if constexpr (r + 1 < R) inv_stage<LOGN, R, TLOG, r + 1>(x, g, iw, iws, T, q2);
+    if constexpr (r + 1 < R) inv_stage<LOGN, R, TLOG, r + 1>(x, g, iw, T, q4);
 }
 
-// Inverse GS butterflies for spans TL .. TL*2^(R-1) (TL = 2^TLOG).
 template <int LOGN, int R, int TLOG>
-__device__ __forceinline__ void inv_compute(uint64_t* v, const uint64_t* __restrict__ iw,
-                                            const uint64_t* __restrict__ iws, const LimbTab& T, int tid) {
+__device__ __forceinline__ void inv_compute(uint64_t* v, const ulonglong2* __restrict__ iw, const LimbTab& T, int tid) {
     using G = Geo<LOGN, R, TLOG>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++)
-        inv_stage<LOGN, R, TLOG, 0>(v + u * (1 << R), G::sigma(tid, u) >> TLOG, iw, iws, T, 2 * T.q);
+        inv_stage<LOGN, R, TLOG, 0>(v + u * (1 << R), G::sigma(tid, u) >> TLOG, iw, T, 4 * T.q);
 }
 
-__device__ __forceinline__ uint64_t canon4(uint64_t x, uint64_t q) {
-    const uint64_t q2 = 2 * q;
-    x = x >= q2 ? x - q2 : x;
+// [0, 8q) -> [0, q)
+__device__ __forceinline__ uint64_t canon8(uint64_t x, uint64_t q) {
+    x = x >= 4 * q ? x - 4 * q : x;
+    x = x >= 2 * q ? x - 2 * q : x;
     return x >= q ? x - q : x;
 }
 
-// Forward transform of one poly-limb.  ld(j) returns canonical element j
-// (any source); st(j, v) receives canonical output element j.  `sm` must
-// hold N u64.  All NttCfg<LOGN>::NT threads of the block must call this.
+// [0, 4q) -> [0, q)
+__device__ __forceinline__ uint64_t canon4(uint64_t x, uint64_t q) {
+    x = x >= 2 * q ? x - 2 * q : x;
+    return x >= q ? x - q : x;
+}
+
+// Forward pass P (stages fwd_s0(P) ..) and the ones after it.  Pass 0's
+// values are already in v; every pass stores its results back to the
+// positions it read (its own sets), so one barrier between passes suffices.
+template <int LOGN, int P>
+__device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulonglong2* fw, uint64_t q, int tid) {
+    using C = NttCfg<LOGN>;
+    constexpr int R = C::fwd_r(P), S0 = C::fwd_s0(P), TLOG = LOGN - S0 - R;
+    if constexpr (P > 0) {
+        __syncthreads();
+        smem_load<LOGN, R, TLOG>(sm, v, tid);
+    }
+    fwd_compute<LOGN, R, S0>(v, fw, q, tid);
+    smem_store<LOGN, R, TLOG>(sm, v, tid);
+    if constexpr (P + 1 < C::NPASS) fwd_passes<LOGN, P + 1>(sm, v, fw, q, tid);
+}
+
+// Forward transform of one poly-limb.  ld(j) returns element j (< 8q, e.g.
+// canonical) for j = tid + k*NT; st(j, v) receives canonical output j in the
+// same coalesced order.  `sm` holds NttCfg<LOGN>::SMEM_WORDS u64.  All NT
+// threads of the block must call this; a caller that reuses `sm` afterwards
+// must __syncthreads() first.  If ld reads `sm`, each thread may only read
+// the positions pad(tid + k*NT) (its own first-pass elements).
 template <int LOGN, class Ld, class St>
 __device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
-    constexpr int N = 1 << LOGN, NT = NttCfg<LOGN>::NT, E = NttCfg<LOGN>::E;
+    using C = NttCfg<LOGN>;
     static_assert(LOGN >= 10 && LOGN <= 14, "single-CTA NTT supports N in [1024, 16384]");
+    static_assert(C::fwd_r(0) == C::RMAX, "the first pass takes RMAX stages");
     const int tid = threadIdx.x;
-    const uint64_t* fw = T.tw;
-    const uint64_t* fws = T.tw + N;
-    uint64_t v[E];
+    const ulonglong2* fw = reinterpret_cast<const ulonglong2*>(T.tw);
+    uint64_t v[C::E];
+    // first pass: one set per thread, elements tid + k*NT
 #pragma unroll
-    for (int u = 0; u < E / 16; u++)
-#pragma unroll
-        for (int k = 0; k < 16; k++) v[u * 16 + k] = ld(tid + NT * u + k * (N / 16));
-    fwd_compute<LOGN, 4, 0>(v, fw, fws, T.q, tid);
-    smem_store<LOGN, 4, LOGN - 4>(sm, v, tid);
+    for (int k = 0; k < C::E; k++) v[k] = ld(tid + k * C::NT);
+    fwd_passes<LOGN, 0>(sm, v, fw, T.q, tid);
     __syncthreads();
-    // pass 2: stages 4..7
-    smem_load<LOGN, 4, LOGN - 8>(sm, v, tid);
-    fwd_compute<LOGN, 4, 4>(v, fw, fws, T.q, tid);
-    constexpr int R3 = (LOGN - 8) < 4 ? (LOGN - 8) : 4;  // stages 8 .. 8+R3-1
-    smem_store<LOGN, 4, LOGN - 8>(sm, v, tid);
-    __syncthreads();
-    smem_load<LOGN, R3, LOGN - 8 - R3>(sm, v, tid);
-    fwd_compute<LOGN, R3, 8>(v, fw, fws, T.q, tid);
-    if constexpr (LOGN - 8 - R3 == 0) {
-        using G = Geo<LOGN, R3, 0>;
 #pragma unroll
-        for (int u = 0; u < G::SETS; u++)
-#pragma unroll
-            for (int k = 0; k < (1 << R3); k++)
-                st(G::elem(G::sigma(tid, u), k), canon4(v[u * (1 << R3) + k], T.q));
-    } else {
-        constexpr int R4 = LOGN - 12;  // 1 or 2
-        smem_store<LOGN, R3, LOGN - 8 - R3>(sm, v, tid);
-        __syncthreads();
-        smem_load<LOGN, R4, 0>(sm, v, tid);
-        fwd_compute<LOGN, R4, 12>(v, fw, fws, T.q, tid);
-        using G = Geo<LOGN, R4, 0>;
-#pragma unroll
-        for (int u = 0; u < G::SETS; u++)
-#pragma unroll
-            for (int k = 0; k < (1 << R4); k++)
-                st(G::elem(G::sigma(tid, u), k), canon4(v[u * (1 << R4) + k], T.q));
+    for (int k = 0; k < C::E; k++) {
+        const int j = tid + k * C::NT;
+        st(j, canon8(sm[pad(j)], T.q));
     }
 }
 
-// Inverse transform (including x N^-1) of one poly-limb; ld returns
-// canonical inputs, st receives canonical outputs.
+// Inverse pass P in GS order (spans 1 .. N/2) mirrors forward pass
+// NPASS-1-P.  Its values are in shared memory on entry; the last pass keeps
+// its results (elements tid + k*NT) in v.
+template <int LOGN, int P>
+__device__ __forceinline__ void inv_passes(uint64_t* sm, uint64_t* v, const ulonglong2* iw, const LimbTab& T, int tid) {
+    using C = NttCfg<LOGN>;
+    constexpr int FP = C::NPASS - 1 - P;
+    constexpr int R = C::fwd_r(FP), TLOG = LOGN - C::fwd_s0(FP) - R;
+    __syncthreads();
+    smem_load<LOGN, R, TLOG>(sm, v, tid);
+    inv_compute<LOGN, R, TLOG>(v, iw, T, tid);
+    if constexpr (P + 1 < C::NPASS) {
+        smem_store<LOGN, R, TLOG>(sm, v, tid);
+        inv_passes<LOGN, P + 1>(sm, v, iw, T, tid);
+    }
+}
+
+// Inverse transform (including x N^-1) of one poly-limb; ld(j) returns
+// element j (< 4q) for j = tid + k*NT, st(j, v) receives canonical output j
+// in the same coalesced order.  A caller that reuses `sm` afterwards must
+// __syncthreads() first.
 template <int LOGN, class Ld, class St>
 __device__ __forceinline__ void ntt_inverse_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
-    constexpr int N = 1 << LOGN, NT = NttCfg<LOGN>::NT, E = NttCfg<LOGN>::E;
+    using C = NttCfg<LOGN>;
     static_assert(LOGN >= 10 && LOGN <= 14, "single-CTA NTT supports N in [1024, 16384]");
     const int tid = threadIdx.x;
-    const uint64_t* iw = T.tw + 2 * N;
-    const uint64_t* iws = T.tw + 3 * N;
-    uint64_t v[E];
-    constexpr int R3 = (LOGN - 8) < 4 ? (LOGN - 8) : 4;
-    if constexpr (LOGN - 8 - R3 == 0) {
-        // passes: (R3, span 1), (4, span 2^R3), (4, span 2^(R3+4))
-        using G = Geo<LOGN, R3, 0>;
+    const ulonglong2* iw = reinterpret_cast<const ulonglong2*>(T.tw) + C::N;
+    uint64_t v[C::E];
 #pragma unroll
-        for (int u = 0; u < G::SETS; u++)
-#pragma unroll
-            for (int k = 0; k < (1 << R3); k++) v[u * (1 << R3) + k] = ld(G::elem(G::sigma(tid, u), k));
-        inv_compute<LOGN, R3, 0>(v, iw, iws, T, tid);
-        smem_store<LOGN, R3, 0>(sm, v, tid);
-    } else {
-        constexpr int R4 = LOGN - 12;
-        using G = Geo<LOGN, R4, 0>;
-#pragma unroll
-        for (int u = 0; u < G::SETS; u++)
-#pragma unroll
-            for (int k = 0; k < (1 << R4); k++) v[u * (1 << R4) + k] = ld(G::elem(G::sigma(tid, u), k));
-        inv_compute<LOGN, R4, 0>(v, iw, iws, T, tid);
-        smem_store<LOGN, R4, 0>(sm, v, tid);
-        __syncthreads();
-        smem_load<LOGN, R3, R4>(sm, v, tid);
-        inv_compute<LOGN, R3, R4>(v, iw, iws, T, tid);
-        smem_store<LOGN, R3, R4>(sm, v, tid);
+    for (int k = 0; k < C::E; k++) {
+        const int j = tid + k * C::NT;
+        sm[pad(j)] = ld(j);
     }
-    __syncthreads();
-    smem_load<LOGN, 4, LOGN - 8>(sm, v, tid);
-    inv_compute<LOGN, 4, LOGN - 8>(v, iw, iws, T, tid);
-    smem_store<LOGN, 4, LOGN - 8>(sm, v, tid);
-    __syncthreads();
-    smem_load<LOGN, 4, LOGN - 4>(sm, v, tid);
-    inv_compute<LOGN, 4, LOGN - 4>(v, iw, iws, T, tid);
+    inv_passes<LOGN, 0>(sm, v, iw, T, tid);
 #pragma unroll
-    for (int u = 0; u < E / 16; u++)
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            const uint64_t x = v[u * 16 + k];
-            st(tid + NT * u + k * (N / 16), x >= T.q ? x - T.q : x);
-        }
+    for (int k = 0; k < C::E; k++) st(tid + k * C::NT, canon4(v[k], T.q));
 }
 
 }  // namespace tsg

@@ -191,6 +191,7 @@ struct ts_ctx {
     size_t scratch_bytes = 0;
     void* pinned = nullptr;
     size_t pinned_bytes = 0;
+    cudaEvent_t pinned_free = nullptr;  // recorded after the last copy out of `pinned`
 };
 
 struct ts_sk {
@@ -264,10 +265,13 @@ int ensure_scratch(ts_ctx* c, size_t bytes) {
     return TS_OK;
 }
 
+// Pinned staging buffer for small per-call inputs; waits until the previous
+// asynchronous copy out of it has executed before it is reused.
 int ensure_pinned(ts_ctx* c, size_t bytes) {
+    if (!c->pinned_free) CU(cudaEventCreateWithFlags(&c->pinned_free, cudaEventDisableTiming));
+    CU(cudaEventSynchronize(c->pinned_free));
     if (bytes <= c->pinned_bytes) return TS_OK;
     if (c->pinned) {
-        CU(cudaStreamSynchronize(c->stream));
         CU(cudaFreeHost(c->pinned));
         c->pinned = nullptr;
         c->pinned_bytes = 0;
@@ -317,31 +321,32 @@ int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bit
     c->h_iw.assign((size_t)L * n, 0);
     for (uint32_t l = 0; l < L; l++) {
         const uint64_t q = moduli[l];
-        if (q < 3 || q >= (1ULL << 62) || q % (2 * n) != 1) {
+        // the lazy NTT keeps values below 8q < 2^64
+        if (q < 3 || q >= (1ULL << 61) || q % (2 * n) != 1) {
             delete c;
-            return fail(TS_ERR_ARG, "modulus %llu is not an NTT-friendly prime below 2^62 for N=%u",
+            return fail(TS_ERR_ARG, "modulus %llu is not an NTT-friendly prime below 2^61 for N=%u",
                         (unsigned long long)q, n);
         }
         c->q[l] = q;
-        uint64_t* fw = tw.data() + ((size_t)l * 4 + 0) * n;
-        uint64_t* fws = tw.data() + ((size_t)l * 4 + 1) * n;
-        uint64_t* iw = tw.data() + ((size_t)l * 4 + 2) * n;
-        uint64_t* iws = tw.data() + ((size_t)l * 4 + 3) * n;
+        uint64_t* fw = c->h_fw.data() + (size_t)l * n;
+        uint64_t* iw = c->h_iw.data() + (size_t)l * n;
         if (!ntt_tables(n, q, fw, iw)) {
             delete c;
             return fail(TS_ERR_ARG, "no primitive 2N-th root for q=%llu", (unsigned long long)q);
         }
+        // device layout per limb: (fw, fw') pairs, then (iw, iw') pairs
+        uint64_t* dst = tw.data() + (size_t)l * 4 * n;
         for (uint32_t i = 0; i < n; i++) {
-            fws[i] = shoup(fw[i], q);
-            iws[i] = shoup(iw[i], q);
+            dst[2 * i] = fw[i];
+            dst[2 * i + 1] = shoup(fw[i], q);
+            dst[2 * (size_t)n + 2 * i] = iw[i];
+            dst[2 * (size_t)n + 2 * i + 1] = shoup(iw[i], q);
         }
-        memcpy(c->h_fw.data() + (size_t)l * n, fw, n * 8);
-        memcpy(c->h_iw.data() + (size_t)l * n, iw, n * 8);
         LimbTab& T = tabs[l];
         T.q = q;
         T.ninv = powmod(n, q - 2, q);  // ntt.rs:48
         T.ninvs = shoup(T.ninv, q);
-        T.iw1n = mulmod(iw[1], T.ninv, q);
+        T.iw1n = mulmod(iw[1], T.ninv, q);  // last inverse stage twiddle with N^-1 folded in
         T.iw1ns = shoup(T.iw1n, q);
         T.mu64 = UINT64_MAX / q;
         T.bk = 64 - __builtin_clzll(q);
@@ -445,36 +450,49 @@ int check_stats(ts_ctx* c) {
     return TS_OK;
 }
 
+// Work buffers of one encryption pass over up to `cap` vectors.
+struct EncWork {
+    int64_t* m;       // [cap][n] rounded coefficients
+    int8_t* e;        // [cap][n] Gaussian error
+    double* f;        // [cap][2][n] FFT scratch
+    uint32_t* fl;     // [cap] rejection flags
+    StreamPlan* pl;   // [cap] exact stream plans
+    size_t cap;
+};
+
+void carve_enc(Carve& cv, size_t cap, size_t n, size_t idx[5]) {
+    idx[0] = cv.add(cap * n * 8);
+    idx[1] = cv.add(cap * n);
+    idx[2] = cv.add(cap * 2 * n * 8);
+    idx[3] = cv.add((2 * cap + 1) * 4);
+    idx[4] = cv.add(cap * sizeof(StreamPlan));
+}
+
+EncWork enc_work(const Carve& cv, void* base, size_t cap, const size_t idx[5]) {
+    return EncWork{cv.at<int64_t>(base, idx[0]), cv.at<int8_t>(base, idx[1]), cv.at<double>(base, idx[2]),
+                   cv.at<uint32_t>(base, idx[3]), cv.at<StreamPlan>(base, idx[4]), cap};
+}
+
 // Core of every secret-key encryption: `count` vectors already on the device
 // (SlotSrc), seeds / key indexes on the device, output ct [count][2][L][n].
+// Uses only the work buffers in `w` (callers own the scratch layout).
 int encrypt_core(ts_ctx* c, const SlotSrc& src, size_t count, const uint64_t* d_seeds, const int* d_skof,
-                 const uint64_t* d_sk, uint64_t* d_ct) {
+                 const uint64_t* d_sk, uint64_t* d_ct, const EncWork& w) {
     const size_t n = c->n;
-    const size_t CH = 256;  // vectors per pass: bounds the scratch
-    for (size_t v0 = 0; v0 < count; v0 += CH) {
-        const size_t nv = count - v0 < CH ? count - v0 : CH;
-        Carve cv;
-        const size_t i_m = cv.add(nv * n * 8), i_e = cv.add(nv * n), i_f = cv.add(nv * 2 * n * 8),
-                     i_fl = cv.add(nv * 4), i_pl = cv.add(nv * sizeof(StreamPlan));
-        int rc = ensure_scratch(c, cv.total());
-        if (rc) return rc;
-        int64_t* m = cv.at<int64_t>(c->scratch, i_m);
-        int8_t* e = cv.at<int8_t>(c->scratch, i_e);
-        double* f = cv.at<double>(c->scratch, i_f);
-        uint32_t* fl = cv.at<uint32_t>(c->scratch, i_fl);
-        StreamPlan* pl = cv.at<StreamPlan>(c->scratch, i_pl);
+    for (size_t v0 = 0; v0 < count; v0 += w.cap) {
+        const size_t nv = count - v0 < w.cap ? count - v0 : w.cap;
         SlotSrc s = src;
         s.src = static_cast<const char*>(src.src) + (size_t)v0 * src.stride * (src.is_f32 ? 4 : 8);
         const uint64_t* seeds = d_seeds + v0;
         const int* skof = d_skof ? d_skof + v0 : nullptr;
         uint64_t* ct = d_ct + v0 * 2 * c->L * n;
-        CU(cudaMemsetAsync(fl, 0, nv * 4, c->stream));
-        CU(launch_encode(c->dc, s, (int)nv, m, e, seeds, 2ULL * c->L * n, f, c->stream));
-        CU(launch_encrypt_limbs(c->dc, ct, m, e, d_sk, skof, seeds, (int)nv, fl, pl, false, c->stream));
+        CU(cudaMemsetAsync(w.fl, 0, (2 * nv + 1) * 4, c->stream));
+        CU(launch_encode(c->dc, s, (int)nv, w.m, w.e, seeds, 2ULL * c->L * n, w.f, c->stream));
+        CU(launch_encrypt_limbs(c->dc, ct, w.m, w.e, d_sk, skof, seeds, (int)nv, w.fl, w.pl, false, c->stream));
         // exact repair of the (rare) streams that met a rejection
-        CU(launch_plan(c->dc, seeds, (int)nv, fl, pl, encrypt_segs(c->L), c->stream));
-        CU(launch_gauss_fix(c->dc, e, seeds, (int)nv, fl, pl, (int)c->L, c->stream));
-        CU(launch_encrypt_limbs(c->dc, ct, m, e, d_sk, skof, seeds, (int)nv, fl, pl, true, c->stream));
+        CU(launch_plan(c->dc, seeds, (int)nv, w.fl, w.pl, encrypt_segs(c->L), c->stream));
+        CU(launch_gauss_fix(c->dc, w.e, seeds, (int)nv, w.fl, w.pl, (int)c->L, c->stream));
+        CU(launch_encrypt_limbs(c->dc, ct, w.m, w.e, d_sk, skof, seeds, (int)nv, w.fl, w.pl, true, c->stream));
     }
     return TS_OK;
 }
@@ -499,11 +517,33 @@ extern "C" {
 
 const char* ts_last_error(void) { return t_err.c_str(); }
 
+int ts_launch_count(uint64_t* out) {
+    if (!out) return fail(TS_ERR_ARG, "out is NULL");
+    *out = launch_count();
+    return TS_OK;
+}
+
+int ts_profile_enable(int on) {
+    prof_enable(on != 0);
+    return TS_OK;
+}
+
+int ts_profile_reset(void) {
+    prof_reset();
+    return TS_OK;
+}
+
+int ts_profile_read(const char* kernel, double* ms, uint64_t* launches) {
+    if (!kernel || !ms || !launches) return fail(TS_ERR_ARG, "NULL argument");
+    if (!prof_read(kernel, ms, launches)) return fail(TS_ERR_ARG, "kernel %s was not profiled", kernel);
+    return TS_OK;
+}
+
 int ts_params_custom(uint32_t poly_degree, const uint32_t* bits, uint32_t L, uint64_t* out) {
     if (!bits || !out || L == 0) return fail(TS_ERR_ARG, "bad arguments");
     if (poly_degree == 0 || (poly_degree & (poly_degree - 1))) return fail(TS_ERR_ARG, "poly_degree must be a power of 2");
     for (uint32_t i = 0; i < L; i++) {
-        if (bits[i] < 2 || bits[i] > 62) return fail(TS_ERR_ARG, "modulus width %u unsupported (2..62)", bits[i]);
+        if (bits[i] < 2 || bits[i] > 61) return fail(TS_ERR_ARG, "modulus width %u unsupported (2..61)", bits[i]);
         out[i] = find_ntt_prime(bits[i], 2ULL * poly_degree);
         if (!out[i]) return fail(TS_ERR_ARG, "No %u-bit NTT-friendly prime found for 2N=%u", bits[i], 2 * poly_degree);
     }
@@ -568,8 +608,8 @@ int ts_ctx_create_custom(uint32_t poly_degree, const uint32_t* modulus_bits, uin
     if (poly_degree == 0 || (poly_degree & (poly_degree - 1))) return fail(TS_ERR_ARG, "poly_degree must be a power of 2");
     uint64_t q[kMaxLimbs];
     for (uint32_t i = 0; i < num_limbs; i++) {
-        if (modulus_bits[i] < 2 || modulus_bits[i] > 62)
-            return fail(TS_ERR_ARG, "modulus width %u unsupported (2..62)", modulus_bits[i]);
+        if (modulus_bits[i] < 2 || modulus_bits[i] > 61)
+            return fail(TS_ERR_ARG, "modulus width %u unsupported (2..61)", modulus_bits[i]);
         q[i] = find_ntt_prime(modulus_bits[i], 2ULL * poly_degree);
         if (!q[i])
             return fail(TS_ERR_ARG, "No %u-bit NTT-friendly prime found for 2N=%u", modulus_bits[i], 2 * poly_degree);
@@ -589,6 +629,7 @@ int ts_ctx_destroy(ts_ctx* c) {
     if (c->stream && c->stream != c->own) cudaStreamSynchronize(c->stream);
     if (c->scratch) cudaFree(c->scratch);
     if (c->pinned) cudaFreeHost(c->pinned);
+    if (c->pinned_free) cudaEventDestroy(c->pinned_free);
     cudaFree(c->d_tw);
     cudaFree(c->d_tabs);
     cudaFree(c->d_fft);
@@ -620,7 +661,17 @@ int ts_ctx_set_stream(ts_ctx* c, void* s) {
     int rc = set_device(c);
     if (rc) return rc;
     CU(cudaStreamSynchronize(c->stream));
-    c->stream = s ? (cudaStream_t)s : c->own;
+    c->stream = (cudaStream_t)s;  // 0 is the legacy default stream
+    return TS_OK;
+}
+
+int ts_ctx_reset_stream(ts_ctx* c) {
+    if (!c) return fail(TS_ERR_ARG, "ctx is NULL");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    CU(cudaStreamSynchronize(c->stream));
+    c->stream = c->own;
     return TS_OK;
 }
 
@@ -670,7 +721,8 @@ int ts_keygen_batch(ts_ctx* c, const uint64_t* seeds, uint32_t count, ts_sk** ou
         return rc;
     }
     Carve cv;
-    const size_t i_s = cv.add(count * 8), i_f = cv.add(count * 4), i_p = cv.add(count * sizeof(StreamPlan));
+    const size_t i_s = cv.add(count * 8), i_f = cv.add((2 * (size_t)count + 1) * 4),
+                 i_p = cv.add(count * sizeof(StreamPlan));
     rc = ensure_scratch(c, cv.total());
     if (rc) {
         cudaFreeAsync(sk->d, c->stream);
@@ -685,7 +737,7 @@ int ts_keygen_batch(ts_ctx* c, const uint64_t* seeds, uint32_t count, ts_sk** ou
     segs.kind[0] = SEG_TERNARY;
     rc = h2d_small(c, ds, seeds, count);
     if (!rc) {
-        cudaError_t e = cudaMemsetAsync(fl, 0, count * 4, c->stream);
+        cudaError_t e = cudaMemsetAsync(fl, 0, (2 * (size_t)count + 1) * 4, c->stream);
         if (e == cudaSuccess) e = launch_keygen(c->dc, sk->d, ds, (int)count, fl, pl, c->stream);
         if (e == cudaSuccess) e = launch_plan(c->dc, ds, (int)count, fl, pl, segs, c->stream);
         if (e == cudaSuccess) e = launch_keygen_fix(c->dc, sk->d, ds, (int)count, fl, pl, c->stream);
@@ -763,7 +815,15 @@ static int encrypt_impl(ts_ctx* c, const ts_sk* sk, const double* data, size_t c
     if (!rc) rc = h2d_small(c, d_seeds, seeds, count);
     if (!rc && sk_index) rc = h2d_small(c, d_skof, (const int*)sk_index, count);
     SlotSrc src{d_data, 0, (int)len, (long long)(on_device ? stride : len), 0, 0};
-    if (!rc) rc = encrypt_core(c, src, count, d_seeds, sk_index ? d_skof : nullptr, sk->d, ct->d);
+    if (!rc) {
+        const size_t cap = count < 256 ? count : 256;
+        Carve cv;
+        size_t idx[5];
+        carve_enc(cv, cap, c->n, idx);
+        rc = ensure_scratch(c, cv.total());
+        if (!rc) rc = encrypt_core(c, src, count, d_seeds, sk_index ? d_skof : nullptr, sk->d, ct->d,
+                                   enc_work(cv, c->scratch, cap, idx));
+    }
     cudaFreeAsync(buf, c->stream);
     if (!rc) rc = check_stats(c);
     if (rc) {
@@ -1160,15 +1220,34 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
     int rc = set_device(c);
     if (rc) return rc;
     const size_t N = c->n, L = c->L, d = lo->d, r = lo->r, cols = lo->cols, nb = lo->batches;
-    const size_t CH = 256;
+    const size_t CH = 512;
     const double scale2 = c->dc.scale * c->dc.scale;
+    // small per-delta inputs: staged once through pinned memory (async H2D)
+    const size_t sm_bytes = (size_t)n * 8 + (size_t)n * 4 * 2 + 512;
+    rc = ensure_pinned(c, sm_bytes);
+    if (rc) return rc;
+    uint64_t* p_seeds = static_cast<uint64_t*>(c->pinned);
+    int* p_ex = reinterpret_cast<int*>(p_seeds + n);
+    int* p_sk = p_ex + n;
+    memcpy(p_seeds, seeds, (size_t)n * 8);
+    if (expert) memcpy(p_ex, expert, (size_t)n * 4);
+    if (sk_index) memcpy(p_sk, sk_index, (size_t)n * 4);
+    void* small = nullptr;
+    rc = dev_alloc(c, &small, sm_bytes);
+    if (rc) return rc;
+    CU(cudaMemcpyAsync(small, c->pinned, sm_bytes - 512, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaEventRecord(c->pinned_free, c->stream));
+    const uint64_t* d_seeds_all = static_cast<uint64_t*>(small);
+    const int* d_ex_all = reinterpret_cast<const int*>(d_seeds_all + n);
+    const int* d_sk_all = d_ex_all + n;
     for (size_t v0 = 0; v0 < n && !rc; v0 += CH) {
         const size_t nv = n - v0 < CH ? n - v0 : CH;
         Carve cv;
         const size_t i_h = cv.add(io_on_device ? 0 : nv * d * 8), i_o = cv.add(io_on_device ? 0 : nv * d * 8),
-                     i_in = cv.add(nv * r * 8), i_s = cv.add(nv * 8), i_ex = cv.add(nv * 4), i_sk = cv.add(nv * 4),
+                     i_in = cv.add(nv * r * 8),
                      i_ct = cv.add(nv * 2 * L * N * 8), i_m = cv.add(nv * N * 8), i_e = cv.add(nv * N),
-                     i_fe = cv.add(nv * 2 * N * 8), i_fl = cv.add(nv * 4), i_pl = cv.add(nv * sizeof(StreamPlan)),
+                     i_fe = cv.add(nv * 2 * N * 8), i_fl = cv.add((2 * nv + 1) * 4),
+                     i_pl = cv.add(nv * sizeof(StreamPlan)),
                      i_M = cv.add(nv * nb * 2 * N * 8), i_fd = cv.add(nv * nb * 2 * N * 8),
                      i_sg = cv.add(nv * nb * cols * 8);
         rc = ensure_scratch(c, cv.total());
@@ -1177,26 +1256,19 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         double* dh = io_on_device ? const_cast<double*>(h) + v0 * d : cv.at<double>(S, i_h);
         double* dout = io_on_device ? delta + v0 * d : cv.at<double>(S, i_o);
         double* dinter = (io_on_device && inter) ? inter + v0 * r : cv.at<double>(S, i_in);
-        uint64_t* ds = cv.at<uint64_t>(S, i_s);
-        int* dex = cv.at<int>(S, i_ex);
-        int* dsk = cv.at<int>(S, i_sk);
+        const uint64_t* ds = d_seeds_all + v0;
+        const int* dex = d_ex_all + v0;
+        const int* dsk = d_sk_all + v0;
         uint64_t* ct = cv.at<uint64_t>(S, i_ct);
-        int64_t* m = cv.at<int64_t>(S, i_m);
-        int8_t* e = cv.at<int8_t>(S, i_e);
-        double* fe = cv.at<double>(S, i_fe);
-        uint32_t* fl = cv.at<uint32_t>(S, i_fl);
-        StreamPlan* pl = cv.at<StreamPlan>(S, i_pl);
         uint64_t* M = cv.at<uint64_t>(S, i_M);
         double* fd = cv.at<double>(S, i_fd);
         double* sg = cv.at<double>(S, i_sg);
         if (!io_on_device) rc = h2d_small(c, dh, h + v0 * d, nv * d);
-        if (!rc) rc = h2d_small(c, ds, seeds + v0, nv);
-        if (!rc && expert) rc = h2d_small(c, dex, (const int*)expert + v0, nv);
-        if (!rc && sk_index) rc = h2d_small(c, dsk, (const int*)sk_index + v0, nv);
         if (rc) break;
         // 1. encrypt the cols-fold replicated hidden states (:1267-1272)
         SlotSrc src{dh, 0, (int)d, (long long)d, (int)d, (int)cols};
-        rc = encrypt_core(c, src, nv, ds, sk_index ? dsk : nullptr, sk->d, ct);
+        const size_t eidx[5] = {i_m, i_e, i_fe, i_fl, i_pl};
+        rc = encrypt_core(c, src, nv, ds, sk_index ? dsk : nullptr, sk->d, ct, enc_work(cv, S, nv, eidx));
         if (rc) break;
         // 2. ct x packed_pt (limbs 0/1) fused with decrypt's c0 + c1*s, INTT (:1311-1315)
         CU(launch_decrypt_limbs(c->dc, M, 2, ct, (long long)2 * L * N, (int)L, sk->d, sk_index ? dsk : nullptr,
@@ -1212,6 +1284,7 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
             if (inter) CU(cudaMemcpyAsync(inter + v0 * r, dinter, nv * r * 8, cudaMemcpyDeviceToHost, c->stream));
         }
     }
+    cudaFreeAsync(small, c->stream);
     if (rc) return rc;
     if (!io_on_device) return check_stats(c);
     return TS_OK;

@@ -1,0 +1,163 @@
+"""Microbenchmarks of single kernels through the C ABI (also the small cases
+used for ncu captures).
+
+    python -m provenloop_b200.microbench ntt [--polys 1024] [--reps 10]
+    python -m provenloop_b200.microbench hadamard [--polys 1024] [--reps 4]
+    python -m provenloop_b200.microbench delta [--batch 256] [--reps 3]
+
+`ntt` is the C2 configuration: `polys` polynomials x 3 limbs x N = 16384 with
+the three largest distinct 50-bit primes == 1 mod 2N, forward then inverse
+negacyclic NTT (checked to round-trip), timed with CUDA events on the
+library's stream.  Prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+
+N_POLY = 16384
+C2_PRIMES = [1125899904679937, 1125899903991809, 1125899903827969]
+
+
+def _ctx(moduli=None, device=0):
+    import torch
+
+    from . import _lib, tensafe_he
+
+    ctx = (tensafe_he.CkksContext(N_POLY, device=device) if moduli is None
+           else tensafe_he.CkksContext.from_moduli(N_POLY, moduli, device=device))
+    stream = torch.cuda.Stream(device=device)
+    _lib.check(_lib.lib().ts_ctx_set_stream(ctx.handle, stream.cuda_stream), "ts_ctx_set_stream")
+    return ctx, stream
+
+
+def _polys(P, dev, seed=1):
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    q = torch.tensor(C2_PRIMES, dtype=torch.int64, device=dev).view(1, 3, 1)
+    return (torch.randint(0, 1 << 62, (P, 3, N_POLY), device=dev, generator=g) % q).contiguous()
+
+
+def ntt(polys=1024, reps=10, device=0, peak_gbs=None):
+    import torch
+
+    from . import _lib
+
+    dev = torch.device("cuda", device)
+    ctx, stream = _ctx(C2_PRIMES, device)
+    L = _lib.lib()
+    with torch.cuda.stream(stream):
+        x = _polys(polys, dev)
+        ref = x.clone()
+        for _ in range(2):
+            _lib.check(L.ts_ntt_forward(ctx.handle, x.data_ptr(), polys, 3, 0))
+            _lib.check(L.ts_ntt_inverse(ctx.handle, x.data_ptr(), polys, 3, 0))
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        fw = iv = 0.0
+        for _ in range(reps):
+            ev[0].record(stream)
+            _lib.check(L.ts_ntt_forward(ctx.handle, x.data_ptr(), polys, 3, 0))
+            ev[1].record(stream)
+            _lib.check(L.ts_ntt_inverse(ctx.handle, x.data_ptr(), polys, 3, 0))
+            ev[2].record(stream)
+            stream.synchronize()
+            fw += ev[0].elapsed_time(ev[1])
+            iv += ev[1].elapsed_time(ev[2])
+        ok = bool(torch.equal(x, ref))
+    byt = polys * 3 * N_POLY * 16  # one read + one write of every 8-byte word
+    out = {"kernel": "ntt", "polys": polys, "limbs": 3, "n": N_POLY, "roundtrip_bit_exact": ok,
+           "forward_ms": fw / reps, "inverse_ms": iv / reps,
+           "forward_gbs": byt / (fw / reps / 1e3) / 1e9, "inverse_gbs": byt / (iv / reps / 1e3) / 1e9,
+           "bytes_per_direction": byt,
+           "butterflies_per_s_forward": polys * 3 * (N_POLY // 2) * 14 / (fw / reps / 1e3)}
+    if peak_gbs:
+        out["forward_frac"] = out["forward_gbs"] / peak_gbs
+        out["inverse_frac"] = out["inverse_gbs"] / peak_gbs
+    return out
+
+
+def hadamard(polys=1024, reps=4, device=0, peak_gbs=None):
+    import torch
+
+    from . import _lib
+
+    dev = torch.device("cuda", device)
+    ctx, stream = _ctx(C2_PRIMES, device)
+    L = _lib.lib()
+    with torch.cuda.stream(stream):
+        a = _polys(polys, dev, 1)
+        b = _polys(polys, dev, 2)
+        out = torch.empty_like(a)
+        for _ in range(2):
+            _lib.check(L.ts_hadamard(ctx.handle, out.data_ptr(), a.data_ptr(), b.data_ptr(), polys, 3, 0))
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record(stream)
+        for _ in range(reps):
+            _lib.check(L.ts_hadamard(ctx.handle, out.data_ptr(), a.data_ptr(), b.data_ptr(), polys, 3, 0))
+        ev[1].record(stream)
+        stream.synchronize()
+        ms = ev[0].elapsed_time(ev[1])
+        qa = torch.tensor(C2_PRIMES, dtype=torch.int64, device=dev).view(1, 3, 1)
+        # spot check a slice exactly with Python integers
+        aa, bb, oo = (t[0, :, :64].cpu().numpy().astype(object) for t in (a, b, out))
+        ok = all(int(oo[l, i]) == int(aa[l, i]) * int(bb[l, i]) % C2_PRIMES[l] for l in range(3) for i in range(64))
+        del qa
+    byt = reps * polys * 3 * N_POLY * 24
+    o = {"kernel": "hadamard", "products": reps * polys, "limbs": 3, "ms": ms, "gbs": byt / (ms / 1e3) / 1e9,
+         "spot_check_exact": ok}
+    if peak_gbs:
+        o["frac"] = o["gbs"] / peak_gbs
+    return o
+
+
+def delta(batch=256, reps=3, device=0):
+    import torch
+
+    from . import _lib
+    from .backend import ZeroMoaiLora
+
+    dev = torch.device("cuda", device)
+    ctx, stream = _ctx(None, device)
+    rng = np.random.default_rng(0)
+    A = (rng.standard_normal((16, 1536)) * 0.02).astype(np.float32)
+    B = (rng.standard_normal((1536, 16)) * 0.02).astype(np.float32)
+    H = rng.standard_normal((batch, 1536))
+    with torch.cuda.stream(stream):
+        sk = ctx.keygen(0)
+        lora = ZeroMoaiLora(ctx, A, B)
+        h = torch.from_numpy(H).to(dev)
+        d = torch.empty_like(h)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        lora.delta_device(sk, h, np.arange(batch, dtype=np.uint64), d)
+        ev[0].record(stream)
+        for i in range(reps):
+            lora.delta_device(sk, h, np.arange((i + 1) * batch, (i + 2) * batch, dtype=np.uint64), d)
+        ev[1].record(stream)
+        stream.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / reps
+    return {"kernel": "lora_delta_pipeline", "batch": batch, "ms_per_batch": ms, "deltas_per_s": batch / (ms / 1e3),
+            "launches_total": _lib.launch_count()}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["ntt", "hadamard", "delta"])
+    ap.add_argument("--polys", type=int, default=1024)
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--reps", type=int, default=None)
+    a = ap.parse_args()
+    if a.what == "ntt":
+        r = ntt(a.polys, a.reps or 10)
+    elif a.what == "hadamard":
+        r = hadamard(a.polys, a.reps or 4)
+    else:
+        r = delta(a.batch, a.reps or 3)
+    print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()

@@ -234,7 +234,7 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    from provenloop_b200 import _lib, tensafe_he
+    from provenloop_b200 import _lib, multigpu, tensafe_he
     from provenloop_b200.backend import ZeroMoaiLora
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -258,16 +258,15 @@ def run_ours(args):
     h_dev = torch.from_numpy(H).to(dev)
     delta_dev = torch.empty((batch, D), dtype=torch.float64, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    gather = None
-    if world > 1 and rank == 0:
-        gather = [torch.empty((batch, D), dtype=torch.float64, device=dev) for _ in range(world)]
-    seed_base = 1 + rank * 1_000_000_000
+    # users are sharded in blocks over ranks; seeds depend on (user, step) only
+    n_users = batch * world
+    u0, u1 = multigpu.user_block(n_users, world, rank)
+    users = np.arange(u0, u1, dtype=np.uint64)
 
     def step(i):
-        seeds = np.arange(seed_base + i * batch, seed_base + (i + 1) * batch, dtype=np.uint64)
+        seeds = np.asarray([multigpu.stream_seed(int(u), i, n_users) for u in users], dtype=np.uint64)
         lora.delta_device(sk, h_dev, seeds, delta_dev)
-        if world > 1:
-            dist.gather(delta_dev, gather_list=gather, dst=0)
+        multigpu.gather_rows(delta_dev, world, rank)   # decrypted deltas to rank 0 (NCCL)
 
     for i in range(args.warmup):
         step(i)
@@ -327,7 +326,7 @@ def run_ours(args):
         flush.zero_()
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
-        seeds = np.arange(seed_base + (100 + k) * batch, seed_base + (101 + k) * batch, dtype=np.uint64)
+        seeds = np.asarray([multigpu.stream_seed(int(u), 1000 + k, n_users) for u in users], dtype=np.uint64)
         lora.delta(sk, hv, seeds, out=dv, want_inter=False)   # H2D, GPU pipeline, D2H, sync
         e2e_ms += (time.perf_counter() - t0) * 1000.0
     t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)

@@ -140,6 +140,21 @@ int ts_ct_select(ts_ctx* ctx, const ts_ct* ct, uint32_t index, ts_ct** out);
 int ts_decrypt(ts_ctx* ctx, const ts_ct* ct, const ts_sk* sk, const int32_t* sk_index, double* out,
                int out_on_device);
 
+/* Decrypt without allocating -- no counterpart in the reference.  For
+ * callers that cannot allocate device memory while serving (a server that
+ * reserves the whole device for its model and KV cache at start-up, or a
+ * plugin host whose device heap belongs to another framework's allocator):
+ * same result as ts_decrypt with key 0 of `sk`, written to out_dev (device
+ * memory, count * num_slots doubles), with all temporaries in one fixed
+ * 2 MiB device array that the library holds on every GPU it is loaded on.
+ * At N = 16384 that fits 4 ciphertexts after ct x pt (CRT, 2 limbs) or 5
+ * fresh ones per call; larger requests fail with TS_ERR_ARG.  The work is
+ * queued on the context's stream and the call returns without waiting.
+ * The first call on a device resolves the array's address
+ * (cudaGetSymbolAddress), so make that first call before any stream
+ * capture.  Calls share the array: calls that overlap on the GPU race. */
+int ts_decrypt_noalloc(ts_ctx* ctx, const ts_ct* ct, const ts_sk* sk, double* out_dev);
+
 /* ct_pt_mul(ct, plaintext) -- lib.rs:178-195 / __mul__ lib.rs:336-356 /
  * ciphertext.rs:408-418: the plaintext (len <= num_slots doubles) is encoded
  * and transformed on the device, then multiplied into every ciphertext. */

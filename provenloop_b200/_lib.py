@@ -67,6 +67,7 @@ SIGNATURES = {
     "ts_ct_import": (cint, [vp, P(u64), P(u64), u32, f64, pvp]),
     "ts_ct_select": (cint, [vp, vp, u32, pvp]),
     "ts_decrypt": (cint, [vp, vp, vp, P(i32), vp, cint]),
+    "ts_decrypt_noalloc": (cint, [vp, vp, vp, vp]),
     "ts_ct_pt_mul": (cint, [vp, vp, P(f64), sz, pvp]),
     "ts_encode_ntt": (cint, [vp, vp, sz, sz, sz, cint, pvp]),
     "ts_pt_destroy": (cint, [vp]),

@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libtsgpu.so")
-SOURCES = ["kernels.cu", "tsgpu.cu"]
+SOURCES = ["kernels.cu", "tsgpu.cu", "noalloc.cu"]
 HEADERS = ["common.cuh", "ntt.cuh", "fft.cuh", "kernels.cuh"]
 
 

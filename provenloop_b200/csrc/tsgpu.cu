@@ -1320,3 +1320,35 @@ int ts_encrypt_stream(ts_ctx* c, const ts_sk* sk, const double* data, size_t cou
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------
+// Read-only accessors for noalloc.cu (the opaque structs are defined here).
+// ---------------------------------------------------------------------
+namespace tsg_host {
+int noalloc_ctx(ts_ctx* c, int* device, const DevCtx** dc, cudaStream_t* stream, uint32_t* n, uint32_t* slots,
+                std::mutex** mu) {
+    *device = c->device;
+    *dc = &c->dc;
+    *stream = c->stream;
+    *n = c->n;
+    *slots = c->slots;
+    *mu = &c->mu;
+    return TS_OK;
+}
+int noalloc_ct(const ts_ct* ct, const ts_ctx** owner, uint32_t* count, uint32_t* limbs, double* scale,
+               const uint64_t** d) {
+    *owner = ct->ctx;
+    *count = ct->count;
+    *limbs = ct->limbs;
+    *scale = ct->scale;
+    *d = ct->d;
+    return TS_OK;
+}
+int noalloc_sk(const ts_sk* sk, const ts_ctx** owner, uint32_t* count, const uint64_t** d) {
+    *owner = sk->ctx;
+    *count = sk->count;
+    *d = sk->d;
+    return TS_OK;
+}
+int noalloc_fail(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace tsg_host

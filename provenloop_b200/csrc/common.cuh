@@ -165,6 +165,13 @@ __device__ __forceinline__ int gaussian_round(uint64_t u1w, uint64_t u2w, double
     return (int)round(v);
 }
 
+// ----------------------------------------------------------------- L2 prefetch
+// Asks the TMA unit to pull [p, p + bytes) into L2 (p 16-byte aligned, bytes
+// a multiple of 16); a hint that neither blocks nor touches shared memory.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // ----------------------------------------------------------------- u128 -> f64
 // Round-to-nearest-even conversion of the 128-bit integer (hi, lo), as Rust's
 // `u128 as f64` (used by the CRT branch of decrypt, ciphertext.rs:379-383).

@@ -58,9 +58,24 @@ __device__ __forceinline__ uint64_t word64(uint64_t seed, uint64_t w) {
     return (uint64_t)chacha_word(seed, w) | ((uint64_t)chacha_word(seed, w + 1) << 32);
 }
 
+// Stream words [16*b0, 16*(b0 + nblk)) of `seed` into win (16-byte
+// aligned, nblk*16 words): one ChaCha block per thread and round, instead of
+// one block per word.
+__device__ __forceinline__ void chacha_window(uint64_t seed, uint64_t b0, int nblk, uint32_t* win) {
+    for (int b = threadIdx.x; b < nblk; b += blockDim.x) {
+        uint32_t w[16];
+        chacha_block(seed, (uint32_t)(b0 + b), w);
+        uint4* o = reinterpret_cast<uint4*>(win + 16 * b);
+        o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        o[2] = make_uint4(w[8], w[9], w[10], w[11]);
+        o[3] = make_uint4(w[12], w[13], w[14], w[15]);
+    }
+}
+
 // Block-wide exclusive scan of one int per thread (blockDim.x <= 1024).
 __device__ int block_exclusive_scan(int x, int* total) {
-    __shared__ int warp_sums[32];
+    __shared__ int warp_sums[33];  // 32 exclusive warp offsets, then the total
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     int incl = x;
 #pragma unroll
@@ -80,11 +95,11 @@ __device__ int block_exclusive_scan(int x, int* total) {
             if (lane >= o) vi += y;
         }
         if (lane < nw) warp_sums[lane] = vi - v;
-        if (lane == 31) warp_sums[31] = vi;  // total (nw <= 32)
+        if (lane == 31) warp_sums[32] = vi;  // total over all nw <= 32 warps
     }
     __syncthreads();
     const int res = incl - x + warp_sums[wid];
-    *total = warp_sums[31];
+    *total = warp_sums[32];
     __syncthreads();
     return res;
 }
@@ -467,8 +482,45 @@ cudaError_t launch_ntt_signed(const DevCtx& c, uint64_t* out, const int64_t* m, 
 }
 
 // ======================================================================
+// Shoup companions of fixed operands (secret keys, cached plaintexts)
+// ======================================================================
+__global__ void k_shoup_companion(uint64_t* __restrict__ out, const uint64_t* __restrict__ in,
+                                  const LimbTab* __restrict__ tabs, int L, int logn, long long total) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const uint64_t q = tabs[(int)((i >> logn) % L)].q;
+        // restoring division of in * 2^64 by q (q < 2^61, so 2r never overflows)
+        uint64_t r = in[i] % q, quo = 0;
+        for (int b = 0; b < 64; b++) {
+            r <<= 1;
+            quo <<= 1;
+            if (r >= q) {
+                r -= q;
+                quo |= 1;
+            }
+        }
+        out[i] = quo;
+    }
+}
+
+cudaError_t launch_shoup_companion(const DevCtx& c, uint64_t* out, const uint64_t* in, long long polys,
+                                   cudaStream_t s) {
+    if (polys <= 0) return cudaSuccess;
+    const long long total = polys << c.logn;
+    const long long blocks = (total + 255) / 256;
+    KScope ks("shoup_companion", s);
+    k_shoup_companion<<<(int)(blocks < 4 * 148 ? blocks : 4 * 148), 256, 0, s>>>(out, in, c.tabs, c.L, c.logn, total);
+    return cudaGetLastError();
+}
+
+// ======================================================================
 // Encryption per (ciphertext, limb) (ciphertext.rs:167-229)
 // ======================================================================
+// Candidates per window round of k_enc_a's plan mode (2 words each); the
+// window of 2 * kEncPlanRound + 16 words follows the NTT buffer.
+constexpr int kEncPlanRound = 4096;
+constexpr size_t kEncPlanWinBytes = (2 * kEncPlanRound + 16) * 4;
+
 // Two single-transform kernels (each fits in registers):
 //   k_enc_a: c1 = NTT(a), a = range_u64(q_l) draws (sampling.rs:62-64);
 //   k_enc_u: c0 = NTT(m + e mod q_l) - c1 * s.
@@ -505,10 +557,36 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
             }
             if (rej) flag_stream(flags, nvec, v);
         } else {
+            // exact plan: candidates 0 .. N + nrej - 1 of this limb's segment
+            // at words off + 2*cidx; the rejected ones are skipped and
+            // accepted candidate cidx lands at output cidx - (# rejected
+            // before it).  Words come through a window behind the NTT buffer.
             const StreamPlan& P = plans[v];
-            for (int i = tid; i < N; i += NT) {
-                const uint32_t ci = cand_index((uint32_t)i, P.rej[limb], P.nrej[limb]);
-                sm[pad(i)] = mod_u64(word64(seed, P.off[limb] + 2ULL * ci), T.q, T.mu64);
+            uint32_t* win = reinterpret_cast<uint32_t*>(sm + NttCfg<LOGN>::SMEM_WORDS);
+            const uint32_t nrej = P.nrej[limb];
+            const uint32_t* rej = P.rej[limb];
+            const int ncand = N + (int)nrej;
+            for (int c0 = 0; c0 < ncand; c0 += kEncPlanRound) {
+                const int cnt = ncand - c0 < kEncPlanRound ? ncand - c0 : kEncPlanRound;
+                const uint64_t ws = P.off[limb] + 2ULL * c0;
+                const int sh = (int)(ws & 15);
+                __syncthreads();
+                chacha_window(seed, ws >> 4, (sh + 2 * cnt + 15) >> 4, win);
+                __syncthreads();
+                for (int cl = tid; cl < cnt; cl += NT) {
+                    const uint32_t cidx = (uint32_t)(c0 + cl);
+                    uint32_t before = 0;
+                    bool rejected = false;
+                    for (uint32_t t = 0; t < nrej; t++) {
+                        before += rej[t] < cidx;
+                        rejected |= rej[t] == cidx;
+                    }
+                    if (!rejected) {
+                        const int o = sh + 2 * cl;
+                        const uint64_t u = (uint64_t)win[o] | ((uint64_t)win[o + 1] << 32);
+                        sm[pad((int)(cidx - before))] = mod_u64(u, T.q, T.mu64);
+                    }
+                }
             }
         }
         __syncthreads();
@@ -521,7 +599,8 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
 template <int LOGN>
 __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     k_enc_u(uint64_t* __restrict__ ct, const int64_t* __restrict__ m, const int8_t* __restrict__ e,
-            const uint64_t* __restrict__ sk, const int* __restrict__ sk_of, const LimbTab* __restrict__ tabs, int L,
+            const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
+            const LimbTab* __restrict__ tabs, int L,
             int nvec, const uint32_t* __restrict__ flags, int list_mode) {
     extern __shared__ __align__(16) uint64_t sm[];
     const int limb = blockIdx.x;
@@ -531,41 +610,47 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
         const int v = list_mode ? (int)flags[nvec + 1 + it] : it;
         uint64_t* c0 = ct + (((size_t)v * 2 * L + limb) << LOGN);
         const uint64_t* c1 = ct + (((size_t)v * 2 * L + L + limb) << LOGN);
-        const uint64_t* s = sk + (((size_t)(sk_of ? sk_of[v] : 0) * L + limb) << LOGN);
+        const size_t so = ((size_t)(sk_of ? sk_of[v] : 0) * L + limb) << LOGN;
+        const uint64_t* s = sk + so;
+        const uint64_t* sp = sks + so;
         const int64_t* mv = m + ((size_t)v << LOGN);
         const int8_t* ev = e + ((size_t)v << LOGN);
+        if (threadIdx.x == 0) prefetch_l2(c1, 1u << (LOGN + 3));  // read by the epilogue
         ntt_forward_block<LOGN>(
             sm, T,
             [&](int j) {
-                return add_mod(signed_residue(mv[j], T.q, T.mu64), signed_residue((int64_t)ev[j], T.q, T.mu64),
-                               T.q);
+                // |e| < q: the reference's residue of a negative e is q + e
+                const int ej = ev[j];
+                return add_mod(signed_residue(mv[j], T.q, T.mu64), ej >= 0 ? (uint64_t)ej : T.q + ej, T.q);
             },
             [&](int j, uint64_t x) {
-                const uint64_t as = mul_barrett(c1[j], s[j], T.q, T.bmu, T.bk);
-                c0[j] = sub_mod(x, as, T.q);
+                // x - c1*s with the product in [0, 4q): x + 4q - as lies in [1, 5q)
+                const uint64_t as = mul_shoup4(c1[j], s[j], sp[j], T.q);
+                c0[j] = canon8(x + 4 * T.q - as, T.q);
             });
         __syncthreads();
     }
 }
 
 cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m, const int8_t* e, const uint64_t* sk,
-                                 const int* sk_of, const uint64_t* seeds, int nvec, uint32_t* flags,
+                                 const uint64_t* sks, const int* sk_of, const uint64_t* seeds, int nvec, uint32_t* flags,
                                  const StreamPlan* plans, bool plan_mode, cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
     const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
-        cudaError_t er = ensure_smem(k_enc_a<LG>, smem);
+        const size_t smem_a = plan_mode ? smem + kEncPlanWinBytes : smem;
+        cudaError_t er = ensure_smem(k_enc_a<LG>, smem + kEncPlanWinBytes);
         if (er != cudaSuccess) return er;
         er = ensure_smem(k_enc_u<LG>, smem);
         if (er != cudaSuccess) return er;
         const int gy = plan_mode ? (nvec < 16 ? nvec : 16) : nvec;
         {
             KScope ks(plan_mode ? "enc_a_fix" : "enc_a", s);
-            k_enc_a<LG><<<dim3(c.L, gy), NttCfg<LG>::NT, smem, s>>>(ct, seeds, c.tabs, c.L, nvec, flags, plans,
-                                                                     plan_mode ? 1 : 0);
+            k_enc_a<LG><<<dim3(c.L, gy), NttCfg<LG>::NT, smem_a, s>>>(ct, seeds, c.tabs, c.L, nvec, flags, plans,
+                                                                       plan_mode ? 1 : 0);
         }
         KScope ks(plan_mode ? "enc_u_fix" : "enc_u", s);
-        k_enc_u<LG><<<dim3(c.L, gy), NttCfg<LG>::NT, smem, s>>>(ct, m, e, sk, sk_of, c.tabs, c.L, nvec, flags,
+        k_enc_u<LG><<<dim3(c.L, gy), NttCfg<LG>::NT, smem, s>>>(ct, m, e, sk, sks, sk_of, c.tabs, c.L, nvec, flags,
                                                                  plan_mode ? 1 : 0);
     });
     return cudaGetLastError();
@@ -574,11 +659,18 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
 // ======================================================================
 // Exact stream plans for streams that hit a rejection (rng.rs:109-133)
 // ======================================================================
+// Candidates each plan thread tests per round, and the window that holds
+// their words (up to 2 words per candidate, 1024 threads, plus one block
+// of misalignment).
+constexpr int kPlanCand = 4;
+constexpr int kPlanWin = kPlanCand * 1024 * 2 + 16;
+
 __device__ void plan_one(const uint64_t* __restrict__ seeds, int v, StreamPlan* plans, const SegList& segs,
                          const LimbTab* __restrict__ tabs, int N, unsigned long long* stats, int tid) {
     __shared__ uint32_t s_nrej;
     __shared__ uint32_t s_rej[kMaxRej + 1];
     __shared__ uint32_t s_overflow;
+    __shared__ __align__(16) uint32_t win[kPlanWin];
     StreamPlan& P = plans[v];
     const uint64_t seed = seeds[v];
     uint64_t off = 0;
@@ -597,16 +689,21 @@ __device__ void plan_one(const uint64_t* __restrict__ seeds, int v, StreamPlan* 
         }
         const int wpc = kind == SEG_UNIFORM ? 2 : 1;
         const uint64_t thr = kind == SEG_UNIFORM ? tabs[segs.limb[sg]].thresh : 1ULL;
+        const int per_round = kPlanCand * (int)blockDim.x;
         long long accepted = 0, base = 0;
         // bounded: a segment that needs more than 4N candidates is reported
         // as an overflow instead of scanning on
         while (accepted < N && base < 4LL * N) {
-            int ok[8], cnt = 0;
+            // candidates base .. base + per_round - 1 sit at words ws + wpc*i
+            const uint64_t ws = off + (uint64_t)wpc * (uint64_t)base;
+            const int sh = (int)(ws & 15);
+            chacha_window(seed, ws >> 4, (sh + wpc * per_round + 15) >> 4, win);
+            __syncthreads();
+            int ok[kPlanCand], cnt = 0;
 #pragma unroll
-            for (int t = 0; t < 8; t++) {
-                const uint64_t cidx = (uint64_t)base + (uint64_t)tid * 8 + t;
-                const uint64_t w = off + (uint64_t)wpc * cidx;
-                const uint64_t val = kind == SEG_UNIFORM ? word64(seed, w) : (uint64_t)chacha_word(seed, w);
+            for (int t = 0; t < kPlanCand; t++) {
+                const int o = sh + wpc * (tid * kPlanCand + t);
+                const uint64_t val = wpc == 2 ? ((uint64_t)win[o] | ((uint64_t)win[o + 1] << 32)) : (uint64_t)win[o];
                 ok[t] = val >= thr;
                 cnt += ok[t];
             }
@@ -614,16 +711,16 @@ __device__ void plan_one(const uint64_t* __restrict__ seeds, int v, StreamPlan* 
             const int pre = block_exclusive_scan(cnt, &total);
             int run = pre;
 #pragma unroll
-            for (int t = 0; t < 8; t++) {
+            for (int t = 0; t < kPlanCand; t++) {
                 if (!ok[t] && accepted + run < N) {
                     const uint32_t slot = atomicAdd(&s_nrej, 1u);
-                    if (slot < kMaxRej) s_rej[slot] = (uint32_t)(base + (long long)tid * 8 + t);
+                    if (slot < kMaxRej) s_rej[slot] = (uint32_t)(base + (long long)tid * kPlanCand + t);
                     else s_overflow = 1;
                 }
                 run += ok[t];
             }
             accepted += total;
-            base += 8LL * blockDim.x;
+            base += per_round;
             __syncthreads();
         }
         if (tid == 0 && accepted < N) s_overflow = 1;
@@ -675,22 +772,39 @@ cudaError_t launch_plan(const DevCtx& c, const uint64_t* seeds, int nstreams, co
     return cudaGetLastError();
 }
 
-__global__ void k_gauss_fix(int8_t* __restrict__ e, const uint64_t* __restrict__ seeds, int N, int nvec,
-                            const uint32_t* __restrict__ flags, const StreamPlan* __restrict__ plans, int seg,
-                            unsigned long long* stats) {
+// Gaussian samples per window round of k_gauss_fix (4 words each).
+constexpr int kGaussRound = 2048;
+
+__global__ void __launch_bounds__(512)
+    k_gauss_fix(int8_t* __restrict__ e, const uint64_t* __restrict__ seeds, int N, int nvec,
+                const uint32_t* __restrict__ flags, const StreamPlan* __restrict__ plans, int seg,
+                unsigned long long* stats) {
+    __shared__ __align__(16) uint32_t win[4 * kGaussRound + 16];
     const int nwork = (int)flags[nvec];
     for (int it = blockIdx.x; it < nwork; it += gridDim.x) {
         const int v = (int)flags[nvec + 1 + it];
         const uint64_t seed = seeds[v];
         const uint64_t off = plans[v].off[seg];
         int ties = 0;
-        for (int j = threadIdx.x; j < N; j += blockDim.x) {
-            const uint64_t w = off + 4ULL * j;
-            bool tie;
-            e[(size_t)v * N + j] = (int8_t)gaussian_round(word64(seed, w), word64(seed, w + 2), 3.19, &tie);
-            ties += tie;
+        for (int j0 = 0; j0 < N; j0 += kGaussRound) {
+            const int cnt = N - j0 < kGaussRound ? N - j0 : kGaussRound;
+            // sample j uses words off + 4j .. off + 4j + 3 (two u64 draws)
+            const uint64_t ws = off + 4ULL * j0;
+            const int sh = (int)(ws & 15);
+            __syncthreads();
+            chacha_window(seed, ws >> 4, (sh + 4 * cnt + 15) >> 4, win);
+            __syncthreads();
+            for (int jj = threadIdx.x; jj < cnt; jj += blockDim.x) {
+                const int o = sh + 4 * jj;
+                const uint64_t u1 = (uint64_t)win[o] | ((uint64_t)win[o + 1] << 32);
+                const uint64_t u2 = (uint64_t)win[o + 2] | ((uint64_t)win[o + 3] << 32);
+                bool tie;
+                e[(size_t)v * N + j0 + jj] = (int8_t)gaussian_round(u1, u2, 3.19, &tie);
+                ties += tie;
+            }
         }
         if (ties && stats) atomicAdd(stats + STAT_NEAR_TIE, (unsigned long long)ties);
+        __syncthreads();
     }
 }
 
@@ -708,15 +822,18 @@ cudaError_t launch_gauss_fix(const DevCtx& c, int8_t* e, const uint64_t* seeds, 
 template <int LOGN>
 __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     k_decrypt_limb(uint64_t* __restrict__ M, int nl, const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs,
-                   const uint64_t* __restrict__ sk, const int* __restrict__ sk_of, const uint64_t* __restrict__ pt,
-                   const int* __restrict__ pt_sel, int per_ct, const LimbTab* __restrict__ tabs, int L) {
+                   const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
+                   const uint64_t* __restrict__ pt, const int* __restrict__ pt_sel, int per_ct,
+                   const LimbTab* __restrict__ tabs, int L) {
     extern __shared__ __align__(16) uint64_t sm[];
     const int limb = blockIdx.x, v = blockIdx.y;
     const LimbTab T = tabs[limb];
     const int ci = v / per_ct;
     const uint64_t* c0 = cts + (size_t)ci * ct_stride + ((size_t)limb << LOGN);
     const uint64_t* c1 = cts + (size_t)ci * ct_stride + ((size_t)(ct_limbs + limb) << LOGN);
-    const uint64_t* s = sk + (((size_t)(sk_of ? sk_of[ci] : 0) * L + limb) << LOGN);
+    const size_t so = ((size_t)(sk_of ? sk_of[ci] : 0) * L + limb) << LOGN;
+    const uint64_t* s = sk + so;
+    const uint64_t* sp = sks + so;
     const uint64_t* p = nullptr;
     if (pt) {
         const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
@@ -732,22 +849,22 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
                 a0 = mul_barrett(a0, pj, T.q, T.bmu, T.bk);
                 a1 = mul_barrett(a1, pj, T.q, T.bmu, T.bk);
             }
-            return add_mod(a0, mul_barrett(a1, s[j], T.q, T.bmu, T.bk), T.q);
+            return a0 + canon4(mul_shoup4(a1, s[j], sp[j], T.q), T.q);  // < 2q
         },
         [&](int j, uint64_t x) { out[j] = x; });
 }
 
 cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uint64_t* cts, long long ct_stride,
-                                 int ct_limbs, const uint64_t* sk, const int* sk_of, const uint64_t* pt,
-                                 const int* pt_sel, int per_ct, int nvec, cudaStream_t s) {
+                                 int ct_limbs, const uint64_t* sk, const uint64_t* sks, const int* sk_of,
+                                 const uint64_t* pt, const int* pt_sel, int per_ct, int nvec, cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
     const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
         cudaError_t er = ensure_smem(k_decrypt_limb<LG>, smem);
         if (er != cudaSuccess) return er;
         KScope ks("decrypt_limb", s);
-        k_decrypt_limb<LG><<<dim3(nl, nvec), NttCfg<LG>::NT, smem, s>>>(M, nl, cts, ct_stride, ct_limbs, sk, sk_of, pt,
-                                                                        pt_sel, per_ct, c.tabs, c.L);
+        k_decrypt_limb<LG><<<dim3(nl, nvec), NttCfg<LG>::NT, smem, s>>>(M, nl, cts, ct_stride, ct_limbs, sk, sks, sk_of,
+                                                                        pt, pt_sel, per_ct, c.tabs, c.L);
     });
     return cudaGetLastError();
 }
@@ -759,7 +876,7 @@ cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uin
 __device__ __forceinline__ double crt_coeff(uint64_t m0, uint64_t m1, const CrtConst& K) {
     const uint64_t m0q1 = mod_u64(m0, K.q1, K.mu64_1);
     const uint64_t diff = m1 >= m0q1 ? m1 - m0q1 : K.q1 - m0q1 + m1;
-    const uint64_t k = mul_barrett(diff, K.q0inv, K.q1, K.bmu1, K.bk1);
+    const uint64_t k = canon4(mul_shoup4(diff, K.q0inv, K.q0inv_s, K.q1), K.q1);
     // mu = m0 + k*q0 (< q0*q1 < 2^101)
     uint64_t lo = k * K.q0;
     uint64_t hi = mulhi64(k, K.q0);
@@ -877,6 +994,127 @@ cudaError_t launch_decode(const DevCtx& c, const uint64_t* M, int nl, bool crt, 
         if (er != cudaSuccess) return er;
         KScope ks("decode_b", s);
         k_decode_b<LG><<<nvec, 1024, smem_b, s>>>(scratch, c.fft, out_slots, seg_out, seg_d, seg_cols);
+    });
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// Fused decrypt + decode + segment sums for the ZeRo-MOAI delta
+// (ciphertext.rs:408-429, :327-399; encoding.rs:295-315;
+//  inference_engine.py:1382-1386)
+// ======================================================================
+template <int LOGN>
+__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+    k_dec_fused(const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs, const uint64_t* __restrict__ sk,
+                const uint64_t* __restrict__ sks, const int* __restrict__ sk_of, const uint64_t* __restrict__ pt,
+                const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel, int per_ct, int nvec, const LimbTab* __restrict__ tabs, int L, CrtConst K, double inv_scale,
+                const double* __restrict__ W, int cols, uint64_t* __restrict__ M0, double* __restrict__ seg_out) {
+    extern __shared__ __align__(16) uint64_t sm[];
+    constexpr int N = 1 << LOGN, NT = NttCfg<LOGN>::NT;
+    const int tid = threadIdx.x;
+    // persistent: one limb-0 buffer per CTA, reused for every vector it
+    // takes, so the round trip stays in L2
+    uint64_t* m0v = M0 + ((size_t)blockIdx.x << LOGN);
+    for (int v = blockIdx.x; v < nvec; v += gridDim.x) {
+        const int ci = v / per_ct;
+        const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
+        const size_t key = (size_t)(sk_of ? sk_of[ci] : 0) * L;
+        const uint64_t* ctb = cts + (size_t)ci * ct_stride;
+        if (tid == 0 && v + (int)gridDim.x < nvec) {
+            // limbs 0-1 of both components of the next vector's ciphertext
+            const uint64_t* nx = cts + (size_t)((v + gridDim.x) / per_ct) * ct_stride;
+            prefetch_l2(nx, 2u << (LOGN + 3));
+            prefetch_l2(nx + ((size_t)ct_limbs << LOGN), 2u << (LOGN + 3));
+        }
+        // phase 1: limb 0 -> scratch (each element written and later re-read
+        // by the same thread)
+        {
+            const LimbTab T = tabs[0];
+            const uint64_t* c0 = ctb;
+            const uint64_t* c1 = ctb + ((size_t)ct_limbs << LOGN);
+            const uint64_t* s = sk + (key << LOGN);
+            const uint64_t* sp = sks + (key << LOGN);
+            const uint64_t* p = pt + ((size_t)pv * L << LOGN);
+            const uint64_t* pp = pts + ((size_t)pv * L << LOGN);
+            ntt_inverse_block<LOGN>(
+                sm, T,
+                [&](int j) {
+                    // p*(c0 + c1*s): c0 + c1*s < 5q, the product lies in [0, 4q)
+                    return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q);
+                },
+                [&](int j, uint64_t x) { m0v[j] = x; });
+        }
+        __syncthreads();
+        // phase 2: limb 1; the last pass parks element j in sm[pad(j)], a
+        // slot only this thread reads or writes from then on
+        {
+            const LimbTab T = tabs[1];
+            const uint64_t* c0 = ctb + ((size_t)1 << LOGN);
+            const uint64_t* c1 = ctb + ((size_t)(ct_limbs + 1) << LOGN);
+            const uint64_t* s = sk + ((key + 1) << LOGN);
+            const uint64_t* sp = sks + ((key + 1) << LOGN);
+            const uint64_t* p = pt + (((size_t)pv * L + 1) << LOGN);
+            const uint64_t* pp = pts + (((size_t)pv * L + 1) << LOGN);
+            ntt_inverse_block<LOGN>(
+                sm, T,
+                [&](int j) {
+                    // p*(c0 + c1*s): c0 + c1*s < 5q, the product lies in [0, 4q)
+                    return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q);
+                },
+                [&](int j, uint64_t x) { sm[pad(j)] = x; });
+        }
+        // CRT, / Delta^2 and the segment functionals over this thread's
+        // elements j = tid + k * NT
+        double acc[kMaxSegCols];
+#pragma unroll
+        for (int c = 0; c < kMaxSegCols; c++) acc[c] = 0.0;
+#pragma unroll 4
+        for (int k = 0; k < N / NT; k++) {
+            const int j = tid + k * NT;
+            const double coeff = __dmul_rn(crt_coeff(m0v[j], sm[pad(j)], K), inv_scale);
+#pragma unroll
+            for (int c = 0; c < kMaxSegCols; c++)
+                if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
+        }
+        // deterministic block reduction of acc[0 .. cols)
+        __syncthreads();
+        double* red = reinterpret_cast<double*>(sm);  // [NT/32][kMaxSegCols]
+        const int lane = tid & 31, wid = tid >> 5;
+#pragma unroll
+        for (int c = 0; c < kMaxSegCols; c++) {
+            double a = acc[c];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+            if (lane == 0) red[wid * kMaxSegCols + c] = a;
+        }
+        __syncthreads();
+        if (tid < cols) {
+            double a = 0.0;
+            for (int w = 0; w < NT / 32; w++) a += red[w * kMaxSegCols + tid];
+            seg_out[(size_t)v * cols + tid] = a;
+        }
+        __syncthreads();
+    }
+}
+
+cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_stride, int ct_limbs,
+                             const uint64_t* sk, const uint64_t* sks, const int* sk_of, const uint64_t* pt,
+                             const uint64_t* pts, const int* pt_sel, int per_ct,
+                             int nvec, double inv_scale, const double* W, int seg_cols, uint64_t* M0, double* seg_out,
+                             cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    if (seg_cols < 1 || seg_cols > kMaxSegCols || c.L < 2) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
+    // one CTA per SM (the padded limb fills most of shared memory); M0 holds
+    // one limb per CTA
+    const int grid = nvec < c.sms ? nvec : c.sms;
+    TSG_LOGN_SWITCH(c.logn, {
+        cudaError_t er = ensure_smem(k_dec_fused<LG>, smem);
+        if (er != cudaSuccess) return er;
+        KScope ks("dec_fused", s);
+        k_dec_fused<LG><<<grid, NttCfg<LG>::NT, smem, s>>>(cts, ct_stride, ct_limbs, sk, sks, sk_of, pt, pts,
+                                                            pt_sel, per_ct, nvec, c.tabs, c.L, c.crt, inv_scale, W, seg_cols, M0,
+                                                            seg_out);
     });
     return cudaGetLastError();
 }

@@ -42,7 +42,7 @@ enum Stat : int {
 
 // CRT(q0, q1) constants of decrypt (ciphertext.rs:351-356).
 struct CrtConst {
-    uint64_t q0, q1, mu64_1, q0inv, bmu1;
+    uint64_t q0, q1, mu64_1, q0inv, q0inv_s, bmu1;  // q0inv_s: Shoup companion of q0^-1 mod q1
     int bk1;
     int pad;
     uint64_t Q_lo, Q_hi;  // q0*q1
@@ -51,6 +51,7 @@ struct CrtConst {
 
 struct DevCtx {
     int logn, n, L;
+    int sms;              // streaming multiprocessors of the context's device
     const LimbTab* tabs;  // device array [L]
     FftTab fft;
     double scale;         // Delta = 2^40 (params.rs:9-12)
@@ -104,12 +105,18 @@ cudaError_t launch_encode(const DevCtx& c, const SlotSrc& src, int nvec, int64_t
 // pt_ntt[v][L][n] = NTT(residues of m[v]) (ciphertext.rs:539-545).
 cudaError_t launch_ntt_signed(const DevCtx& c, uint64_t* out, const int64_t* m, int nvec, cudaStream_t s);
 
+// Shoup companions out[i] = floor(in[i] * 2^64 / q_l) of canonical
+// residues, for `polys` consecutive poly-limbs whose limb index is poly % L.
+cudaError_t launch_shoup_companion(const DevCtx& c, uint64_t* out, const uint64_t* in, long long polys,
+                                   cudaStream_t s);
+
 // Secret-key encryption of nvec vectors into ct[v][2][L][n]
-// (ciphertext.rs:167-229).  sk_of[v] selects the key (sk + sk_of[v]*L*n);
-// when plan_mode, only streams with flags[v] != 0 are (re)computed using
-// plans[v].
+// (ciphertext.rs:167-229).  sk_of[v] selects the key (sk + sk_of[v]*L*n,
+// Shoup companions at the same offset from sks); when plan_mode, only
+// streams with flags[v] != 0 are (re)computed using plans[v].
 cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m, const int8_t* e,
-                                 const uint64_t* sk, const int* sk_of, const uint64_t* seeds, int nvec,
+                                 const uint64_t* sk, const uint64_t* sks, const int* sk_of, const uint64_t* seeds,
+                                 int nvec,
                                  uint32_t* flags, const StreamPlan* plans, bool plan_mode, cudaStream_t s);
 
 // Flag buffers hold (2*count + 1) uint32: per-stream flags, the number of
@@ -129,8 +136,10 @@ cudaError_t launch_keygen_fix(const DevCtx& c, uint64_t* sk, const uint64_t* see
 // null, both components are first multiplied by pt + pt_of(v)*L*n
 // (ct x pt fused into decrypt; ciphertext.rs:408-429 then :327-349).
 // ct_of(v) = v / per_ct, pt_of(v) = (pt_sel ? pt_sel[v / per_ct] : 0)*per_ct + v % per_ct.
+// sks holds the keys' Shoup companions.
 cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uint64_t* cts, long long ct_stride,
-                                 int ct_limbs, const uint64_t* sk, const int* sk_of, const uint64_t* pt,
+                                 int ct_limbs, const uint64_t* sk, const uint64_t* sks, const int* sk_of,
+                                 const uint64_t* pt,
                                  const int* pt_sel, int per_ct, int nvec, cudaStream_t s);
 
 // Decrypt back half (ciphertext.rs:351-399 + encoding.rs:219-315): CRT of
@@ -140,6 +149,20 @@ cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uin
 cudaError_t launch_decode(const DevCtx& c, const uint64_t* M, int nl, bool crt, double scale, int nvec,
                           double* out_slots, double* seg_out, int seg_d, int seg_cols, double* scratch_cplx,
                           cudaStream_t s);
+
+// Fused decrypt side of the ZeRo-MOAI delta, one CTA per vector v (a
+// ciphertext-plaintext product): INTT of limbs 0 and 1 of
+// c0*p + (c1*p)*s = p*(c0 + c1*s), CRT to f64 / scale, and the segment sums
+// of the decoded slots as the linear functional seg[c] = sum_j coeff_j W[c][j]
+// (W[c][j] = sum over the segment's slots k of cos(pi j (2k+1) / N)).
+// sks / pts hold the Shoup companions of the keys / plaintexts.
+// Supports seg_cols <= kMaxSegCols; M0 is [min(nvec, sms)][n] u64 scratch.
+constexpr int kMaxSegCols = 10;
+cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_stride, int ct_limbs,
+                             const uint64_t* sk, const uint64_t* sks, const int* sk_of, const uint64_t* pt,
+                             const uint64_t* pts, const int* pt_sel, int per_ct,
+                             int nvec, double inv_scale, const double* W, int seg_cols, uint64_t* M0, double* seg_out,
+                             cudaStream_t s);
 
 // delta[i][d] = sum_k B[d][k] * inter[i][k] (inference_engine.py:1392).
 cudaError_t launch_bmat(const float* B, const double* inter, double* delta, int nvec, int d, int r,

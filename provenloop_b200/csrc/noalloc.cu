@@ -40,7 +40,7 @@ int noalloc_ctx(ts_ctx* c, int* device, const DevCtx** dc, cudaStream_t* stream,
                 std::mutex** mu);
 int noalloc_ct(const ts_ct* ct, const ts_ctx** owner, uint32_t* count, uint32_t* limbs, double* scale,
                const uint64_t** d);
-int noalloc_sk(const ts_sk* sk, const ts_ctx** owner, uint32_t* count, const uint64_t** d);
+int noalloc_sk(const ts_sk* sk, const ts_ctx** owner, uint32_t* count, const uint64_t** d, const uint64_t** ds);
 int noalloc_fail(int code, const char* msg);
 }  // namespace tsg_host
 
@@ -54,10 +54,10 @@ extern "C" int ts_decrypt_noalloc(ts_ctx* ctx, const ts_ct* ct, const ts_sk* sk,
     double scale = 0.0;
     std::mutex* mu = nullptr;
     const ts_ctx *ct_owner = nullptr, *sk_owner = nullptr;
-    const uint64_t *d_ct = nullptr, *d_sk = nullptr;
+    const uint64_t *d_ct = nullptr, *d_sk = nullptr, *d_sks = nullptr;
     noalloc_ctx(ctx, &device, &dc, &stream, &n, &slots, &mu);
     noalloc_ct(ct, &ct_owner, &count, &limbs, &scale, &d_ct);
-    noalloc_sk(sk, &sk_owner, &kcount, &d_sk);
+    noalloc_sk(sk, &sk_owner, &kcount, &d_sk, &d_sks);
     if (ct_owner != ctx || sk_owner != ctx)
         return noalloc_fail(TS_ERR_ARG, "ts_decrypt_noalloc: objects belong to another context");
     if (reinterpret_cast<uintptr_t>(out_dev) % 8)
@@ -94,7 +94,7 @@ extern "C" int ts_decrypt_noalloc(ts_ctx* ctx, const ts_ct* ct, const ts_sk* sk,
     }
     uint64_t* M = static_cast<uint64_t*>(base);
     double* fft = reinterpret_cast<double*>(static_cast<char*>(base) + m_bytes);
-    e = launch_decrypt_limbs(*dc, M, nl, d_ct, (long long)2 * limbs * n, (int)limbs, d_sk, nullptr, nullptr, nullptr, 1,
+    e = launch_decrypt_limbs(*dc, M, nl, d_ct, (long long)2 * limbs * n, (int)limbs, d_sk, d_sks, nullptr, nullptr, nullptr, 1,
                              (int)count, stream);
     if (e == cudaSuccess)
         e = launch_decode(*dc, M, nl, crt, scale, (int)count, out_dev, nullptr, 0, 0, fft, stream);

@@ -5,6 +5,7 @@
 // kernels.cu.  Parameter and table construction restates
 // tensafe-he-core/src/params.rs, rns.rs and encoding.rs (cited inline); all
 // per-ciphertext arithmetic runs on the GPU.
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -197,8 +198,11 @@ struct ts_ctx {
 struct ts_sk {
     ts_ctx* ctx;
     uint32_t count;
-    uint64_t* d;  // [count][L][n]
+    uint64_t* d;  // [count][L][n] residues, then [count][L][n] Shoup companions
 };
+
+// Shoup companions of a key set (floor(s * 2^64 / q_l) per coefficient).
+static const uint64_t* sk_shoup(const ts_sk* sk) { return sk->d + (size_t)sk->count * sk->ctx->L * sk->ctx->n; }
 
 struct ts_ct {
     ts_ctx* ctx;
@@ -216,8 +220,9 @@ struct ts_pt {
 struct ts_lora {
     ts_ctx* ctx;
     uint32_t experts, r, d, cols, batches;
-    uint64_t* d_pt;  // [experts][batches][L][n]
+    uint64_t* d_pt;  // [experts][batches][L][n] residues, then as many Shoup companions
     float* d_b;      // [experts][d][r]
+    double* d_w;     // [cols][n] segment functionals, or null (cols > kMaxSegCols)
 };
 
 namespace {
@@ -368,6 +373,7 @@ int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bit
         K.bmu1 = tabs[1].bmu;
         K.bk1 = tabs[1].bk;
         K.q0inv = powmod(q0 % q1, q1 - 2, q1);
+        K.q0inv_s = (uint64_t)(((u128)K.q0inv << 64) / q1);
         const u128 Q = (u128)q0 * q1;
         const u128 H = Q / 2;
         K.Q_lo = (uint64_t)Q;
@@ -413,6 +419,12 @@ int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bit
         return rc;
     }
     c->dc.logn = logn;
+    c->dc.sms = 148;
+    {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device) == cudaSuccess && sms > 0)
+            c->dc.sms = sms;
+    }
     c->dc.n = (int)n;
     c->dc.L = (int)L;
     c->dc.tabs = c->d_tabs;
@@ -477,7 +489,7 @@ EncWork enc_work(const Carve& cv, void* base, size_t cap, const size_t idx[5]) {
 // (SlotSrc), seeds / key indexes on the device, output ct [count][2][L][n].
 // Uses only the work buffers in `w` (callers own the scratch layout).
 int encrypt_core(ts_ctx* c, const SlotSrc& src, size_t count, const uint64_t* d_seeds, const int* d_skof,
-                 const uint64_t* d_sk, uint64_t* d_ct, const EncWork& w) {
+                 const uint64_t* d_sk, const uint64_t* d_sks, uint64_t* d_ct, const EncWork& w) {
     const size_t n = c->n;
     for (size_t v0 = 0; v0 < count; v0 += w.cap) {
         const size_t nv = count - v0 < w.cap ? count - v0 : w.cap;
@@ -488,11 +500,11 @@ int encrypt_core(ts_ctx* c, const SlotSrc& src, size_t count, const uint64_t* d_
         uint64_t* ct = d_ct + v0 * 2 * c->L * n;
         CU(cudaMemsetAsync(w.fl, 0, (2 * nv + 1) * 4, c->stream));
         CU(launch_encode(c->dc, s, (int)nv, w.m, w.e, seeds, 2ULL * c->L * n, w.f, c->stream));
-        CU(launch_encrypt_limbs(c->dc, ct, w.m, w.e, d_sk, skof, seeds, (int)nv, w.fl, w.pl, false, c->stream));
+        CU(launch_encrypt_limbs(c->dc, ct, w.m, w.e, d_sk, d_sks, skof, seeds, (int)nv, w.fl, w.pl, false, c->stream));
         // exact repair of the (rare) streams that met a rejection
         CU(launch_plan(c->dc, seeds, (int)nv, w.fl, w.pl, encrypt_segs(c->L), c->stream));
         CU(launch_gauss_fix(c->dc, w.e, seeds, (int)nv, w.fl, w.pl, (int)c->L, c->stream));
-        CU(launch_encrypt_limbs(c->dc, ct, w.m, w.e, d_sk, skof, seeds, (int)nv, w.fl, w.pl, true, c->stream));
+        CU(launch_encrypt_limbs(c->dc, ct, w.m, w.e, d_sk, d_sks, skof, seeds, (int)nv, w.fl, w.pl, true, c->stream));
     }
     return TS_OK;
 }
@@ -715,7 +727,7 @@ int ts_keygen_batch(ts_ctx* c, const uint64_t* seeds, uint32_t count, ts_sk** ou
     int rc = set_device(c);
     if (rc) return rc;
     ts_sk* sk = new ts_sk{c, count, nullptr};
-    rc = dev_alloc(c, (void**)&sk->d, (size_t)count * c->L * c->n * 8);
+    rc = dev_alloc(c, (void**)&sk->d, 2 * (size_t)count * c->L * c->n * 8);
     if (rc) {
         delete sk;
         return rc;
@@ -741,6 +753,9 @@ int ts_keygen_batch(ts_ctx* c, const uint64_t* seeds, uint32_t count, ts_sk** ou
         if (e == cudaSuccess) e = launch_keygen(c->dc, sk->d, ds, (int)count, fl, pl, c->stream);
         if (e == cudaSuccess) e = launch_plan(c->dc, ds, (int)count, fl, pl, segs, c->stream);
         if (e == cudaSuccess) e = launch_keygen_fix(c->dc, sk->d, ds, (int)count, fl, pl, c->stream);
+        if (e == cudaSuccess)
+            e = launch_shoup_companion(c->dc, sk->d + (size_t)count * c->L * c->n, sk->d, (long long)count * c->L,
+                                       c->stream);
         if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
         if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "keygen: %s", cudaGetErrorString(e));
     }
@@ -821,7 +836,7 @@ static int encrypt_impl(ts_ctx* c, const ts_sk* sk, const double* data, size_t c
         size_t idx[5];
         carve_enc(cv, cap, c->n, idx);
         rc = ensure_scratch(c, cv.total());
-        if (!rc) rc = encrypt_core(c, src, count, d_seeds, sk_index ? d_skof : nullptr, sk->d, ct->d,
+        if (!rc) rc = encrypt_core(c, src, count, d_seeds, sk_index ? d_skof : nullptr, sk->d, sk_shoup(sk), ct->d,
                                    enc_work(cv, c->scratch, cap, idx));
     }
     cudaFreeAsync(buf, c->stream);
@@ -910,7 +925,8 @@ int ts_ct_select(ts_ctx* c, const ts_ct* ct, uint32_t index, ts_ct** out) {
 }
 
 // ------------------------------------------------------------------ decrypt
-static int decrypt_core(ts_ctx* c, const ts_ct* ct, const uint64_t* d_sk, const int* d_skof, double* d_out) {
+static int decrypt_core(ts_ctx* c, const ts_ct* ct, const uint64_t* d_sk, const uint64_t* d_sks, const int* d_skof,
+                        double* d_out) {
     const size_t n = c->n;
     const bool crt = ct->scale > c->dc.scale * 1.5 && ct->limbs >= 2;  // ciphertext.rs:351
     const int nl = crt ? 2 : 1;
@@ -924,7 +940,7 @@ static int decrypt_core(ts_ctx* c, const ts_ct* ct, const uint64_t* d_sk, const 
         uint64_t* M = cv.at<uint64_t>(c->scratch, i_M);
         double* f = cv.at<double>(c->scratch, i_f);
         const long long stride = (long long)2 * ct->limbs * n;
-        CU(launch_decrypt_limbs(c->dc, M, nl, ct->d + v0 * stride, stride, (int)ct->limbs, d_sk,
+        CU(launch_decrypt_limbs(c->dc, M, nl, ct->d + v0 * stride, stride, (int)ct->limbs, d_sk, d_sks,
                                 d_skof ? d_skof + v0 : nullptr, nullptr, nullptr, 1, (int)nv, c->stream));
         CU(launch_decode(c->dc, M, nl, crt, ct->scale, (int)nv, d_out + v0 * c->slots, nullptr, 0, 0, f, c->stream));
     }
@@ -947,7 +963,7 @@ int ts_decrypt(ts_ctx* c, const ts_ct* ct, const ts_sk* sk, const int32_t* sk_in
     double* d_out = out_on_device ? out : static_cast<double*>(buf);
     int* d_skof = reinterpret_cast<int*>(static_cast<char*>(buf) + (out_on_device ? 0 : ((out_bytes + 255) & ~(size_t)255)));
     if (sk_index) rc = h2d_small(c, d_skof, (const int*)sk_index, ct->count);
-    if (!rc) rc = decrypt_core(c, ct, sk->d, sk_index ? d_skof : nullptr, d_out);
+    if (!rc) rc = decrypt_core(c, ct, sk->d, sk_shoup(sk), sk_index ? d_skof : nullptr, d_out);
     if (!rc && !out_on_device) {
         cudaError_t e = cudaMemcpyAsync(out, d_out, out_bytes, cudaMemcpyDeviceToHost, c->stream);
         if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "D2H: %s", cudaGetErrorString(e));
@@ -1161,14 +1177,42 @@ int ts_lora_load(ts_ctx* c, const float* A, const float* B, uint32_t experts, ui
                 for (uint32_t j = 0; j < d; j++) row[(size_t)i * d + j] = (double)a_row[j];
             }
         }
-    ts_lora* lo = new ts_lora{c, experts, r, d, cols, nb, nullptr, nullptr};
+    ts_lora* lo = new ts_lora{c, experts, r, d, cols, nb, nullptr, nullptr, nullptr};
     double* d_in = nullptr;
-    rc = dev_alloc(c, (void**)&lo->d_pt, (size_t)experts * nb * c->L * c->n * 8);
+    // Segment functionals of the decode (encoding.rs:295-315): slot k of a
+    // decoded polynomial is sum_j coeff_j cos(pi j (2k+1) / N), so the sum
+    // over segment c (slots c*d .. c*d+d-1) is sum_j coeff_j W[c][j] with
+    //   W[c][j] = sin(d t) cos(t (2 c d + d)) / sin(t),  t = pi j / N  (W[c][0] = d),
+    // evaluated in long double.
+    std::vector<double> W;
+    if (cols <= (uint32_t)kMaxSegCols && c->L >= 2) {
+        W.resize((size_t)cols * c->n);
+        const long double pi = 3.141592653589793238462643383279502884L;
+        for (uint32_t cc = 0; cc < cols; cc++)
+            for (uint32_t j = 0; j < c->n; j++) {
+                if (j == 0) {
+                    W[(size_t)cc * c->n] = (double)d;
+                    continue;
+                }
+                const long double t = pi * (long double)j / (long double)c->n;
+                W[(size_t)cc * c->n + j] =
+                    (double)(sinl((long double)d * t) * cosl(t * (long double)(2ULL * cc * d + d)) / sinl(t));
+            }
+    }
+    const size_t pt_words = (size_t)experts * nb * c->L * c->n;
+    rc = dev_alloc(c, (void**)&lo->d_pt, 2 * pt_words * 8);
     if (!rc) rc = dev_alloc(c, (void**)&lo->d_b, (size_t)experts * d * r * 4);
+    if (!rc && !W.empty()) rc = dev_alloc(c, (void**)&lo->d_w, W.size() * 8);
+    if (!rc && !W.empty()) rc = h2d_small(c, lo->d_w, W.data(), W.size());
     if (!rc) rc = dev_alloc(c, (void**)&d_in, packed.size() * 8);
     if (!rc) rc = h2d_small(c, d_in, packed.data(), packed.size());
     if (!rc) rc = h2d_small(c, lo->d_b, B, (size_t)experts * d * r);
     if (!rc) rc = encode_ntt_core(c, d_in, (size_t)experts * nb, c->slots, c->slots, lo->d_pt);
+    if (!rc) {
+        cudaError_t e = launch_shoup_companion(c->dc, lo->d_pt + pt_words, lo->d_pt, (long long)experts * nb * c->L,
+                                               c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "lora_load: %s", cudaGetErrorString(e));
+    }
     if (d_in) cudaFreeAsync(d_in, c->stream);
     if (!rc) {
         cudaError_t e = cudaStreamSynchronize(c->stream);
@@ -1177,6 +1221,7 @@ int ts_lora_load(ts_ctx* c, const float* A, const float* B, uint32_t experts, ui
     if (rc) {
         if (lo->d_pt) cudaFreeAsync(lo->d_pt, c->stream);
         if (lo->d_b) cudaFreeAsync(lo->d_b, c->stream);
+        if (lo->d_w) cudaFreeAsync(lo->d_w, c->stream);
         delete lo;
         return rc;
     }
@@ -1190,6 +1235,7 @@ int ts_lora_destroy(ts_lora* lo) {
     cudaSetDevice(lo->ctx->device);
     cudaFreeAsync(lo->d_pt, lo->ctx->stream);
     cudaFreeAsync(lo->d_b, lo->ctx->stream);
+    if (lo->d_w) cudaFreeAsync(lo->d_w, lo->ctx->stream);
     delete lo;
     return TS_OK;
 }
@@ -1220,7 +1266,8 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
     int rc = set_device(c);
     if (rc) return rc;
     const size_t N = c->n, L = c->L, d = lo->d, r = lo->r, cols = lo->cols, nb = lo->batches;
-    const size_t CH = 512;
+    // deltas per pass: large enough that every kernel's grid spans many waves
+    const size_t CH = 2048;
     const double scale2 = c->dc.scale * c->dc.scale;
     // small per-delta inputs: staged once through pinned memory (async H2D)
     const size_t sm_bytes = (size_t)n * 8 + (size_t)n * 4 * 2 + 512;
@@ -1248,8 +1295,10 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
                      i_ct = cv.add(nv * 2 * L * N * 8), i_m = cv.add(nv * N * 8), i_e = cv.add(nv * N),
                      i_fe = cv.add(nv * 2 * N * 8), i_fl = cv.add((2 * nv + 1) * 4),
                      i_pl = cv.add(nv * sizeof(StreamPlan)),
-                     i_M = cv.add(nv * nb * 2 * N * 8), i_fd = cv.add(nv * nb * 2 * N * 8),
-                     i_sg = cv.add(nv * nb * cols * 8);
+                     // fused decrypt: one limb-0 buffer per CTA; otherwise both limbs of
+                     // every vector and the FFT scratch of the decode
+                     i_M = cv.add(lo->d_w ? std::min(nv * nb, (size_t)c->dc.sms) * N * 8 : nv * nb * 2 * N * 8),
+                     i_fd = cv.add(lo->d_w ? 0 : nv * nb * 2 * N * 8), i_sg = cv.add(nv * nb * cols * 8);
         rc = ensure_scratch(c, cv.total());
         if (rc) break;
         void* S = c->scratch;
@@ -1268,13 +1317,25 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         // 1. encrypt the cols-fold replicated hidden states (:1267-1272)
         SlotSrc src{dh, 0, (int)d, (long long)d, (int)d, (int)cols};
         const size_t eidx[5] = {i_m, i_e, i_fe, i_fl, i_pl};
-        rc = encrypt_core(c, src, nv, ds, sk_index ? dsk : nullptr, sk->d, ct, enc_work(cv, S, nv, eidx));
+        rc = encrypt_core(c, src, nv, ds, sk_index ? dsk : nullptr, sk->d, sk_shoup(sk), ct,
+                          enc_work(cv, S, nv, eidx));
         if (rc) break;
-        // 2. ct x packed_pt (limbs 0/1) fused with decrypt's c0 + c1*s, INTT (:1311-1315)
-        CU(launch_decrypt_limbs(c->dc, M, 2, ct, (long long)2 * L * N, (int)L, sk->d, sk_index ? dsk : nullptr,
-                                lo->d_pt, expert ? dex : nullptr, (int)nb, (int)(nv * nb), c->stream));
-        // 3. CRT, / Delta^2, canonical embedding, segment sums (:1382-1386)
-        CU(launch_decode(c->dc, M, 2, true, scale2, (int)(nv * nb), nullptr, sg, (int)d, (int)cols, fd, c->stream));
+        if (lo->d_w) {
+            // 2+3. per (delta, batch): ct x packed_pt (limbs 0/1), c0 + c1*s, INTT,
+            // CRT / Delta^2 and the segment sums of the decoded slots (:1311-1386)
+            CU(launch_dec_fused(c->dc, ct, (long long)2 * L * N, (int)L, sk->d, sk_shoup(sk), sk_index ? dsk : nullptr,
+                                lo->d_pt, lo->d_pt + (size_t)lo->experts * nb * L * N,
+                                expert ? dex : nullptr, (int)nb, (int)(nv * nb), 1.0 / scale2, lo->d_w, (int)cols, M,
+                                sg, c->stream));
+        } else {
+            // 2. ct x packed_pt (limbs 0/1) fused with decrypt's c0 + c1*s, INTT (:1311-1315)
+            CU(launch_decrypt_limbs(c->dc, M, 2, ct, (long long)2 * L * N, (int)L, sk->d, sk_shoup(sk),
+                                    sk_index ? dsk : nullptr,
+                                    lo->d_pt, expert ? dex : nullptr, (int)nb, (int)(nv * nb), c->stream));
+            // 3. CRT, / Delta^2, canonical embedding, segment sums (:1382-1386)
+            CU(launch_decode(c->dc, M, 2, true, scale2, (int)(nv * nb), nullptr, sg, (int)d, (int)cols, fd,
+                             c->stream));
+        }
         CU(launch_gather_inter(sg, dinter, (int)nv, (int)nb, (int)cols, (int)r, c->stream));
         // 4. delta = B @ intermediate (:1392)
         CU(launch_bmat(lo->d_b, dinter, dout, (int)nv, (int)d, (int)r, expert ? dex : nullptr, (long long)d * r,
@@ -1344,10 +1405,11 @@ int noalloc_ct(const ts_ct* ct, const ts_ctx** owner, uint32_t* count, uint32_t*
     *d = ct->d;
     return TS_OK;
 }
-int noalloc_sk(const ts_sk* sk, const ts_ctx** owner, uint32_t* count, const uint64_t** d) {
+int noalloc_sk(const ts_sk* sk, const ts_ctx** owner, uint32_t* count, const uint64_t** d, const uint64_t** ds) {
     *owner = sk->ctx;
     *count = sk->count;
     *d = sk->d;
+    *ds = sk_shoup(sk);
     return TS_OK;
 }
 int noalloc_fail(int code, const char* msg) { return fail(code, "%s", msg); }

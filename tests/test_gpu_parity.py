@@ -188,6 +188,30 @@ def test_encrypt_batch_mixed_keys_and_rejections(T, ctx16, octx16):
         assert np.array_equal(c0, o0) and np.array_equal(c1, o1), i
 
 
+# 61-bit NTT primes just below 2^61 * (1 - 2e-4): 2^64 mod q is 2e-4 of 2^64,
+# so range_u64 rejects one draw in 5000 and every N = 16384 limb segment
+# holds a few rejections at scattered positions.
+DENSE_REJECT = [2305381840610885633, 2305381840610426881]
+
+
+def test_encrypt_dense_rejections(T, oracle):
+    """Every stream needs the exact repair (more flagged streams than repair
+    CTAs), with several rejections per limb anywhere in the segment."""
+    ctx = T.CkksContext.from_moduli(16384, DENSE_REJECT)
+    o = oracle.Ctx(16384, DENSE_REJECT)
+    rng = np.random.default_rng(14)
+    X = rng.standard_normal((24, 2000))
+    seeds = list(range(1000, 1024))
+    ct = ctx.encrypt_batch(X, ctx.keygen_batch([5]), seeds)
+    osk = o.keygen(5)
+    for i in range(24):
+        c0, c1 = ct.export(i)
+        o0, o1, _ = o.encrypt(X[i], osk, seed=seeds[i])
+        assert np.array_equal(c1, o1) and np.array_equal(c0, o0), i
+    st = ctx.stats()
+    assert st["streams_repaired"] >= 20 and st["plan_overflow"] == 0
+
+
 def test_encrypt_n8192_reject(T, oracle):
     ctx = T.CkksContext(8192)
     o = oracle.Ctx(8192)
@@ -311,6 +335,25 @@ def test_lora_delta_batch_experts_and_users(T, ctx16, octx16):
     osks = [octx16.keygen(0), octx16.keygen(1)]
     for i in range(6):
         od, oi = octx16.lora_delta(osks[ski[i]], H[i], A[expert[i]], B[expert[i]], enc_seed=seeds[i])
+        assert np.abs(delta[i] - od).max() < 1e-4, i
+        assert np.abs(inter[i] - oi).max() < 1e-8, i
+
+
+def test_lora_delta_more_vectors_than_sms(T, ctx16, octx16):
+    """80 users x 4 batches = 320 (delta, batch) vectors: the fused decrypt
+    kernel's CTAs each take two or three of them."""
+    from provenloop_b200.backend import ZeroMoaiLora
+    rng = np.random.default_rng(12)
+    r, d, n = 16, 1536, 80
+    A = (rng.standard_normal((r, d)) * 0.02).astype(np.float32)
+    B = (rng.standard_normal((d, r)) * 0.02).astype(np.float32)
+    H = rng.standard_normal((n, d))
+    seeds = list(range(500, 500 + n))
+    lora = ZeroMoaiLora(ctx16, A, B)
+    delta, inter = lora.delta(ctx16.keygen(4), H, seeds)
+    osk = octx16.keygen(4)
+    for i in range(n):
+        od, oi = octx16.lora_delta(osk, H[i], A, B, enc_seed=seeds[i])
         assert np.abs(delta[i] - od).max() < 1e-4, i
         assert np.abs(inter[i] - oi).max() < 1e-8, i
 

@@ -215,6 +215,10 @@ def run_reference(args):
 #   decode_b      per (ct, batch):       read 16N
 #   encode_a      per ct:                write 16N (+ d*8 read)
 #   encode_b      per ct:                read 16N, write m (8N) + e (N) = 25N
+#   dec_fused     per delta:             the decrypt side of the compulsory-traffic model:
+#                                        read ct limbs 0-1 (4 x 8N) + s limbs 0-1 (2 x 8N)
+#                                        + NTT(pt) limbs 0-1 per batch (2B x 8N), write
+#                                        B*cols segment sums = 8N(6 + 2B) + 8*B*cols
 #   ntt_*         per poly-limb:         read 8N + write 8N = 16N
 def kernel_bytes_per_delta(name: str, L: int = 4, nb: int = 4) -> float:
     n = N_POLY
@@ -226,6 +230,7 @@ def kernel_bytes_per_delta(name: str, L: int = 4, nb: int = 4) -> float:
         "decode_b": 16 * n * nb,
         "encode_a": 16 * n + D * 8,
         "encode_b": 25 * n,
+        "dec_fused": 8 * n * (6 + 2 * nb) + 8 * nb * 5,
     }
     return float(table.get(name, 0))
 
@@ -353,7 +358,9 @@ def run_ours(args):
         roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
                 "measured" else "fallback 6650 GB/s", "traffic": traffic,
-                "algorithmic_bytes_per_launch": total_bytes / n, "avg_launch_ms": ms / n}
+                "algorithmic_bytes_per_launch": total_bytes / n, "avg_launch_ms": ms / n,
+                "note": "integer-issue bound (64-bit modular NTT on the IMAD pipe): see "
+                        "profiles/ncu_delta_kernels_b148.md"}
 
     micro = None
     if rank == 0 and not args.no_micro:

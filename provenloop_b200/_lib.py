@@ -12,7 +12,8 @@ import threading
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libtsgpu.so")
+# TSGPU_LIBRARY selects another build of the same ABI (e.g. an instrumented one)
+LIB_PATH = os.environ.get("TSGPU_LIBRARY") or os.path.join(HERE, "libtsgpu.so")
 
 TS_OK = 0
 TS_ERR_ARG = -1

@@ -93,9 +93,12 @@ __device__ __forceinline__ uint64_t mod_u64(uint64_t x, uint64_t q, uint64_t mu6
 // (encoding.rs:198-202, ciphertext.rs:196-201): v >= 0 -> v % q, else
 // q - ((-v) % q).  The negative branch yields q (not 0) when q | v, which
 // the reference also does.
+// Branch-free, so that callers' loads are not serialised behind divergent
+// branches.
 __device__ __forceinline__ uint64_t signed_residue(int64_t v, uint64_t q, uint64_t mu64) {
-    if (v >= 0) return mod_u64((uint64_t)v, q, mu64);
-    return q - mod_u64((uint64_t)0 - (uint64_t)v, q, mu64);
+    const bool neg = v < 0;
+    const uint64_t r = mod_u64(neg ? (uint64_t)0 - (uint64_t)v : (uint64_t)v, q, mu64);
+    return neg ? q - r : r;
 }
 
 // ----------------------------------------------------------------- ChaCha20
@@ -175,18 +178,21 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
 // ----------------------------------------------------------------- u128 -> f64
 // Round-to-nearest-even conversion of the 128-bit integer (hi, lo), as Rust's
 // `u128 as f64` (used by the CRT branch of decrypt, ciphertext.rs:379-383).
+// Branch-free: both the hi == 0 and the general result are formed and one
+// is selected.
 __device__ __forceinline__ double u128_to_f64(uint64_t hi, uint64_t lo) {
-    if (hi == 0) return __ull2double_rn(lo);
-    int lz = __clzll((long long)hi);
-    int nbits = 128 - lz;
-    uint64_t top = lz ? ((hi << lz) | (lo >> (64 - lz))) : hi;
-    uint64_t rest = lz ? (lo << lz) : lo;
+    const int lz = __clzll((long long)hi) & 63;  // (hi == 0 selects the other result)
+    const int nbits = 128 - lz;
+    const uint64_t top = lz ? ((hi << lz) | (lo >> (64 - lz))) : hi;
+    const uint64_t rest = lz ? (lo << lz) : lo;
     uint64_t mant = top >> 11;
-    uint64_t rbit = (top >> 10) & 1;
-    bool sticky = ((top & 0x3FF) != 0) || (rest != 0);
-    if (rbit && (sticky || (mant & 1))) mant++;
+    const uint64_t rbit = (top >> 10) & 1;
+    const bool sticky = ((top & 0x3FF) != 0) || (rest != 0);
+    mant += (rbit && (sticky || (mant & 1))) ? 1 : 0;
     // mant < 2^54; scale by 2^(nbits-53) (exact)
-    return __dmul_rn(__ull2double_rn(mant), __longlong_as_double((long long)(1023 + nbits - 53) << 52));
+    const double big =
+        __dmul_rn(__ull2double_rn(mant), __longlong_as_double((long long)(1023 + nbits - 53) << 52));
+    return hi ? big : __ull2double_rn(lo);
 }
 
 // Rust `f64 as i64` (saturating, NaN -> 0).

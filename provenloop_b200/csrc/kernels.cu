@@ -884,12 +884,11 @@ __device__ __forceinline__ double crt_coeff(uint64_t m0, uint64_t m1, const CrtC
     hi += (lo < m0) ? 1 : 0;
     // (the reference's "mu >= Q -> mu % Q" branch cannot trigger: mu < Q)
     const bool neg = (hi > K.H_hi) || (hi == K.H_hi && lo > K.H_lo);
-    if (neg) {
-        const uint64_t dlo = K.Q_lo - lo;
-        const uint64_t dhi = K.Q_hi - hi - (K.Q_lo < lo ? 1 : 0);
-        return -u128_to_f64(dhi, dlo);
-    }
-    return u128_to_f64(hi, lo);
+    // |mu - Q| for the negative half, selected without a branch
+    const uint64_t dlo = K.Q_lo - lo;
+    const uint64_t dhi = K.Q_hi - hi - (K.Q_lo < lo ? 1 : 0);
+    const double mag = u128_to_f64(neg ? dhi : hi, neg ? dlo : lo);
+    return neg ? -mag : mag;
 }
 
 template <int LOGN>
@@ -1003,7 +1002,9 @@ cudaError_t launch_decode(const DevCtx& c, const uint64_t* M, int nl, bool crt, 
 // (ciphertext.rs:408-429, :327-399; encoding.rs:295-315;
 //  inference_engine.py:1382-1386)
 // ======================================================================
-template <int LOGN>
+// NC0 / NC1: correction-free INTT for limb 0 / limb 1 (chosen by the host
+// from the moduli, so each instantiation holds only two transforms).
+template <int LOGN, bool NC0, bool NC1>
 __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     k_dec_fused(const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs, const uint64_t* __restrict__ sk,
                 const uint64_t* __restrict__ sks, const int* __restrict__ sk_of, const uint64_t* __restrict__ pt,
@@ -1036,13 +1037,12 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
             const uint64_t* sp = sks + (key << LOGN);
             const uint64_t* p = pt + ((size_t)pv * L << LOGN);
             const uint64_t* pp = pts + ((size_t)pv * L << LOGN);
-            ntt_inverse_block<LOGN>(
-                sm, T,
-                [&](int j) {
-                    // p*(c0 + c1*s): c0 + c1*s < 5q, the product lies in [0, 4q)
-                    return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q);
-                },
-                [&](int j, uint64_t x) { m0v[j] = x; });
+            // p*(c0 + c1*s): c0 + c1*s < 5q, the product lies in [0, 4q)
+            auto ld = [&](int j) {
+                return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q);
+            };
+            auto st = [&](int j, uint64_t x) { m0v[j] = x; };
+            ntt_inverse_impl<LOGN, NC0>(sm, T, ld, st);
         }
         __syncthreads();
         // phase 2: limb 1; the last pass parks element j in sm[pad(j)], a
@@ -1055,26 +1055,32 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
             const uint64_t* sp = sks + ((key + 1) << LOGN);
             const uint64_t* p = pt + (((size_t)pv * L + 1) << LOGN);
             const uint64_t* pp = pts + (((size_t)pv * L + 1) << LOGN);
-            ntt_inverse_block<LOGN>(
-                sm, T,
-                [&](int j) {
-                    // p*(c0 + c1*s): c0 + c1*s < 5q, the product lies in [0, 4q)
-                    return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q);
-                },
-                [&](int j, uint64_t x) { sm[pad(j)] = x; });
+            auto ld = [&](int j) {
+                return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q);
+            };
+            auto st = [&](int j, uint64_t x) { sm[pad(j)] = x; };
+            ntt_inverse_impl<LOGN, NC1>(sm, T, ld, st);
         }
         // CRT, / Delta^2 and the segment functionals over this thread's
         // elements j = tid + k * NT
         double acc[kMaxSegCols];
 #pragma unroll
         for (int c = 0; c < kMaxSegCols; c++) acc[c] = 0.0;
-#pragma unroll 4
-        for (int k = 0; k < N / NT; k++) {
-            const int j = tid + k * NT;
-            const double coeff = __dmul_rn(crt_coeff(m0v[j], sm[pad(j)], K), inv_scale);
+        // limb-0 loads issued in groups of 8 ahead of their arithmetic
+        constexpr int G = 8;
+#pragma unroll 1
+        for (int k0 = 0; k0 < N / NT; k0 += G) {
+            uint64_t m0r[G];
 #pragma unroll
-            for (int c = 0; c < kMaxSegCols; c++)
-                if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
+            for (int kk = 0; kk < G; kk++) m0r[kk] = m0v[tid + (k0 + kk) * NT];
+#pragma unroll
+            for (int kk = 0; kk < G; kk++) {
+                const int j = tid + (k0 + kk) * NT;
+                const double coeff = __dmul_rn(crt_coeff(m0r[kk], sm[pad(j)], K), inv_scale);
+#pragma unroll
+                for (int c = 0; c < kMaxSegCols; c++)
+                    if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
+            }
         }
         // deterministic block reduction of acc[0 .. cols)
         __syncthreads();
@@ -1108,11 +1114,15 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
     // one CTA per SM (the padded limb fills most of shared memory); M0 holds
     // one limb per CTA
     const int grid = nvec < c.sms ? nvec : c.sms;
+    // correction-free INTT where the modulus leaves the headroom (as in ntt_inverse_block)
+    const bool nc0 = c.q0 < (1ULL << (61 - c.logn)), nc1 = c.q1 < (1ULL << (61 - c.logn));
     TSG_LOGN_SWITCH(c.logn, {
-        cudaError_t er = ensure_smem(k_dec_fused<LG>, smem);
+        auto kern = nc0 ? (nc1 ? k_dec_fused<LG, true, true> : k_dec_fused<LG, true, false>)
+                        : (nc1 ? k_dec_fused<LG, false, true> : k_dec_fused<LG, false, false>);
+        cudaError_t er = ensure_smem(kern, smem);
         if (er != cudaSuccess) return er;
         KScope ks("dec_fused", s);
-        k_dec_fused<LG><<<grid, NttCfg<LG>::NT, smem, s>>>(cts, ct_stride, ct_limbs, sk, sks, sk_of, pt, pts,
+        kern<<<grid, NttCfg<LG>::NT, smem, s>>>(cts, ct_stride, ct_limbs, sk, sks, sk_of, pt, pts,
                                                             pt_sel, per_ct, nvec, c.tabs, c.L, c.crt, inv_scale, W, seg_cols, M0,
                                                             seg_out);
     });

@@ -52,6 +52,7 @@ struct CrtConst {
 struct DevCtx {
     int logn, n, L;
     int sms;              // streaming multiprocessors of the context's device
+    uint64_t q0, q1;      // moduli of limbs 0 and 1 (host copies, for kernel selection)
     const LimbTab* tabs;  // device array [L]
     FftTab fft;
     double scale;         // Delta = 2^40 (params.rs:9-12)

@@ -25,8 +25,11 @@
 // Butterflies: Harvey-style lazy reduction with Shoup twiddle products whose
 // quotient comes from three 32x32 partial products (remainder in [0, 4q));
 // values stay in [0, 8q) forward and [0, 4q) inverse, which needs q < 2^61
-// (the reference's primes are <= 60 bits).  Each twiddle and its companion
-// are one 16-byte load.  N^-1 is folded into the last inverse stage.
+// (the reference's primes are <= 60 bits).  Inverse transforms of limbs
+// with headroom (q < 2^(61 - log2 N), the 40-bit primes) skip the per-stage
+// corrections entirely (the NC variants below).
+// Each twiddle and its companion are one 16-byte load.  N^-1 is folded into
+// the last inverse stage.
 #pragma once
 #include "common.cuh"
 
@@ -104,7 +107,10 @@ __device__ __forceinline__ void smem_store(uint64_t* sm, const uint64_t* v, int 
 // One forward CT stage (sub-stage r of a radix-2^R pass starting at stage
 // S0) on the 2^R values x of set-group g.  Template recursion keeps every
 // loop bound a compile-time constant so x stays in registers.
-template <int R, int S0, int r>
+// NC ("no correction") drops the X >= 4q step: each stage then adds at most
+// 4q to the bound, so inputs < 8q stay below 8q + 4q*LOGN <= 64q, which fits
+// 64 bits for q < 2^57 (the 40/50-bit limbs).
+template <int R, int S0, int r, bool NC>
 __device__ __forceinline__ void fwd_stage(uint64_t* x, int g, const ulonglong2* __restrict__ fw, uint64_t q,
                                           uint64_t q4) {
     constexpr int half = 1 << (R - 1 - r);
@@ -115,32 +121,38 @@ __device__ __forceinline__ void fwd_stage(uint64_t* x, int g, const ulonglong2* 
         for (int kk = 0; kk < half; kk++) {
             const int k = gi * 2 * half + kk;
             uint64_t X = x[k];
-            X = X >= q4 ? X - q4 : X;                                 // [0, 4q)
+            if constexpr (!NC) X = X >= q4 ? X - q4 : X;             // [0, 4q)
             const uint64_t T = mul_shoup4(x[k + half], w.x, w.y, q);  // [0, 4q)
-            x[k] = X + T;                                             // [0, 8q)
-            x[k + half] = X + q4 - T;                                 // (0, 8q)
+            x[k] = X + T;                                             // [0, 8q) (NC: bound + 4q)
+            x[k + half] = X + q4 - T;                                 // (0, 8q) (NC: bound + 4q)
         }
     }
-    if constexpr (r + 1 < R) fwd_stage<R, S0, r + 1>(x, g, fw, q, q4);
+    if constexpr (r + 1 < R) fwd_stage<R, S0, r + 1, NC>(x, g, fw, q, q4);
 }
 
-template <int LOGN, int R, int S0>
+template <int LOGN, int R, int S0, bool NC>
 __device__ __forceinline__ void fwd_compute(uint64_t* v, const ulonglong2* __restrict__ fw, uint64_t q, int tid) {
     constexpr int TLOG = LOGN - S0 - R;
     using G = Geo<LOGN, R, TLOG>;
 #pragma unroll
-    for (int u = 0; u < G::SETS; u++) fwd_stage<R, S0, 0>(v + u * (1 << R), G::sigma(tid, u) >> TLOG, fw, q, 4 * q);
+    for (int u = 0; u < G::SETS; u++)
+        fwd_stage<R, S0, 0, NC>(v + u * (1 << R), G::sigma(tid, u) >> TLOG, fw, q, 4 * q);
 }
 
 // One inverse GS stage (span 2^(TLOG+r)) on values in [0, 4q); the stage of
 // span N/2 folds N^-1 into both outputs.
-template <int LOGN, int R, int TLOG, int r>
+// NC drops the X + Y >= 4q step: the bound then doubles per stage, from 4q
+// before global stage 0 to 4q * 2^s before stage s, and the difference
+// branch adds that bound instead of 4q.  Everything stays below 2^64 for
+// q < 2^(61 - LOGN) (the 40-bit limbs).
+template <int LOGN, int R, int TLOG, int r, bool NC>
 __device__ __forceinline__ void inv_stage(uint64_t* x, int g, const ulonglong2* __restrict__ iw, const LimbTab& T,
                                           uint64_t q4) {
     constexpr int span = 1 << r;
     constexpr int m = 1 << (LOGN - TLOG - r - 1);
     constexpr bool last = (TLOG + r == LOGN - 1);
     const uint64_t q = T.q;
+    const uint64_t off = NC ? q4 << (TLOG + r) : q4;  // bound of the inputs of this stage
 #pragma unroll
     for (int gi = 0; gi < ((1 << R) >> (r + 1)); gi++) {
         ulonglong2 w;
@@ -156,22 +168,24 @@ __device__ __forceinline__ void inv_stage(uint64_t* x, int g, const ulonglong2* 
             const uint64_t X = x[k], Y = x[k + span];
             if constexpr (last) {
                 x[k] = mul_shoup4(X + Y, T.ninv, T.ninvs, q);
+            } else if constexpr (NC) {
+                x[k] = X + Y;
             } else {
                 const uint64_t s = X + Y;
                 x[k] = s >= q4 ? s - q4 : s;
             }
-            x[k + span] = mul_shoup4(X + q4 - Y, w.x, w.y, q);
+            x[k + span] = mul_shoup4(X + off - Y, w.x, w.y, q);
         }
     }
-    if constexpr (r + 1 < R) inv_stage<LOGN, R, TLOG, r + 1>(x, g, iw, T, q4);
+    if constexpr (r + 1 < R) inv_stage<LOGN, R, TLOG, r + 1, NC>(x, g, iw, T, q4);
 }
 
-template <int LOGN, int R, int TLOG>
+template <int LOGN, int R, int TLOG, bool NC>
 __device__ __forceinline__ void inv_compute(uint64_t* v, const ulonglong2* __restrict__ iw, const LimbTab& T, int tid) {
     using G = Geo<LOGN, R, TLOG>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++)
-        inv_stage<LOGN, R, TLOG, 0>(v + u * (1 << R), G::sigma(tid, u) >> TLOG, iw, T, 4 * T.q);
+        inv_stage<LOGN, R, TLOG, 0, NC>(v + u * (1 << R), G::sigma(tid, u) >> TLOG, iw, T, 4 * T.q);
 }
 
 // [0, 8q) -> [0, q)
@@ -190,7 +204,7 @@ __device__ __forceinline__ uint64_t canon4(uint64_t x, uint64_t q) {
 // Forward pass P (stages fwd_s0(P) ..) and the ones after it.  Pass 0's
 // values are already in v; every pass stores its results back to the
 // positions it read (its own sets), so one barrier between passes suffices.
-template <int LOGN, int P>
+template <int LOGN, int P, bool NC>
 __device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulonglong2* fw, uint64_t q, int tid) {
     using C = NttCfg<LOGN>;
     constexpr int R = C::fwd_r(P), S0 = C::fwd_s0(P), TLOG = LOGN - S0 - R;
@@ -198,9 +212,9 @@ __device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulon
         __syncthreads();
         smem_load<LOGN, R, TLOG>(sm, v, tid);
     }
-    fwd_compute<LOGN, R, S0>(v, fw, q, tid);
+    fwd_compute<LOGN, R, S0, NC>(v, fw, q, tid);
     smem_store<LOGN, R, TLOG>(sm, v, tid);
-    if constexpr (P + 1 < C::NPASS) fwd_passes<LOGN, P + 1>(sm, v, fw, q, tid);
+    if constexpr (P + 1 < C::NPASS) fwd_passes<LOGN, P + 1, NC>(sm, v, fw, q, tid);
 }
 
 // Forward transform of one poly-limb.  ld(j) returns element j (< 8q, e.g.
@@ -209,8 +223,8 @@ __device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulon
 // threads of the block must call this; a caller that reuses `sm` afterwards
 // must __syncthreads() first.  If ld reads `sm`, each thread may only read
 // the positions pad(tid + k*NT) (its own first-pass elements).
-template <int LOGN, class Ld, class St>
-__device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
+template <int LOGN, bool NC, class Ld, class St>
+__device__ __forceinline__ void ntt_forward_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
     using C = NttCfg<LOGN>;
     static_assert(LOGN >= 10 && LOGN <= 14, "single-CTA NTT supports N in [1024, 16384]");
     static_assert(C::fwd_r(0) == C::RMAX, "the first pass takes RMAX stages");
@@ -220,29 +234,37 @@ __device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T
     // first pass: one set per thread, elements tid + k*NT
 #pragma unroll
     for (int k = 0; k < C::E; k++) v[k] = ld(tid + k * C::NT);
-    fwd_passes<LOGN, 0>(sm, v, fw, T.q, tid);
+    fwd_passes<LOGN, 0, NC>(sm, v, fw, T.q, tid);
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < C::E; k++) {
         const int j = tid + k * C::NT;
-        st(j, canon8(sm[pad(j)], T.q));
+        st(j, NC ? mod_u64(sm[pad(j)], T.q, T.mu64) : canon8(sm[pad(j)], T.q));
     }
+}
+
+// Forward transform.  The correction-free variant (NC) measured no faster
+// here: the forward butterfly is bound by the IMAD pipe, not by the ALU
+// instructions NC removes, so every limb uses the corrected butterflies.
+template <int LOGN, class Ld, class St>
+__device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
+    ntt_forward_impl<LOGN, false>(sm, T, ld, st);
 }
 
 // Inverse pass P in GS order (spans 1 .. N/2) mirrors forward pass
 // NPASS-1-P.  Its values are in shared memory on entry; the last pass keeps
 // its results (elements tid + k*NT) in v.
-template <int LOGN, int P>
+template <int LOGN, int P, bool NC>
 __device__ __forceinline__ void inv_passes(uint64_t* sm, uint64_t* v, const ulonglong2* iw, const LimbTab& T, int tid) {
     using C = NttCfg<LOGN>;
     constexpr int FP = C::NPASS - 1 - P;
     constexpr int R = C::fwd_r(FP), TLOG = LOGN - C::fwd_s0(FP) - R;
     __syncthreads();
     smem_load<LOGN, R, TLOG>(sm, v, tid);
-    inv_compute<LOGN, R, TLOG>(v, iw, T, tid);
+    inv_compute<LOGN, R, TLOG, NC>(v, iw, T, tid);
     if constexpr (P + 1 < C::NPASS) {
         smem_store<LOGN, R, TLOG>(sm, v, tid);
-        inv_passes<LOGN, P + 1>(sm, v, iw, T, tid);
+        inv_passes<LOGN, P + 1, NC>(sm, v, iw, T, tid);
     }
 }
 
@@ -250,8 +272,8 @@ __device__ __forceinline__ void inv_passes(uint64_t* sm, uint64_t* v, const ulon
 // element j (< 4q) for j = tid + k*NT, st(j, v) receives canonical output j
 // in the same coalesced order.  A caller that reuses `sm` afterwards must
 // __syncthreads() first.
-template <int LOGN, class Ld, class St>
-__device__ __forceinline__ void ntt_inverse_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
+template <int LOGN, bool NC, class Ld, class St>
+__device__ __forceinline__ void ntt_inverse_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
     using C = NttCfg<LOGN>;
     static_assert(LOGN >= 10 && LOGN <= 14, "single-CTA NTT supports N in [1024, 16384]");
     const int tid = threadIdx.x;
@@ -262,9 +284,19 @@ __device__ __forceinline__ void ntt_inverse_block(uint64_t* sm, const LimbTab& T
         const int j = tid + k * C::NT;
         sm[pad(j)] = ld(j);
     }
-    inv_passes<LOGN, 0>(sm, v, iw, T, tid);
+    inv_passes<LOGN, 0, NC>(sm, v, iw, T, tid);
 #pragma unroll
     for (int k = 0; k < C::E; k++) st(tid + k * C::NT, canon4(v[k], T.q));
+}
+
+// Inverse transform, with the correction-free butterflies when
+// 4q * 2^LOGN * 2 fits 64 bits (a uniform branch per CTA).
+template <int LOGN, class Ld, class St>
+__device__ __forceinline__ void ntt_inverse_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
+    if (T.q < (1ULL << (61 - LOGN)))
+        ntt_inverse_impl<LOGN, true>(sm, T, ld, st);
+    else
+        ntt_inverse_impl<LOGN, false>(sm, T, ld, st);
 }
 
 }  // namespace tsg

@@ -125,6 +125,21 @@ int ts_encrypt_batch(ts_ctx* ctx, const ts_sk* sk, const double* data, size_t co
  * the arrays in order (the i-th array starts where the (i-1)-th stopped). */
 int ts_encrypt_stream(ts_ctx* ctx, const ts_sk* sk, const double* data, size_t count, size_t len, size_t stride,
                       uint64_t seed, ts_ct** out);
+/* Public-key path.  CkksContext::keygen_public (ciphertext.rs:114-154;
+ * lib.rs:102-110): pk = (b, a) with a uniform and b = -a*s + e, both NTT
+ * domain, from TenSafeRng::from_seed(seed); key sk_index of sk. */
+int ts_keygen_public(ts_ctx* ctx, const ts_sk* sk, uint32_t sk_index, uint64_t seed, ts_pk** out);
+int ts_pk_destroy(ts_pk* pk);
+/* Copy b and a ([L][n] each, NTT domain) to host memory (either may be NULL). */
+int ts_pk_export(const ts_pk* pk, uint64_t* b_host, uint64_t* a_host);
+/* CkksContext::encrypt_pk (ciphertext.rs:240-319; lib.rs:142-164), batched:
+ * `count` vectors (row stride `stride`), independent seeds[i];
+ * c0 = b*u + m + e0, c1 = a*u + e1. */
+int ts_encrypt_pk(ts_ctx* ctx, const ts_pk* pk, const double* data, size_t count, size_t len, size_t stride,
+                  const uint64_t* seeds, int data_on_device, ts_ct** out);
+/* CkksContext::rescale (ciphertext.rs:476-535; lib.rs:218-225): drop the last
+ * limb, dividing by its modulus; scale / q_last.  TS_ERR_ARG with 1 limb. */
+int ts_rescale(ts_ctx* ctx, const ts_ct* ct, ts_ct** out);
 int ts_ct_destroy(ts_ct* ct);
 int ts_ct_info(const ts_ct* ct, uint32_t* count, uint32_t* num_limbs, double* scale);
 /* Copy ciphertext `index` to host: c0, c1 [num_limbs][n] (either may be NULL). */

@@ -62,6 +62,11 @@ SIGNATURES = {
     "ts_encrypt": (cint, [vp, vp, P(f64), sz, u64, pvp]),
     "ts_encrypt_batch": (cint, [vp, vp, vp, sz, sz, sz, P(u64), P(i32), cint, pvp]),
     "ts_encrypt_stream": (cint, [vp, vp, P(f64), sz, sz, sz, u64, pvp]),
+    "ts_keygen_public": (cint, [vp, vp, u32, u64, pvp]),
+    "ts_pk_destroy": (cint, [vp]),
+    "ts_pk_export": (cint, [vp, P(u64), P(u64)]),
+    "ts_encrypt_pk": (cint, [vp, vp, vp, sz, sz, sz, P(u64), cint, pvp]),
+    "ts_rescale": (cint, [vp, vp, pvp]),
     "ts_ct_destroy": (cint, [vp]),
     "ts_ct_info": (cint, [vp, P(u32), P(u32), P(f64)]),
     "ts_ct_export": (cint, [vp, u32, P(u64), P(u64)]),

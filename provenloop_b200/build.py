@@ -54,15 +54,20 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return LIB
     nvcc = nvcc_path()
     objs = []
+    procs = []
+    # the sources compile in parallel; --split-compile spreads the device
+    # optimisation of the large kernel file over the host's cores
     for s in SOURCES:
         obj = os.path.join(CSRC, s.replace(".cu", ".o"))
-        cmd = [nvcc, "-c", os.path.join(CSRC, s), "-o", obj] + flags(verbose)
-        r = subprocess.run(cmd, capture_output=True, text=True)
-        if r.returncode != 0:
-            raise RuntimeError(f"nvcc failed for {s}:\n{r.stdout}\n{r.stderr}")
-        if verbose:
-            sys.stdout.write(r.stdout + r.stderr)
+        cmd = [nvcc, "-c", os.path.join(CSRC, s), "-o", obj, "--split-compile=0"] + flags(verbose)
+        procs.append((s, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
         objs.append(obj)
+    for s, p in procs:
+        out, err = p.communicate()
+        if p.returncode != 0:
+            raise RuntimeError(f"nvcc failed for {s}:\n{out}\n{err}")
+        if verbose:
+            sys.stdout.write(out + err)
     tmp = LIB + ".tmp"
     cmd = [nvcc, "-shared", "-o", tmp] + objs + ["-gencode", "arch=compute_100a,code=sm_100a", "-lcudart"]
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -199,8 +199,39 @@ bool prof_read(const char* name, double* ms, uint64_t* launches) {
         case 12: { constexpr int LG = 12; __VA_ARGS__; } break;   \
         case 13: { constexpr int LG = 13; __VA_ARGS__; } break;   \
         case 14: { constexpr int LG = 14; __VA_ARGS__; } break;   \
+        case 15: { constexpr int LG = 15; __VA_ARGS__; } break;   \
         default: return cudaErrorInvalidValue;                    \
     }
+
+// Launch of an NTT kernel whose transforms span `cl` CTAs along x: a plain
+// launch for cl = 1, a cluster launch (cluster dimension cl along x) else.
+template <class... KArgs, class... Args>
+cudaError_t launch_cl(int cl, void (*kern)(KArgs...), dim3 grid, unsigned block, size_t smem, cudaStream_t s,
+                      Args... args) {
+    if (cl == 1) {
+        kern<<<grid, block, smem, s>>>(args...);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(block, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = (unsigned)cl;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Shared-memory bytes of one NTT CTA (its padded share of a poly-limb).
+template <int LOGN>
+constexpr size_t ntt_smem_bytes() {
+    return (size_t)NttCfg<LOGN>::SMEM_WORDS * 8;
+}
 
 // ======================================================================
 // Plain batched NTT / INTT (ntt.rs:79-141)
@@ -209,7 +240,7 @@ template <int LOGN, bool INV>
 __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     k_ntt(uint64_t* __restrict__ data, const LimbTab* __restrict__ tabs, int lmod, int l0) {
     extern __shared__ __align__(16) uint64_t sm[];
-    const long long p = blockIdx.x;
+    const long long p = blockIdx.x / NttCfg<LOGN>::CL;
     const LimbTab T = tabs[l0 + (int)(p % lmod)];
     uint64_t* a = data + (p << LOGN);
     auto ld = [&](int j) { return a[j]; };
@@ -222,13 +253,14 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
 
 cudaError_t launch_ntt(const DevCtx& c, uint64_t* data, long long P, int lmod, int l0, bool inverse, cudaStream_t s) {
     if (P <= 0) return cudaSuccess;
-    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
+        constexpr size_t smem = ntt_smem_bytes<LG>();
+        constexpr int CL = NttCfg<LG>::CL;
         auto kern = inverse ? k_ntt<LG, true> : k_ntt<LG, false>;
         cudaError_t e = ensure_smem(kern, smem);
         if (e != cudaSuccess) return e;
         KScope ks(inverse ? "ntt_inverse" : "ntt_forward", s);
-        kern<<<(unsigned)P, NttCfg<LG>::NT, smem, s>>>(data, c.tabs, lmod, l0);
+        return launch_cl(CL, kern, dim3((unsigned)(P * CL)), NttCfg<LG>::NT, smem, s, data, c.tabs, lmod, l0);
     });
     return cudaGetLastError();
 }
@@ -291,63 +323,71 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     k_keygen(uint64_t* __restrict__ sk, const uint64_t* __restrict__ seeds, const LimbTab* __restrict__ tabs, int L,
              int nkeys, uint32_t* flags, const StreamPlan* __restrict__ plans, int plan_mode) {
     extern __shared__ __align__(16) uint64_t sm[];
-    constexpr int N = 1 << LOGN, NT = NttCfg<LOGN>::NT;
-    const int limb = blockIdx.x, tid = threadIdx.x;
+    using C = NttCfg<LOGN>;
+    constexpr int NT = C::NT, H = C::H;
+    const int limb = blockIdx.x / C::CL, tid = threadIdx.x;
+    const int h0 = ntt_rank<LOGN>() * H;  // first element of this CTA's share
     const LimbTab T = tabs[limb];
     const int nwork = plan_mode ? (int)flags[nkeys] : 1;
     for (int it = blockIdx.y; it < (plan_mode ? nwork : (int)blockIdx.y + 1); it += gridDim.y) {
         const int key = plan_mode ? (int)flags[nkeys + 1 + it] : it;
         const uint64_t seed = seeds[key];
         if (!plan_mode) {
-            // word i = sample i; block b holds samples 16b .. 16b+15
+            // word i = sample i; block b holds samples 16b .. 16b+15 (this
+            // CTA draws the blocks of its share)
             bool rej = false;
-            for (int b = tid; b < N / 16; b += NT) {
+            for (int b = h0 / 16 + tid; b < (h0 + H) / 16; b += NT) {
                 uint32_t w[16];
                 chacha_block(seed, (uint32_t)b, w);
 #pragma unroll
                 for (int c = 0; c < 16; c++) {
                     rej |= (w[c] == 0u);  // range_u32(3) threshold is 1 (rng.rs:112)
-                    sm[pad(16 * b + c)] = ternary_coeff(w[c], T.q);
+                    sm[pad(16 * b + c - h0)] = ternary_coeff(w[c], T.q);
                 }
             }
             if (rej && limb == 0) flag_stream(flags, nkeys, key);
         } else {
             const StreamPlan& P = plans[key];
-            for (int i = tid; i < N; i += NT) {
+            for (int i = h0 + tid; i < h0 + H; i += NT) {
                 const uint32_t ci = cand_index((uint32_t)i, P.rej[0], P.nrej[0]);
-                sm[pad(i)] = ternary_coeff(chacha_word(seed, P.off[0] + ci), T.q);
+                sm[pad(i - h0)] = ternary_coeff(chacha_word(seed, P.off[0] + ci), T.q);
             }
         }
-        __syncthreads();
+        if constexpr (C::CL == 2) cluster_sync();  // the transform reads both shares
+        else __syncthreads();
         uint64_t* out = sk + (((size_t)key * L + limb) << LOGN);
+        const SmemView<LOGN> in = ntt_smem_view<LOGN>(sm);
         ntt_forward_block<LOGN>(
-            sm, T, [&](int j) { return sm[pad(j)]; }, [&](int j, uint64_t x) { out[j] = x; });
+            sm, T, [&](int j) { return in(j); }, [&](int j, uint64_t x) { out[j] = x; });
         __syncthreads();
     }
 }
 
 cudaError_t launch_keygen(const DevCtx& c, uint64_t* sk, const uint64_t* seeds, int nkeys, uint32_t* flags,
                           StreamPlan* plans, cudaStream_t s) {
-    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
+        constexpr size_t smem = ntt_smem_bytes<LG>();
+        constexpr int CL = NttCfg<LG>::CL;
         cudaError_t e = ensure_smem(k_keygen<LG>, smem);
         if (e != cudaSuccess) return e;
         KScope ks("keygen", s);
-        k_keygen<LG><<<dim3(c.L, nkeys), NttCfg<LG>::NT, smem, s>>>(sk, seeds, c.tabs, c.L, nkeys, flags, plans, 0);
+        return launch_cl(CL, k_keygen<LG>, dim3(c.L * CL, nkeys), NttCfg<LG>::NT, smem, s, sk, seeds, c.tabs, c.L,
+                         nkeys, flags, plans, 0);
     });
     return cudaGetLastError();
 }
 
 cudaError_t launch_keygen_fix(const DevCtx& c, uint64_t* sk, const uint64_t* seeds, int nkeys, const uint32_t* flags,
                               const StreamPlan* plans, cudaStream_t s) {
-    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
+        constexpr size_t smem = ntt_smem_bytes<LG>();
+        constexpr int CL = NttCfg<LG>::CL;
         cudaError_t e = ensure_smem(k_keygen<LG>, smem);
         if (e != cudaSuccess) return e;
         KScope ks("keygen_fix", s);
         const int gy = nkeys < 8 ? nkeys : 8;
-        k_keygen<LG><<<dim3(c.L, gy), NttCfg<LG>::NT, smem, s>>>(sk, seeds, c.tabs, c.L, nkeys,
-                                                                   const_cast<uint32_t*>(flags), plans, 1);
+        return launch_cl(CL, k_keygen<LG>, dim3(c.L * CL, gy), NttCfg<LG>::NT, smem, s, sk, seeds, c.tabs, c.L, nkeys,
+                         const_cast<uint32_t*>(flags), plans, 1);
     });
     return cudaGetLastError();
 }
@@ -644,7 +684,7 @@ template <int LOGN>
 __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     k_ntt_signed(uint64_t* __restrict__ out, const int64_t* __restrict__ m, const LimbTab* __restrict__ tabs, int L) {
     extern __shared__ __align__(16) uint64_t sm[];
-    const int limb = blockIdx.x, v = blockIdx.y;
+    const int limb = blockIdx.x / NttCfg<LOGN>::CL, v = blockIdx.y;
     const LimbTab T = tabs[limb];
     const int64_t* mv = m + ((size_t)v << LOGN);
     uint64_t* o = out + (((size_t)v * L + limb) << LOGN);
@@ -654,12 +694,13 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
 
 cudaError_t launch_ntt_signed(const DevCtx& c, uint64_t* out, const int64_t* m, int nvec, cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
-    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
+        constexpr size_t smem = ntt_smem_bytes<LG>();
+        constexpr int CL = NttCfg<LG>::CL;
         cudaError_t e = ensure_smem(k_ntt_signed<LG>, smem);
         if (e != cudaSuccess) return e;
         KScope ks("ntt_signed", s);
-        k_ntt_signed<LG><<<dim3(c.L, nvec), NttCfg<LG>::NT, smem, s>>>(out, m, c.tabs, c.L);
+        return launch_cl(CL, k_ntt_signed<LG>, dim3(c.L * CL, nvec), NttCfg<LG>::NT, smem, s, out, m, c.tabs, c.L);
     });
     return cudaGetLastError();
 }
@@ -717,8 +758,10 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     k_enc_a(uint64_t* __restrict__ ct, const uint64_t* __restrict__ seeds, const LimbTab* __restrict__ tabs, int L,
             int nvec, uint32_t* flags, const StreamPlan* __restrict__ plans, int plan_mode) {
     extern __shared__ __align__(16) uint64_t sm[];
-    constexpr int N = 1 << LOGN, NT = NttCfg<LOGN>::NT;
-    const int limb = blockIdx.x, tid = threadIdx.x;
+    using C = NttCfg<LOGN>;
+    constexpr int N = 1 << LOGN, NT = C::NT, H = C::H;
+    const int limb = blockIdx.x / C::CL, tid = threadIdx.x;
+    const int h0 = ntt_rank<LOGN>() * H;  // first element of this CTA's share
     const LimbTab T = tabs[limb];
     const int nwork = plan_mode ? (int)flags[nvec] : 1;
     for (int it = blockIdx.y; it < (plan_mode ? nwork : (int)blockIdx.y + 1); it += gridDim.y) {
@@ -726,16 +769,17 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
         const uint64_t seed = seeds[v];
         uint64_t* c1 = ct + (((size_t)v * 2 * L + L + limb) << LOGN);
         if (!plan_mode) {
+            // this CTA's share: candidates h0 .. h0 + H - 1, 8 per block
             const uint32_t blk0 = (uint32_t)limb * (N / 8);
             bool rej = false;
-            for (int b = tid; b < N / 8; b += NT) {
+            for (int b = h0 / 8 + tid; b < (h0 + H) / 8; b += NT) {
                 uint32_t w[16];
                 chacha_block(seed, blk0 + (uint32_t)b, w);
 #pragma unroll
                 for (int c = 0; c < 8; c++) {
                     const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
                     rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
-                    sm[pad(8 * b + c)] = mod_u64(u, T.q, T.mu64);
+                    sm[pad(8 * b + c - h0)] = mod_u64(u, T.q, T.mu64);
                 }
             }
             if (rej) flag_stream(flags, nvec, v);
@@ -764,17 +808,20 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
                         before += rej[t] < cidx;
                         rejected |= rej[t] == cidx;
                     }
-                    if (!rejected) {
+                    const int i = (int)(cidx - before);
+                    if (!rejected && i >= h0 && i < h0 + H) {  // outputs of this CTA's share
                         const int o = sh + 2 * cl;
                         const uint64_t u = (uint64_t)win[o] | ((uint64_t)win[o + 1] << 32);
-                        sm[pad((int)(cidx - before))] = mod_u64(u, T.q, T.mu64);
+                        sm[pad(i - h0)] = mod_u64(u, T.q, T.mu64);
                     }
                 }
             }
         }
-        __syncthreads();
+        if constexpr (C::CL == 2) cluster_sync();  // the transform reads both shares
+        else __syncthreads();
+        const SmemView<LOGN> in = ntt_smem_view<LOGN>(sm);
         ntt_forward_block<LOGN>(
-            sm, T, [&](int j) { return sm[pad(j)]; }, [&](int j, uint64_t x) { c1[j] = x; });
+            sm, T, [&](int j) { return in(j); }, [&](int j, uint64_t x) { c1[j] = x; });
         __syncthreads();
     }
 }
@@ -786,7 +833,9 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
             const LimbTab* __restrict__ tabs, int L,
             int nvec, const uint32_t* __restrict__ flags, int list_mode) {
     extern __shared__ __align__(16) uint64_t sm[];
-    const int limb = blockIdx.x;
+    using C = NttCfg<LOGN>;
+    const int limb = blockIdx.x / C::CL;
+    const int h0 = ntt_rank<LOGN>() * C::H;
     const LimbTab T = tabs[limb];
     const int nwork = list_mode ? (int)flags[nvec] : 1;
     for (int it = blockIdx.y; it < (list_mode ? nwork : (int)blockIdx.y + 1); it += gridDim.y) {
@@ -798,7 +847,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
         const uint64_t* sp = sks + so;
         const int64_t* mv = m + ((size_t)v << LOGN);
         const int8_t* ev = e + ((size_t)v << LOGN);
-        if (threadIdx.x == 0) prefetch_l2(c1, 1u << (LOGN + 3));  // read by the epilogue
+        if (threadIdx.x == 0) prefetch_l2(c1 + h0, (unsigned)C::H * 8u);  // this CTA's share, read by the epilogue
         ntt_forward_block<LOGN>(
             sm, T,
             [&](int j) {
@@ -819,8 +868,9 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
                                  const uint64_t* sks, const int* sk_of, const uint64_t* seeds, int nvec, uint32_t* flags,
                                  const StreamPlan* plans, bool plan_mode, cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
-    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
+        constexpr size_t smem = ntt_smem_bytes<LG>();
+        constexpr int CL = NttCfg<LG>::CL;
         const size_t smem_a = plan_mode ? smem + kEncPlanWinBytes : smem;
         cudaError_t er = ensure_smem(k_enc_a<LG>, smem + kEncPlanWinBytes);
         if (er != cudaSuccess) return er;
@@ -829,13 +879,133 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
         const int gy = plan_mode ? (nvec < 16 ? nvec : 16) : nvec;
         {
             KScope ks(plan_mode ? "enc_a_fix" : "enc_a", s);
-            k_enc_a<LG><<<dim3(c.L, gy), NttCfg<LG>::NT, smem_a, s>>>(ct, seeds, c.tabs, c.L, nvec, flags, plans,
-                                                                       plan_mode ? 1 : 0);
+            er = launch_cl(CL, k_enc_a<LG>, dim3(c.L * CL, gy), NttCfg<LG>::NT, smem_a, s, ct, seeds, c.tabs, c.L, nvec,
+                           flags, plans, plan_mode ? 1 : 0);
+            if (er != cudaSuccess) return er;
         }
         KScope ks(plan_mode ? "enc_u_fix" : "enc_u", s);
-        k_enc_u<LG><<<dim3(c.L, gy), NttCfg<LG>::NT, smem, s>>>(ct, m, e, sk, sks, sk_of, c.tabs, c.L, nvec, flags,
-                                                                 plan_mode ? 1 : 0);
+        return launch_cl(CL, k_enc_u<LG>, dim3(c.L * CL, gy), NttCfg<LG>::NT, smem, s, ct, m, e, sk, sks, sk_of, c.tabs,
+                         c.L, nvec, (const uint32_t*)flags, plan_mode ? 1 : 0);
     });
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// Public-key encryption (ciphertext.rs:240-319): c0 = b*u + NTT(m + e0),
+// c1 = a*u + NTT(e1), with u = NTT(ternary) computed by the key-generation
+// kernel from the same stream (the reference's u mapping composed with its
+// ternary sampler equals keygen's: draw 0 -> 1, 1 -> q-1, 2 -> 0).
+// ======================================================================
+// Gaussian samples j = 4b .. 4b+3 of vector v from words off + 16b (off a
+// multiple of 16): one ChaCha block per thread.
+__global__ void k_gauss_gen(int8_t* __restrict__ e, const uint64_t* __restrict__ seeds, int N, uint64_t off,
+                            unsigned long long* stats) {
+    const int v = blockIdx.y;
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    int ties = 0;
+    if (b < N / 4) {
+        uint32_t w[16];
+        chacha_block(seeds[v], (uint32_t)((off >> 4) + (uint64_t)b), w);
+        char4 o;
+        bool tie;
+        o.x = (signed char)gaussian_round((uint64_t)w[0] | ((uint64_t)w[1] << 32),
+                                          (uint64_t)w[2] | ((uint64_t)w[3] << 32), 3.19, &tie);
+        ties += tie;
+        o.y = (signed char)gaussian_round((uint64_t)w[4] | ((uint64_t)w[5] << 32),
+                                          (uint64_t)w[6] | ((uint64_t)w[7] << 32), 3.19, &tie);
+        ties += tie;
+        o.z = (signed char)gaussian_round((uint64_t)w[8] | ((uint64_t)w[9] << 32),
+                                          (uint64_t)w[10] | ((uint64_t)w[11] << 32), 3.19, &tie);
+        ties += tie;
+        o.w = (signed char)gaussian_round((uint64_t)w[12] | ((uint64_t)w[13] << 32),
+                                          (uint64_t)w[14] | ((uint64_t)w[15] << 32), 3.19, &tie);
+        ties += tie;
+        reinterpret_cast<char4*>(e + (size_t)v * N)[b] = o;
+    }
+    if (ties && stats) atomicAdd(stats + STAT_NEAR_TIE, (unsigned long long)ties);
+}
+
+cudaError_t launch_gauss_gen(const DevCtx& c, int8_t* e, const uint64_t* seeds, int nvec, uint64_t off,
+                             cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    if (off & 15) return cudaErrorInvalidValue;
+    KScope ks("gauss_gen", s);
+    k_gauss_gen<<<dim3((c.n / 4 + 255) / 256, nvec), 256, 0, s>>>(e, seeds, c.n, off, c.stats);
+    return cudaGetLastError();
+}
+
+// Component comp = blockIdx.z of ciphertext v, limb blockIdx.x / CL.
+template <int LOGN>
+__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+    k_enc_pk(uint64_t* __restrict__ ct, const int64_t* __restrict__ m, const int8_t* __restrict__ e0,
+             const int8_t* __restrict__ e1, const uint64_t* __restrict__ U, const uint64_t* __restrict__ pk,
+             const uint64_t* __restrict__ pks, const LimbTab* __restrict__ tabs, int L) {
+    extern __shared__ __align__(16) uint64_t sm[];
+    const int limb = blockIdx.x / NttCfg<LOGN>::CL, v = blockIdx.y, comp = blockIdx.z;
+    const LimbTab T = tabs[limb];
+    uint64_t* out = ct + (((size_t)v * 2 * L + (size_t)comp * L + limb) << LOGN);
+    // pk layout [2][L][n]: b then a; u of this vector and limb
+    const uint64_t* P = pk + (((size_t)(comp ? L : 0) + limb) << LOGN);
+    const uint64_t* Ps = pks + (((size_t)(comp ? L : 0) + limb) << LOGN);
+    const uint64_t* u = U + (((size_t)v * L + limb) << LOGN);
+    const int64_t* mv = m + ((size_t)v << LOGN);
+    const int8_t* ev = (comp ? e1 : e0) + ((size_t)v << LOGN);
+    ntt_forward_block<LOGN>(
+        sm, T,
+        [&](int j) {
+            // |e| < q: the reference's residue of a negative e is q + e
+            const int ej = ev[j];
+            const uint64_t er = ej >= 0 ? (uint64_t)ej : T.q + ej;
+            return comp ? er : add_mod(signed_residue(mv[j], T.q, T.mu64), er, T.q);
+        },
+        [&](int j, uint64_t x) { out[j] = canon8(x + mul_shoup4(u[j], P[j], Ps[j], T.q), T.q); });
+}
+
+cudaError_t launch_enc_pk(const DevCtx& c, uint64_t* ct, const int64_t* m, const int8_t* e0, const int8_t* e1,
+                          const uint64_t* U, const uint64_t* pk, const uint64_t* pks, int nvec, cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    TSG_LOGN_SWITCH(c.logn, {
+        constexpr size_t smem = ntt_smem_bytes<LG>();
+        constexpr int CL = NttCfg<LG>::CL;
+        cudaError_t er = ensure_smem(k_enc_pk<LG>, smem);
+        if (er != cudaSuccess) return er;
+        KScope ks("enc_pk", s);
+        return launch_cl(CL, k_enc_pk<LG>, dim3(c.L * CL, nvec, 2), NttCfg<LG>::NT, smem, s, ct, m, e0, e1, U, pk, pks,
+                         c.tabs, c.L);
+    });
+    return cudaGetLastError();
+}
+
+// ======================================================================
+// Rescale (ciphertext.rs:476-535), coefficient-domain step: for limbs
+// l < nl-1 of both components, (x_l - (x_last mod q_l)) * q_last^-1 mod q_l.
+// ======================================================================
+__global__ void k_rescale_combine(uint64_t* __restrict__ out, const uint64_t* __restrict__ in, int nl, int logn,
+                                  long long total, const LimbTab* __restrict__ tabs, RescaleInv inv) {
+    const int n = 1 << logn;
+    for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
+         t += (long long)gridDim.x * blockDim.x) {
+        // t indexes out [count][2][nl-1][n]
+        const int i = (int)(t & (n - 1));
+        const long long pl = t >> logn;
+        const int l = (int)(pl % (nl - 1));
+        const long long vc = pl / (nl - 1);  // vector * 2 + component
+        const LimbTab& T = tabs[l];
+        const uint64_t x = in[((vc * nl + l) << logn) + i];
+        const uint64_t y = mod_u64(in[((vc * nl + nl - 1) << logn) + i], T.q, T.mu64);
+        const uint64_t d = x >= y ? x - y : T.q - y + x;
+        out[t] = mul_barrett(d, inv.v[l], T.q, T.bmu, T.bk);
+    }
+}
+
+cudaError_t launch_rescale_combine(const DevCtx& c, uint64_t* out, const uint64_t* in, int count, int nl,
+                                   const RescaleInv& inv, cudaStream_t s) {
+    if (count <= 0 || nl < 2) return cudaErrorInvalidValue;
+    const long long total = (long long)count * 2 * (nl - 1) << c.logn;
+    const long long blocks = (total + 255) / 256;
+    KScope ks("rescale", s);
+    k_rescale_combine<<<(int)(blocks < 8 * 148 ? blocks : 8 * 148), 256, 0, s>>>(out, in, nl, c.logn, total, c.tabs,
+                                                                                 inv);
     return cudaGetLastError();
 }
 
@@ -849,14 +1019,14 @@ constexpr int kPlanCand = 4;
 constexpr int kPlanWin = kPlanCand * 1024 * 2 + 16;
 
 __device__ void plan_one(const uint64_t* __restrict__ seeds, int v, StreamPlan* plans, const SegList& segs,
-                         const LimbTab* __restrict__ tabs, int N, unsigned long long* stats, int tid) {
+                         const LimbTab* __restrict__ tabs, int N, unsigned long long* stats, int tid, uint64_t base) {
     __shared__ uint32_t s_nrej;
     __shared__ uint32_t s_rej[kMaxRej + 1];
     __shared__ uint32_t s_overflow;
     __shared__ __align__(16) uint32_t win[kPlanWin];
     StreamPlan& P = plans[v];
     const uint64_t seed = seeds[v];
-    uint64_t off = 0;
+    uint64_t off = base;  // first word of this stream's segments
     if (tid == 0) s_overflow = 0;
     for (int sg = 0; sg < segs.count; sg++) {
         const int kind = segs.kind[sg];
@@ -939,19 +1109,22 @@ __device__ void plan_one(const uint64_t* __restrict__ seeds, int v, StreamPlan* 
 
 __global__ void __launch_bounds__(1024, 1)
     k_plan(const uint64_t* __restrict__ seeds, int nstreams, const uint32_t* __restrict__ flags, StreamPlan* plans,
-           SegList segs, const LimbTab* __restrict__ tabs, int N, unsigned long long* stats) {
+           SegList segs, const LimbTab* __restrict__ tabs, int N, unsigned long long* stats,
+           const uint64_t* __restrict__ bases) {
     const int tid = threadIdx.x;
     const int nwork = (int)flags[nstreams];
     for (int it = blockIdx.x; it < nwork; it += gridDim.x) {
-        plan_one(seeds, (int)flags[nstreams + 1 + it], plans, segs, tabs, N, stats, tid);
+        const int v = (int)flags[nstreams + 1 + it];
+        plan_one(seeds, v, plans, segs, tabs, N, stats, tid, bases ? bases[v] : 0);
     }
 }
 
 cudaError_t launch_plan(const DevCtx& c, const uint64_t* seeds, int nstreams, const uint32_t* flags, StreamPlan* plans,
-                        const SegList& segs, cudaStream_t s) {
+                        const SegList& segs, cudaStream_t s, const uint64_t* bases) {
     if (nstreams <= 0) return cudaSuccess;
     KScope ks("plan", s);
-    k_plan<<<nstreams < 32 ? nstreams : 32, 1024, 0, s>>>(seeds, nstreams, flags, plans, segs, c.tabs, c.n, c.stats);
+    k_plan<<<nstreams < 32 ? nstreams : 32, 1024, 0, s>>>(seeds, nstreams, flags, plans, segs, c.tabs, c.n, c.stats,
+                                                          bases);
     return cudaGetLastError();
 }
 
@@ -1009,7 +1182,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
                    const uint64_t* __restrict__ pt, const int* __restrict__ pt_sel, int per_ct,
                    const LimbTab* __restrict__ tabs, int L) {
     extern __shared__ __align__(16) uint64_t sm[];
-    const int limb = blockIdx.x, v = blockIdx.y;
+    const int limb = blockIdx.x / NttCfg<LOGN>::CL, v = blockIdx.y;
     const LimbTab T = tabs[limb];
     const int ci = v / per_ct;
     const uint64_t* c0 = cts + (size_t)ci * ct_stride + ((size_t)limb << LOGN);
@@ -1041,13 +1214,14 @@ cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uin
                                  int ct_limbs, const uint64_t* sk, const uint64_t* sks, const int* sk_of,
                                  const uint64_t* pt, const int* pt_sel, int per_ct, int nvec, cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
-    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
     TSG_LOGN_SWITCH(c.logn, {
+        constexpr size_t smem = ntt_smem_bytes<LG>();
+        constexpr int CL = NttCfg<LG>::CL;
         cudaError_t er = ensure_smem(k_decrypt_limb<LG>, smem);
         if (er != cudaSuccess) return er;
         KScope ks("decrypt_limb", s);
-        k_decrypt_limb<LG><<<dim3(nl, nvec), NttCfg<LG>::NT, smem, s>>>(M, nl, cts, ct_stride, ct_limbs, sk, sks, sk_of,
-                                                                        pt, pt_sel, per_ct, c.tabs, c.L);
+        return launch_cl(CL, k_decrypt_limb<LG>, dim3(nl * CL, nvec), NttCfg<LG>::NT, smem, s, M, nl, cts, ct_stride,
+                         ct_limbs, sk, sks, sk_of, pt, pt_sel, per_ct, c.tabs, c.L);
     });
     return cudaGetLastError();
 }
@@ -1191,22 +1365,26 @@ template <int LOGN, bool NC0, bool NC1>
 __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     k_dec_fused(const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs, const uint64_t* __restrict__ sk,
                 const uint64_t* __restrict__ sks, const int* __restrict__ sk_of, const uint64_t* __restrict__ pt,
-                const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel, int per_ct, int nvec, const LimbTab* __restrict__ tabs, int L, CrtConst K, double inv_scale,
-                const double* __restrict__ W, int cols, uint64_t* __restrict__ M0, double* __restrict__ seg_out) {
+                const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel, int per_ct, int nvec,
+                const LimbTab* __restrict__ tabs, int L, CrtConst K, double inv_scale, const double* __restrict__ W,
+                int cols, uint64_t* __restrict__ M0, double* __restrict__ seg_out) {
     extern __shared__ __align__(16) uint64_t sm[];
-    constexpr int N = 1 << LOGN, NT = NttCfg<LOGN>::NT;
+    using C = NttCfg<LOGN>;
+    constexpr int N = C::N, NT = C::NT, CL = C::CL;
     const int tid = threadIdx.x;
-    // persistent: one limb-0 buffer per CTA, reused for every vector it
-    // takes, so the round trip stays in L2
+    // persistent over transform groups (one CTA, or a cluster pair for
+    // CL = 2); each CTA keeps one limb-0 buffer, reused for every vector,
+    // so the round trip stays in L2
+    const int grp = blockIdx.x / CL, ngrp = gridDim.x / CL;
     uint64_t* m0v = M0 + ((size_t)blockIdx.x << LOGN);
-    for (int v = blockIdx.x; v < nvec; v += gridDim.x) {
+    for (int v = grp; v < nvec; v += ngrp) {
         const int ci = v / per_ct;
         const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
         const size_t key = (size_t)(sk_of ? sk_of[ci] : 0) * L;
         const uint64_t* ctb = cts + (size_t)ci * ct_stride;
-        if (tid == 0 && v + (int)gridDim.x < nvec) {
+        if (tid == 0 && v + ngrp < nvec) {
             // limbs 0-1 of both components of the next vector's ciphertext
-            const uint64_t* nx = cts + (size_t)((v + gridDim.x) / per_ct) * ct_stride;
+            const uint64_t* nx = cts + (size_t)((v + ngrp) / per_ct) * ct_stride;
             prefetch_l2(nx, 2u << (LOGN + 3));
             prefetch_l2(nx + ((size_t)ct_limbs << LOGN), 2u << (LOGN + 3));
         }
@@ -1228,8 +1406,10 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
             ntt_inverse_impl<LOGN, NC0>(sm, T, ld, st);
         }
         __syncthreads();
-        // phase 2: limb 1; the last pass parks element j in sm[pad(j)], a
-        // slot only this thread reads or writes from then on
+        double acc[kMaxSegCols];
+#pragma unroll
+        for (int c = 0; c < kMaxSegCols; c++) acc[c] = 0.0;
+        // phase 2: limb 1
         {
             const LimbTab T = tabs[1];
             const uint64_t* c0 = ctb + ((size_t)1 << LOGN);
@@ -1241,31 +1421,45 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
             auto ld = [&](int j) {
                 return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q);
             };
-            auto st = [&](int j, uint64_t x) { sm[pad(j)] = x; };
-            ntt_inverse_impl<LOGN, NC1>(sm, T, ld, st);
-        }
-        // CRT, / Delta^2 and the segment functionals over this thread's
-        // elements j = tid + k * NT
-        double acc[kMaxSegCols];
+            if constexpr (CL == 1) {
+                // the last pass parks element j in sm[pad(j)], a slot only
+                // this thread reads or writes from then on
+                auto st = [&](int j, uint64_t x) { sm[pad(j)] = x; };
+                ntt_inverse_impl<LOGN, NC1>(sm, T, ld, st);
+            } else {
+                // the last pass's elements span both halves: combine each
+                // with its limb-0 value (written by this thread) on the spot
+                auto st = [&](int j, uint64_t x) {
+                    const double coeff = __dmul_rn(crt_coeff(m0v[j], x, K), inv_scale);
 #pragma unroll
-        for (int c = 0; c < kMaxSegCols; c++) acc[c] = 0.0;
-        // limb-0 loads issued in groups of 8 ahead of their arithmetic
-        constexpr int G = 8;
-#pragma unroll 1
-        for (int k0 = 0; k0 < N / NT; k0 += G) {
-            uint64_t m0r[G];
-#pragma unroll
-            for (int kk = 0; kk < G; kk++) m0r[kk] = m0v[tid + (k0 + kk) * NT];
-#pragma unroll
-            for (int kk = 0; kk < G; kk++) {
-                const int j = tid + (k0 + kk) * NT;
-                const double coeff = __dmul_rn(crt_coeff(m0r[kk], sm[pad(j)], K), inv_scale);
-#pragma unroll
-                for (int c = 0; c < kMaxSegCols; c++)
-                    if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
+                    for (int c = 0; c < kMaxSegCols; c++)
+                        if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
+                };
+                ntt_inverse_impl<LOGN, NC1>(sm, T, ld, st);
             }
         }
-        // deterministic block reduction of acc[0 .. cols)
+        if constexpr (CL == 1) {
+            // CRT, / Delta^2 and the segment functionals over this thread's
+            // elements j = tid + k * NT; limb-0 loads issued in groups of 8
+            // ahead of their arithmetic
+            constexpr int G = 8;
+#pragma unroll 1
+            for (int k0 = 0; k0 < N / NT; k0 += G) {
+                uint64_t m0r[G];
+#pragma unroll
+                for (int kk = 0; kk < G; kk++) m0r[kk] = m0v[tid + (k0 + kk) * NT];
+#pragma unroll
+                for (int kk = 0; kk < G; kk++) {
+                    const int j = tid + (k0 + kk) * NT;
+                    const double coeff = __dmul_rn(crt_coeff(m0r[kk], sm[pad(j)], K), inv_scale);
+#pragma unroll
+                    for (int c = 0; c < kMaxSegCols; c++)
+                        if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
+                }
+            }
+        }
+        // deterministic reduction of acc[0 .. cols): warps, then (CL = 2)
+        // the two CTAs in rank order
         __syncthreads();
         double* red = reinterpret_cast<double*>(sm);  // [NT/32][kMaxSegCols]
         const int lane = tid & 31, wid = tid >> 5;
@@ -1276,13 +1470,26 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
             for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
             if (lane == 0) red[wid * kMaxSegCols + c] = a;
         }
-        __syncthreads();
-        if (tid < cols) {
-            double a = 0.0;
-            for (int w = 0; w < NT / 32; w++) a += red[w * kMaxSegCols + tid];
-            seg_out[(size_t)v * cols + tid] = a;
+        if constexpr (CL == 1) {
+            __syncthreads();
+            if (tid < cols) {
+                double a = 0.0;
+                for (int w = 0; w < NT / 32; w++) a += red[w * kMaxSegCols + tid];
+                seg_out[(size_t)v * cols + tid] = a;
+            }
+            __syncthreads();
+        } else {
+            cluster_sync();
+            if (ntt_rank<LOGN>() == 0 && tid < cols) {
+                double a = 0.0;
+                for (int r = 0; r < CL; r++) {
+                    const double* rr = reinterpret_cast<const double*>(cluster_smem(sm, r));
+                    for (int w = 0; w < NT / 32; w++) a += rr[w * kMaxSegCols + tid];
+                }
+                seg_out[(size_t)v * cols + tid] = a;
+            }
+            cluster_sync();
         }
-        __syncthreads();
     }
 }
 
@@ -1293,21 +1500,21 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
                              cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
     if (seg_cols < 1 || seg_cols > kMaxSegCols || c.L < 2) return cudaErrorInvalidValue;
-    const size_t smem = (size_t)(c.n + c.n / 16) * 8;  // padded poly-limb
-    // one CTA per SM (the padded limb fills most of shared memory); M0 holds
-    // one limb per CTA
-    const int grid = nvec < c.sms ? nvec : c.sms;
     // correction-free INTT where the modulus leaves the headroom (as in ntt_inverse_block)
     const bool nc0 = c.q0 < (1ULL << (61 - c.logn)), nc1 = c.q1 < (1ULL << (61 - c.logn));
     TSG_LOGN_SWITCH(c.logn, {
+        constexpr size_t smem = ntt_smem_bytes<LG>();
+        constexpr int CL = NttCfg<LG>::CL;
+        // one CTA per SM (the padded share fills most of shared memory); M0
+        // holds one limb per CTA
+        const int groups = nvec < c.sms / CL ? nvec : c.sms / CL;
         auto kern = nc0 ? (nc1 ? k_dec_fused<LG, true, true> : k_dec_fused<LG, true, false>)
                         : (nc1 ? k_dec_fused<LG, false, true> : k_dec_fused<LG, false, false>);
         cudaError_t er = ensure_smem(kern, smem);
         if (er != cudaSuccess) return er;
         KScope ks("dec_fused", s);
-        kern<<<grid, NttCfg<LG>::NT, smem, s>>>(cts, ct_stride, ct_limbs, sk, sks, sk_of, pt, pts,
-                                                            pt_sel, per_ct, nvec, c.tabs, c.L, c.crt, inv_scale, W, seg_cols, M0,
-                                                            seg_out);
+        return launch_cl(CL, kern, dim3(groups * CL), NttCfg<LG>::NT, smem, s, cts, ct_stride, ct_limbs, sk, sks,
+                         sk_of, pt, pts, pt_sel, per_ct, nvec, c.tabs, c.L, c.crt, inv_scale, W, seg_cols, M0, seg_out);
     });
     return cudaGetLastError();
 }

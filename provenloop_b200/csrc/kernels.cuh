@@ -124,11 +124,31 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
                                  int nvec,
                                  uint32_t* flags, const StreamPlan* plans, bool plan_mode, cudaStream_t s);
 
+// Gaussian errors e[v][j] from stream words off + 4j (off a multiple of 16)
+// of seeds[v] (sampling.rs:51-58), for every vector.
+cudaError_t launch_gauss_gen(const DevCtx& c, int8_t* e, const uint64_t* seeds, int nvec, uint64_t off,
+                             cudaStream_t s);
+// Public-key encryption (ciphertext.rs:240-319) of nvec vectors into
+// ct[v][2][L][n] from m, e0, e1, U = NTT(u) [v][L][n] and pk = (b, a)
+// [2][L][n] with Shoup companions pks.
+cudaError_t launch_enc_pk(const DevCtx& c, uint64_t* ct, const int64_t* m, const int8_t* e0, const int8_t* e1,
+                          const uint64_t* U, const uint64_t* pk, const uint64_t* pks, int nvec, cudaStream_t s);
+
+// q_last^-1 mod q_l for the limbs kept by a rescale.
+struct RescaleInv {
+    uint64_t v[kMaxLimbs];
+};
+// Rescale's coefficient-domain step (ciphertext.rs:499-521): in is
+// INTT(ct) [count][2][nl][n], out [count][2][nl-1][n] (still coefficients).
+cudaError_t launch_rescale_combine(const DevCtx& c, uint64_t* out, const uint64_t* in, int count, int nl,
+                                   const RescaleInv& inv, cudaStream_t s);
+
 // Flag buffers hold (2*count + 1) uint32: per-stream flags, the number of
 // flagged streams, and their indexes; zero them before the speculative pass.
-// Exact plans for flagged streams (CTAs walk the flagged list).
+// Exact plans for flagged streams (CTAs walk the flagged list).  Stream v's
+// segments start at word bases[v] (0 when bases is null).
 cudaError_t launch_plan(const DevCtx& c, const uint64_t* seeds, int nstreams, const uint32_t* flags,
-                        StreamPlan* plans, const SegList& segs, cudaStream_t s);
+                        StreamPlan* plans, const SegList& segs, cudaStream_t s, const uint64_t* bases = nullptr);
 // Recompute the Gaussian e[v] of flagged streams from plan segment `seg`.
 cudaError_t launch_gauss_fix(const DevCtx& c, int8_t* e, const uint64_t* seeds, int nvec, const uint32_t* flags,
                              const StreamPlan* plans, int seg, cudaStream_t s);

@@ -30,7 +30,18 @@
 // corrections entirely (the NC variants below).
 // Each twiddle and its companion are one 16-byte load.  N^-1 is folded into
 // the last inverse stage.
+//
+// N = 32768 (256 KiB per poly-limb) spans a cluster of two CTAs (CL = 2):
+// CTA h holds elements [h*N/2, (h+1)*N/2) in its own padded shared memory
+// and 512 threads x 32 values.  Of the three radix-32 passes, the one whose
+// butterflies cross the halves (spans N/32 .. N/2: the forward's first, the
+// inverse's last) is split by sets, each CTA taking half of the 1024 sets
+// and reaching the partner's elements through distributed shared memory;
+// the other two passes are local.  The kernel must then be launched with
+// cluster dimension 2 along x, and block pairs see the same work item.
 #pragma once
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace tsg {
@@ -54,10 +65,13 @@ __device__ __forceinline__ int pad(int j) { return j + (j >> 4); }
 template <int LOGN>
 struct NttCfg {
     static constexpr int N = 1 << LOGN;
+    static constexpr int CL = LOGN >= 15 ? 2 : 1;   // CTAs per transform (cluster size)
+    static constexpr int H = N / CL;                // elements held by one CTA
     static constexpr int E = LOGN >= 13 ? 32 : 16;  // values per thread
-    static constexpr int NT = N / E;                // threads per CTA
+    static constexpr int NT = H / E;                // threads per CTA
+    static constexpr int JS = N / E;                // element stride of a first-pass set
     static constexpr int RMAX = E == 32 ? 5 : 4;    // stages per pass
-    static constexpr int SMEM_WORDS = N + N / 16;   // padded poly-limb
+    static constexpr int SMEM_WORDS = H + H / 16;   // padded share of the poly-limb
     static constexpr int NPASS = (LOGN + RMAX - 1) / RMAX;
     // stages of forward pass p: RMAX each, the last pass the remainder
     __host__ __device__ static constexpr int fwd_r(int p) { return p < NPASS - 1 ? RMAX : LOGN - RMAX * (NPASS - 1); }
@@ -70,38 +84,83 @@ struct NttCfg {
 // tid owns sets sigma = tid + NT*u, u < SETS.  j0 and k << TLOG occupy
 // disjoint bits, so pad(j0 + (k << TLOG)) = pad(j0) + K + K/16 with
 // K = k << TLOG: one base register plus a compile-time offset.
+//
+// With CL = 2 the CTA of rank h takes sets h*NT*SETS .. (h+1)*NT*SETS - 1.
+// In a local pass (TLOG + R < LOGN) those are exactly the sets whose
+// elements lie in half h, and pbase gives the local padded address.
 template <int LOGN, int R, int TLOG>
 struct Geo {
     static constexpr int N = 1 << LOGN;
     static constexpr int NT = NttCfg<LOGN>::NT;
+    static constexpr int H = NttCfg<LOGN>::H;
     static constexpr int SETS = NttCfg<LOGN>::E >> R;
-    __device__ __forceinline__ static int sigma(int tid, int u) { return tid + NT * u; }
+    __device__ __forceinline__ static int sigma(int h, int tid, int u) { return h * NT * SETS + tid + NT * u; }
     __device__ __forceinline__ static int pbase(int sg) {
-        return pad(((sg >> TLOG) << (TLOG + R)) + (sg & ((1 << TLOG) - 1)));
+        return pad((((sg >> TLOG) << (TLOG + R)) + (sg & ((1 << TLOG) - 1))) & (H - 1));
     }
     __host__ __device__ static constexpr int koff(int k) { return (k << TLOG) + ((k << TLOG) >> 4); }
 };
 
 template <int LOGN, int R, int TLOG>
-__device__ __forceinline__ void smem_load(const uint64_t* sm, uint64_t* v, int tid) {
+__device__ __forceinline__ void smem_load(const uint64_t* sm, uint64_t* v, int h, int tid) {
     using G = Geo<LOGN, R, TLOG>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++) {
-        const uint64_t* b = sm + G::pbase(G::sigma(tid, u));
+        const uint64_t* b = sm + G::pbase(G::sigma(h, tid, u));
 #pragma unroll
         for (int k = 0; k < (1 << R); k++) v[u * (1 << R) + k] = b[G::koff(k)];
     }
 }
 
 template <int LOGN, int R, int TLOG>
-__device__ __forceinline__ void smem_store(uint64_t* sm, const uint64_t* v, int tid) {
+__device__ __forceinline__ void smem_store(uint64_t* sm, const uint64_t* v, int h, int tid) {
     using G = Geo<LOGN, R, TLOG>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++) {
-        uint64_t* b = sm + G::pbase(G::sigma(tid, u));
+        uint64_t* b = sm + G::pbase(G::sigma(h, tid, u));
 #pragma unroll
         for (int k = 0; k < (1 << R); k++) b[G::koff(k)] = v[u * (1 << R) + k];
     }
+}
+
+// Cluster helpers (CL = 2).  The rank, and shared memory of either CTA of
+// the pair as a generic pointer.
+__device__ __forceinline__ int cluster_rank() { return (int)cooperative_groups::this_cluster().block_rank(); }
+__device__ __forceinline__ void cluster_sync() { cooperative_groups::this_cluster().sync(); }
+__device__ __forceinline__ uint64_t* cluster_smem(uint64_t* sm, int rank) {
+    return cooperative_groups::this_cluster().map_shared_rank(sm, rank);
+}
+
+// Rank of this CTA within its transform (0 unless CL = 2).
+template <int LOGN>
+__device__ __forceinline__ int ntt_rank() {
+    if constexpr (NttCfg<LOGN>::CL == 2) return cluster_rank();
+    return 0;
+}
+
+// A poly-limb staged in the shared memory of the transform's CTAs (each
+// CTA its own share, at padded local positions): element j for callers
+// whose first-pass loader reads shared memory.
+template <int LOGN>
+struct SmemView {
+    using C = NttCfg<LOGN>;
+    uint64_t* part[C::CL];
+    __device__ __forceinline__ uint64_t operator()(int j) const {
+        if constexpr (C::CL == 2) return (j < C::H ? part[0] : part[1])[pad(j & (C::H - 1))];
+        return part[0][pad(j)];
+    }
+};
+
+template <int LOGN>
+__device__ __forceinline__ SmemView<LOGN> ntt_smem_view(uint64_t* sm) {
+    SmemView<LOGN> v;
+    if constexpr (NttCfg<LOGN>::CL == 2) {
+        v.part[0] = cluster_smem(sm, 0);
+        v.part[1] = cluster_smem(sm, 1);
+    } else {
+        v.part[0] = sm;
+    }
+    return v;
 }
 
 // One forward CT stage (sub-stage r of a radix-2^R pass starting at stage
@@ -131,12 +190,13 @@ __device__ __forceinline__ void fwd_stage(uint64_t* x, int g, const ulonglong2* 
 }
 
 template <int LOGN, int R, int S0, bool NC>
-__device__ __forceinline__ void fwd_compute(uint64_t* v, const ulonglong2* __restrict__ fw, uint64_t q, int tid) {
+__device__ __forceinline__ void fwd_compute(uint64_t* v, const ulonglong2* __restrict__ fw, uint64_t q, int h,
+                                            int tid) {
     constexpr int TLOG = LOGN - S0 - R;
     using G = Geo<LOGN, R, TLOG>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++)
-        fwd_stage<R, S0, 0, NC>(v + u * (1 << R), G::sigma(tid, u) >> TLOG, fw, q, 4 * q);
+        fwd_stage<R, S0, 0, NC>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, fw, q, 4 * q);
 }
 
 // One inverse GS stage (span 2^(TLOG+r)) on values in [0, 4q); the stage of
@@ -181,11 +241,12 @@ __device__ __forceinline__ void inv_stage(uint64_t* x, int g, const ulonglong2* 
 }
 
 template <int LOGN, int R, int TLOG, bool NC>
-__device__ __forceinline__ void inv_compute(uint64_t* v, const ulonglong2* __restrict__ iw, const LimbTab& T, int tid) {
+__device__ __forceinline__ void inv_compute(uint64_t* v, const ulonglong2* __restrict__ iw, const LimbTab& T, int h,
+                                            int tid) {
     using G = Geo<LOGN, R, TLOG>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++)
-        inv_stage<LOGN, R, TLOG, 0, NC>(v + u * (1 << R), G::sigma(tid, u) >> TLOG, iw, T, 4 * T.q);
+        inv_stage<LOGN, R, TLOG, 0, NC>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, iw, T, 4 * T.q);
 }
 
 // [0, 8q) -> [0, q)
@@ -205,41 +266,61 @@ __device__ __forceinline__ uint64_t canon4(uint64_t x, uint64_t q) {
 // values are already in v; every pass stores its results back to the
 // positions it read (its own sets), so one barrier between passes suffices.
 template <int LOGN, int P, bool NC>
-__device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulonglong2* fw, uint64_t q, int tid) {
+__device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulonglong2* fw, uint64_t q, int h,
+                                           int tid) {
     using C = NttCfg<LOGN>;
     constexpr int R = C::fwd_r(P), S0 = C::fwd_s0(P), TLOG = LOGN - S0 - R;
     if constexpr (P > 0) {
-        __syncthreads();
-        smem_load<LOGN, R, TLOG>(sm, v, tid);
+        if constexpr (C::CL == 2 && P == 1) cluster_sync();  // both halves written
+        else __syncthreads();
+        smem_load<LOGN, R, TLOG>(sm, v, h, tid);
     }
-    fwd_compute<LOGN, R, S0, NC>(v, fw, q, tid);
-    smem_store<LOGN, R, TLOG>(sm, v, tid);
-    if constexpr (P + 1 < C::NPASS) fwd_passes<LOGN, P + 1, NC>(sm, v, fw, q, tid);
+    fwd_compute<LOGN, R, S0, NC>(v, fw, q, h, tid);
+    if constexpr (C::CL == 2 && P == 0) {
+        // the first pass's sets span both halves: element sigma + k*JS goes
+        // to CTA k / (E/2).  The partner must be done reading its shared
+        // memory (the previous transform, or a loader that reads it) first.
+        static_assert(R == 5 && C::E == 32, "cluster NTT expects radix-32 passes");
+        cluster_sync();
+        const int sg = Geo<LOGN, R, TLOG>::sigma(h, tid, 0);
+        uint64_t* s0 = cluster_smem(sm, 0);
+        uint64_t* s1 = cluster_smem(sm, 1);
+#pragma unroll
+        for (int k = 0; k < C::E; k++) (k < C::E / 2 ? s0 : s1)[pad(sg + (k & (C::E / 2 - 1)) * C::JS)] = v[k];
+    } else {
+        smem_store<LOGN, R, TLOG>(sm, v, h, tid);
+    }
+    if constexpr (P + 1 < C::NPASS) fwd_passes<LOGN, P + 1, NC>(sm, v, fw, q, h, tid);
 }
 
 // Forward transform of one poly-limb.  ld(j) returns element j (< 8q, e.g.
-// canonical) for j = tid + k*NT; st(j, v) receives canonical output j in the
-// same coalesced order.  `sm` holds NttCfg<LOGN>::SMEM_WORDS u64.  All NT
-// threads of the block must call this; a caller that reuses `sm` afterwards
-// must __syncthreads() first.  If ld reads `sm`, each thread may only read
-// the positions pad(tid + k*NT) (its own first-pass elements).
+// canonical) for j = sigma + k*JS, sigma = rank*NT + tid (rank 0 unless
+// CL = 2); st(j, v) receives canonical output j for j = rank*H + tid + k*NT,
+// coalesced.  `sm` holds NttCfg<LOGN>::SMEM_WORDS u64.  All NT threads of
+// the block (both blocks of the cluster for CL = 2) must call this; a caller
+// that reuses `sm` afterwards must __syncthreads() first.  If ld reads `sm`,
+// each thread may only read the positions of its own first-pass elements
+// (through ntt_smem_view for CL = 2, after a cluster_sync).
 template <int LOGN, bool NC, class Ld, class St>
 __device__ __forceinline__ void ntt_forward_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
     using C = NttCfg<LOGN>;
-    static_assert(LOGN >= 10 && LOGN <= 14, "single-CTA NTT supports N in [1024, 16384]");
+    static_assert(LOGN >= 10 && LOGN <= 15, "NTT supports N in [1024, 32768]");
     static_assert(C::fwd_r(0) == C::RMAX, "the first pass takes RMAX stages");
     const int tid = threadIdx.x;
+    const int h = ntt_rank<LOGN>();
     const ulonglong2* fw = reinterpret_cast<const ulonglong2*>(T.tw);
     uint64_t v[C::E];
-    // first pass: one set per thread, elements tid + k*NT
+    // first pass: one set per thread, elements sigma + k*JS
+    const int sg = h * C::NT + tid;
 #pragma unroll
-    for (int k = 0; k < C::E; k++) v[k] = ld(tid + k * C::NT);
-    fwd_passes<LOGN, 0, NC>(sm, v, fw, T.q, tid);
+    for (int k = 0; k < C::E; k++) v[k] = ld(sg + k * C::JS);
+    fwd_passes<LOGN, 0, NC>(sm, v, fw, T.q, h, tid);
     __syncthreads();
+    // own share, coalesced: j = h*H + tid + k*NT
 #pragma unroll
     for (int k = 0; k < C::E; k++) {
-        const int j = tid + k * C::NT;
-        st(j, NC ? mod_u64(sm[pad(j)], T.q, T.mu64) : canon8(sm[pad(j)], T.q));
+        const int jl = tid + k * C::NT;
+        st(h * C::H + jl, NC ? mod_u64(sm[pad(jl)], T.q, T.mu64) : canon8(sm[pad(jl)], T.q));
     }
 }
 
@@ -255,38 +336,57 @@ __device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T
 // NPASS-1-P.  Its values are in shared memory on entry; the last pass keeps
 // its results (elements tid + k*NT) in v.
 template <int LOGN, int P, bool NC>
-__device__ __forceinline__ void inv_passes(uint64_t* sm, uint64_t* v, const ulonglong2* iw, const LimbTab& T, int tid) {
+__device__ __forceinline__ void inv_passes(uint64_t* sm, uint64_t* v, const ulonglong2* iw, const LimbTab& T, int h,
+                                           int tid) {
     using C = NttCfg<LOGN>;
     constexpr int FP = C::NPASS - 1 - P;
     constexpr int R = C::fwd_r(FP), TLOG = LOGN - C::fwd_s0(FP) - R;
-    __syncthreads();
-    smem_load<LOGN, R, TLOG>(sm, v, tid);
-    inv_compute<LOGN, R, TLOG, NC>(v, iw, T, tid);
+    if constexpr (C::CL == 2 && FP == 0) {
+        // the last pass's sets span both halves: element sigma + k*JS is in
+        // CTA k / (E/2); once both CTAs hold their values in registers the
+        // partner may reuse its shared memory
+        static_assert(R == 5 && C::E == 32, "cluster NTT expects radix-32 passes");
+        cluster_sync();
+        const int sg = Geo<LOGN, R, TLOG>::sigma(h, tid, 0);
+        const uint64_t* s0 = cluster_smem(sm, 0);
+        const uint64_t* s1 = cluster_smem(sm, 1);
+#pragma unroll
+        for (int k = 0; k < C::E; k++) v[k] = (k < C::E / 2 ? s0 : s1)[pad(sg + (k & (C::E / 2 - 1)) * C::JS)];
+        cluster_sync();
+    } else {
+        __syncthreads();
+        smem_load<LOGN, R, TLOG>(sm, v, h, tid);
+    }
+    inv_compute<LOGN, R, TLOG, NC>(v, iw, T, h, tid);
     if constexpr (P + 1 < C::NPASS) {
-        smem_store<LOGN, R, TLOG>(sm, v, tid);
-        inv_passes<LOGN, P + 1, NC>(sm, v, iw, T, tid);
+        smem_store<LOGN, R, TLOG>(sm, v, h, tid);
+        inv_passes<LOGN, P + 1, NC>(sm, v, iw, T, h, tid);
     }
 }
 
 // Inverse transform (including x N^-1) of one poly-limb; ld(j) returns
-// element j (< 4q) for j = tid + k*NT, st(j, v) receives canonical output j
-// in the same coalesced order.  A caller that reuses `sm` afterwards must
-// __syncthreads() first.
+// element j (< 4q) for j = rank*H + tid + k*NT, st(j, v) receives canonical
+// output j for j = sigma + k*JS, sigma = rank*NT + tid.  A caller that reuses
+// `sm` afterwards must __syncthreads() first.
 template <int LOGN, bool NC, class Ld, class St>
 __device__ __forceinline__ void ntt_inverse_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
     using C = NttCfg<LOGN>;
-    static_assert(LOGN >= 10 && LOGN <= 14, "single-CTA NTT supports N in [1024, 16384]");
+    static_assert(LOGN >= 10 && LOGN <= 15, "NTT supports N in [1024, 32768]");
     const int tid = threadIdx.x;
+    const int h = ntt_rank<LOGN>();
     const ulonglong2* iw = reinterpret_cast<const ulonglong2*>(T.tw) + C::N;
     uint64_t v[C::E];
+    // own share: j = h*H + tid + k*NT
 #pragma unroll
     for (int k = 0; k < C::E; k++) {
-        const int j = tid + k * C::NT;
-        sm[pad(j)] = ld(j);
+        const int jl = tid + k * C::NT;
+        sm[pad(jl)] = ld(h * C::H + jl);
     }
-    inv_passes<LOGN, 0, NC>(sm, v, iw, T, tid);
+    inv_passes<LOGN, 0, NC>(sm, v, iw, T, h, tid);
+    // last-pass set: elements sigma + k*JS (for CL = 1, sigma = tid)
+    const int sg = h * C::NT + tid;
 #pragma unroll
-    for (int k = 0; k < C::E; k++) st(tid + k * C::NT, canon4(v[k], T.q));
+    for (int k = 0; k < C::E; k++) st(sg + k * C::JS, canon4(v[k], T.q));
 }
 
 // Inverse transform, with the correction-free butterflies when

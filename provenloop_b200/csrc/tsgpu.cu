@@ -204,6 +204,11 @@ struct ts_sk {
 // Shoup companions of a key set (floor(s * 2^64 / q_l) per coefficient).
 static const uint64_t* sk_shoup(const ts_sk* sk) { return sk->d + (size_t)sk->count * sk->ctx->L * sk->ctx->n; }
 
+struct ts_pk {
+    ts_ctx* ctx;
+    uint64_t* d;  // [2][L][n] = (b, a), NTT domain, then [2][L][n] Shoup companions
+};
+
 struct ts_ct {
     ts_ctx* ctx;
     uint32_t count, limbs;
@@ -306,8 +311,8 @@ SegList encrypt_segs(uint32_t L) {
 int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bits, int device, ts_ctx** out) {
     if (!out) return fail(TS_ERR_ARG, "out is NULL");
     *out = nullptr;
-    if (n < 1024 || n > 16384 || (n & (n - 1)))
-        return fail(TS_ERR_UNSUPPORTED, "Unsupported poly_mod_degree: %u (this build supports 1024..16384)", n);
+    if (n < 1024 || n > 32768 || (n & (n - 1)))
+        return fail(TS_ERR_UNSUPPORTED, "Unsupported poly_mod_degree: %u (this build supports 1024..32768)", n);
     if (L < 1 || L > (uint32_t)kMaxLimbs) return fail(TS_ERR_ARG, "num_limbs %u out of range [1, %d]", L, kMaxLimbs);
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(TS_ERR_NODEVICE, "no CUDA device");
@@ -1300,7 +1305,7 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
                      i_pl = cv.add(nv * sizeof(StreamPlan)),
                      // fused decrypt: one limb-0 buffer per CTA; otherwise both limbs of
                      // every vector and the FFT scratch of the decode
-                     i_M = cv.add(lo->d_w ? std::min(nv * nb, (size_t)c->dc.sms) * N * 8 : nv * nb * 2 * N * 8),
+                     i_M = cv.add(lo->d_w ? (size_t)c->dc.sms * N * 8 : nv * nb * 2 * N * 8),
                      i_fd = cv.add(lo->d_w ? 0 : nv * nb * 2 * N * 8), i_sg = cv.add(nv * nb * cols * 8);
         rc = ensure_scratch(c, cv.total());
         if (rc) break;
@@ -1377,10 +1382,288 @@ int ts_dp_noise(ts_ctx* c, double* h, uint32_t n, uint32_t d, double clip, doubl
     return rc;
 }
 
+// ------------------------------------------------------------------ public key
+int ts_keygen_public(ts_ctx* c, const ts_sk* sk, uint32_t sk_index, uint64_t seed, ts_pk** out) {
+    if (!c || !sk || !out) return fail(TS_ERR_ARG, "bad keygen_public arguments");
+    if (sk->ctx != c) return fail(TS_ERR_ARG, "secret key belongs to another context");
+    if (sk_index >= sk->count) return fail(TS_ERR_ARG, "sk_index out of range");
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    const size_t words = (size_t)c->L * c->n;
+    ts_pk* pk = new ts_pk{c, nullptr};
+    rc = dev_alloc(c, (void**)&pk->d, 4 * words * 8);
+    if (rc) {
+        delete pk;
+        return rc;
+    }
+    // pk = (b, a) is exactly a secret-key encryption of the zero message
+    // under the same stream layout (ciphertext.rs:114-154 against :167-229:
+    // a limbs, then e; b = -a*s + e), so it reuses the encryption pipeline.
+    Carve cv;
+    size_t idx[5];
+    carve_enc(cv, 1, c->n, idx);
+    const size_t i_seed = cv.add(8);
+    rc = ensure_scratch(c, cv.total());
+    uint64_t* d_seed = rc ? nullptr : cv.at<uint64_t>(c->scratch, i_seed);
+    if (!rc) rc = h2d_small(c, d_seed, &seed, 1);
+    if (!rc) {
+        SlotSrc zero{d_seed, 0, 0, 1, 0, 0};  // len 0: every slot is 0
+        rc = encrypt_core(c, zero, 1, d_seed, nullptr, sk->d + sk_index * words, sk_shoup(sk) + sk_index * words,
+                          pk->d, enc_work(cv, c->scratch, 1, idx));
+    }
+    if (!rc) {
+        cudaError_t e = launch_shoup_companion(c->dc, pk->d + 2 * words, pk->d, 2LL * c->L, c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "keygen_public: %s", cudaGetErrorString(e));
+    }
+    if (!rc) rc = check_stats(c);
+    if (rc) {
+        cudaFreeAsync(pk->d, c->stream);
+        delete pk;
+        return rc;
+    }
+    *out = pk;
+    return TS_OK;
+}
+
+int ts_pk_destroy(ts_pk* pk) {
+    if (!pk) return TS_OK;
+    Lock lk(pk->ctx);
+    cudaSetDevice(pk->ctx->device);
+    cudaFreeAsync(pk->d, pk->ctx->stream);
+    delete pk;
+    return TS_OK;
+}
+
+int ts_pk_export(const ts_pk* pk, uint64_t* b, uint64_t* a) {
+    if (!pk) return fail(TS_ERR_ARG, "pk is NULL");
+    ts_ctx* c = pk->ctx;
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    const size_t words = (size_t)c->L * c->n;
+    if (b) CU(cudaMemcpyAsync(b, pk->d, words * 8, cudaMemcpyDeviceToHost, c->stream));
+    if (a) CU(cudaMemcpyAsync(a, pk->d + words, words * 8, cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    return TS_OK;
+}
+
+int ts_encrypt_pk(ts_ctx* c, const ts_pk* pk, const double* data, size_t count, size_t len, size_t stride,
+                  const uint64_t* seeds, int data_on_device, ts_ct** out) {
+    if (!c || !pk || !out || !seeds || count == 0 || (!data && len)) return fail(TS_ERR_ARG, "bad encrypt_pk arguments");
+    if (pk->ctx != c) return fail(TS_ERR_ARG, "public key belongs to another context");
+    Lock lk(c);
+    if (len > c->slots) len = c->slots;  // lib.rs:142-164 pads / truncates like encrypt
+    if (stride < len) stride = len;
+    if (data_on_device && !aligned(data, 8)) return fail(TS_ERR_ARG, "device data must be 8-byte aligned");
+    int rc = set_device(c);
+    if (rc) return rc;
+    const size_t n = c->n, L = c->L, words = L * n;
+    ts_ct* ct = nullptr;
+    rc = new_ct(c, (uint32_t)count, c->L, c->dc.scale, &ct);
+    if (rc) return rc;
+    void* buf = nullptr;
+    const size_t data_bytes = data_on_device ? 0 : count * (len ? len : 1) * 8;
+    rc = dev_alloc(c, &buf, data_bytes + count * 8 + 512);
+    if (rc) {
+        cudaFreeAsync(ct->d, c->stream);
+        delete ct;
+        return rc;
+    }
+    double* d_data = data_on_device ? const_cast<double*>(data) : static_cast<double*>(buf);
+    uint64_t* d_seeds = reinterpret_cast<uint64_t*>(static_cast<char*>(buf) + ((data_bytes + 255) & ~(size_t)255));
+    if (!data_on_device) rc = h2d_rows(c, d_data, data, count, len, stride);
+    if (!rc) rc = h2d_small(c, d_seeds, seeds, count);
+    // stream layout (ciphertext.rs:240-319): ternary u (N words, rejecting
+    // 0), then e0 and e1 (4N words each)
+    SegList segs{};
+    segs.count = 3;
+    segs.kind[0] = SEG_TERNARY;
+    segs.kind[1] = SEG_GAUSS;
+    segs.kind[2] = SEG_GAUSS;
+    const size_t cap = count < 256 ? count : 256;
+    Carve cv;
+    size_t idx[5];
+    carve_enc(cv, cap, n, idx);
+    const size_t i_e1 = cv.add(cap * n), i_u = cv.add(cap * words * 8);
+    if (!rc) rc = ensure_scratch(c, cv.total());
+    for (size_t v0 = 0; v0 < count && !rc; v0 += cap) {
+        const size_t nv = count - v0 < cap ? count - v0 : cap;
+        const EncWork w = enc_work(cv, c->scratch, cap, idx);
+        int8_t* e1 = cv.at<int8_t>(c->scratch, i_e1);
+        uint64_t* U = cv.at<uint64_t>(c->scratch, i_u);
+        const uint64_t* sd = d_seeds + v0;
+        SlotSrc src{d_data + v0 * (data_on_device ? stride : len), 0, (int)len,
+                    (long long)(data_on_device ? stride : len), 0, 0};
+        CU(cudaMemsetAsync(w.fl, 0, (2 * nv + 1) * 4, c->stream));
+        CU(launch_encode(c->dc, src, (int)nv, w.m, w.e, sd, n, w.f, c->stream));  // m, e0 at word N
+        CU(launch_gauss_gen(c->dc, e1, sd, (int)nv, 5 * n, c->stream));          // e1 at word 5N
+        CU(launch_keygen(c->dc, U, sd, (int)nv, w.fl, w.pl, c->stream));         // NTT(u), flags
+        // exact repair of streams whose ternary segment rejected a draw
+        CU(launch_plan(c->dc, sd, (int)nv, w.fl, w.pl, segs, c->stream));
+        CU(launch_keygen_fix(c->dc, U, sd, (int)nv, w.fl, w.pl, c->stream));
+        CU(launch_gauss_fix(c->dc, w.e, sd, (int)nv, w.fl, w.pl, 1, c->stream));
+        CU(launch_gauss_fix(c->dc, e1, sd, (int)nv, w.fl, w.pl, 2, c->stream));
+        CU(launch_enc_pk(c->dc, ct->d + v0 * 2 * words, w.m, w.e, e1, U, pk->d, pk->d + 2 * words, (int)nv,
+                         c->stream));
+    }
+    cudaFreeAsync(buf, c->stream);
+    if (!rc) rc = check_stats(c);
+    if (rc) {
+        cudaFreeAsync(ct->d, c->stream);
+        delete ct;
+        return rc;
+    }
+    *out = ct;
+    return TS_OK;
+}
+
+// ------------------------------------------------------------------ rescale
+int ts_rescale(ts_ctx* c, const ts_ct* ct, ts_ct** out) {
+    if (!c || !ct || !out) return fail(TS_ERR_ARG, "bad rescale arguments");
+    if (ct->ctx != c) return fail(TS_ERR_ARG, "ciphertext belongs to another context");
+    if (ct->limbs < 2) return fail(TS_ERR_ARG, "Cannot rescale: only 1 limb left");  // ciphertext.rs:479
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    const uint32_t nl = ct->limbs;
+    const uint64_t q_last = c->q[nl - 1];
+    RescaleInv inv{};
+    for (uint32_t l = 0; l + 1 < nl; l++) {
+        // rns.rs:114-117 asserts a != 0: a chain that repeats its last prime
+        // (custom(..) duplicates) cannot be rescaled
+        if (q_last % c->q[l] == 0) return fail(TS_ERR_ARG, "Cannot invert zero (limb %u repeats the last prime)", l);
+        inv.v[l] = powmod(q_last % c->q[l], c->q[l] - 2, c->q[l]);
+    }
+    const size_t n = c->n, words = (size_t)ct->count * 2 * nl * n;
+    ts_ct* o = nullptr;
+    rc = new_ct(c, ct->count, nl - 1, ct->scale / (double)q_last, &o);  // ciphertext.rs:531
+    if (rc) return rc;
+    rc = ensure_scratch(c, words * 8);
+    if (!rc) {
+        uint64_t* t = static_cast<uint64_t*>(c->scratch);
+        cudaError_t e = cudaMemcpyAsync(t, ct->d, words * 8, cudaMemcpyDeviceToDevice, c->stream);
+        if (e == cudaSuccess) e = launch_ntt(c->dc, t, (long long)ct->count * 2 * nl, (int)nl, 0, true, c->stream);
+        if (e == cudaSuccess) e = launch_rescale_combine(c->dc, o->d, t, (int)ct->count, (int)nl, inv, c->stream);
+        if (e == cudaSuccess)
+            e = launch_ntt(c->dc, o->d, (long long)ct->count * 2 * (nl - 1), (int)nl - 1, 0, false, c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "rescale: %s", cudaGetErrorString(e));
+    }
+    if (rc) {
+        cudaFreeAsync(o->d, c->stream);
+        delete o;
+        return rc;
+    }
+    *out = o;
+    return TS_OK;
+}
+
+// batch_encrypt (lib.rs:231-258): the arrays consume ONE stream in order, so
+// array i starts where array i-1 stopped.  Array i takes 2(L*N + R_i) + 4N
+// words, R_i = its uniform rejections, so its start depends on every earlier
+// array's rejections.  The starts are found by fixed-point iteration: plan
+// every array from the starts implied by the previous round's rejection
+// counts (round 0: none) until they repeat -- each round settles at least
+// the first array whose start moved, and rejections are rare, so one or two
+// rounds suffice.  Every array is then encrypted from its exact plan.
 int ts_encrypt_stream(ts_ctx* c, const ts_sk* sk, const double* data, size_t count, size_t len, size_t stride,
                       uint64_t seed, ts_ct** out) {
-    (void)c; (void)sk; (void)data; (void)count; (void)len; (void)stride; (void)seed; (void)out;
-    return fail(TS_ERR_STATE, "ts_encrypt_stream: not built yet");
+    if (!c || !sk || !out || count == 0 || (!data && len)) return fail(TS_ERR_ARG, "bad batch_encrypt arguments");
+    if (sk->ctx != c) return fail(TS_ERR_ARG, "secret key belongs to another context");
+    Lock lk(c);
+    if (len > c->slots) len = c->slots;  // lib.rs:244-250 pads / truncates each array
+    if (stride < len) stride = len;
+    int rc = set_device(c);
+    if (rc) return rc;
+    const size_t n = c->n, L = c->L, words = L * n;
+    ts_ct* ct = nullptr;
+    rc = new_ct(c, (uint32_t)count, c->L, c->dc.scale, &ct);
+    if (rc) return rc;
+    Carve cb;
+    const size_t b_data = cb.add(count * (len ? len : 1) * 8), b_seed = cb.add(count * 8), b_base = cb.add(count * 8),
+                 b_fl = cb.add((2 * count + 1) * 4), b_pl = cb.add(count * sizeof(StreamPlan));
+    void* buf = nullptr;
+    rc = dev_alloc(c, &buf, cb.total());
+    if (rc) {
+        cudaFreeAsync(ct->d, c->stream);
+        delete ct;
+        return rc;
+    }
+    double* d_data = cb.at<double>(buf, b_data);
+    uint64_t* d_seeds = cb.at<uint64_t>(buf, b_seed);
+    uint64_t* d_base = cb.at<uint64_t>(buf, b_base);
+    uint32_t* d_fl = cb.at<uint32_t>(buf, b_fl);
+    StreamPlan* d_pl = cb.at<StreamPlan>(buf, b_pl);
+    std::vector<uint64_t> hseed(count, seed), base(count), nbase(count);
+    std::vector<uint32_t> hfl(2 * count + 1);
+    for (size_t v = 0; v < count; v++) {
+        hfl[v] = 1;
+        hfl[count + 1 + v] = (uint32_t)v;
+    }
+    hfl[count] = (uint32_t)count;
+    rc = h2d_rows(c, d_data, data, count, len, stride);
+    if (!rc) rc = h2d_small(c, d_seeds, hseed.data(), count);
+    if (!rc) rc = h2d_small(c, d_fl, hfl.data(), hfl.size());
+    const SegList segs = encrypt_segs(c->L);
+    std::vector<StreamPlan> hp(count);
+    for (size_t v = 0; v < count; v++) base[v] = v * (2 * words + 4 * n);  // no rejections
+    for (size_t round = 0; !rc; round++) {
+        if (round > count) {
+            rc = fail(TS_ERR_STATE, "batch_encrypt: stream offsets did not settle");
+            break;
+        }
+        rc = h2d_small(c, d_base, base.data(), count);
+        if (rc) break;
+        CU(launch_plan(c->dc, d_seeds, (int)count, d_fl, d_pl, segs, c->stream, d_base));
+        CU(cudaMemcpyAsync(hp.data(), d_pl, count * sizeof(StreamPlan), cudaMemcpyDeviceToHost, c->stream));
+        CU(cudaStreamSynchronize(c->stream));
+        nbase[0] = 0;
+        for (size_t v = 0; v < count; v++) {
+            if (hp[v].status) {
+                rc = fail(TS_ERR_STATE, "a sampling stream rejected more than %d candidates in one segment", kMaxRej);
+                break;
+            }
+            if (v + 1 < count) {
+                uint64_t rej = 0;
+                for (uint32_t l = 0; l < L; l++) rej += hp[v].nrej[l];
+                nbase[v + 1] = nbase[v] + 2 * (words + rej) + 4 * n;
+            }
+        }
+        if (rc || nbase == base) break;
+        base = nbase;
+    }
+    // encrypt every array from its plan, in chunks
+    const size_t cap = count < 256 ? count : 256;
+    Carve cv;
+    size_t idx[5];
+    carve_enc(cv, cap, n, idx);
+    if (!rc) rc = ensure_scratch(c, cv.total());
+    for (size_t v0 = 0; v0 < count && !rc; v0 += cap) {
+        const size_t nv = count - v0 < cap ? count - v0 : cap;
+        const EncWork w = enc_work(cv, c->scratch, cap, idx);
+        std::vector<uint32_t> cfl(2 * nv + 1);  // every array of the chunk flagged
+        for (size_t v = 0; v < nv; v++) {
+            cfl[v] = 1;
+            cfl[nv + 1 + v] = (uint32_t)v;
+        }
+        cfl[nv] = (uint32_t)nv;
+        rc = h2d_small(c, w.fl, cfl.data(), cfl.size());
+        if (rc) break;
+        SlotSrc src{d_data + v0 * len, 0, (int)len, (long long)len, 0, 0};
+        CU(launch_encode(c->dc, src, (int)nv, w.m, w.e, d_seeds, 2 * words, w.f, c->stream));
+        CU(launch_gauss_fix(c->dc, w.e, d_seeds + v0, (int)nv, w.fl, d_pl + v0, (int)L, c->stream));
+        CU(launch_encrypt_limbs(c->dc, ct->d + v0 * 2 * words, w.m, w.e, sk->d, sk_shoup(sk), nullptr, d_seeds + v0,
+                                (int)nv, w.fl, d_pl + v0, true, c->stream));
+    }
+    cudaFreeAsync(buf, c->stream);
+    if (!rc) rc = check_stats(c);
+    if (rc) {
+        cudaFreeAsync(ct->d, c->stream);
+        delete ct;
+        return rc;
+    }
+    *out = ct;
+    return TS_OK;
 }
 
 }  // extern "C"

@@ -90,11 +90,22 @@ class TenSafeSecretKey:
 
 
 class TenSafePublicKey:
-    """Public key (lib.rs:303-307)."""
+    """Public key pk = (b, a), NTT domain, on the device (lib.rs:303-307)."""
 
-    def __init__(self, ctx, h):
+    def __init__(self, ctx: "CkksContext", h):
         self._ctx = ctx
-        self._hd = _Handle(h, lambda h: None, ctx)
+        self._hd = _Handle(h, lib().ts_pk_destroy, ctx)
+
+    @property
+    def handle(self):
+        return self._hd._h
+
+    def export(self):
+        """(b, a) residues, each [L, N] uint64 (tests)."""
+        n = self._ctx._L * self._ctx._n
+        b, a = np.zeros(n, np.uint64), np.zeros(n, np.uint64)
+        check(lib().ts_pk_export(self.handle, ptr(b, C.c_uint64), ptr(a, C.c_uint64)), "ts_pk_export")
+        return b.reshape(self._ctx._L, self._ctx._n), a.reshape(self._ctx._L, self._ctx._n)
 
 
 class TenSafeCiphertext:
@@ -221,6 +232,35 @@ class CkksContext:
         return TenSafeSecretKey(self, h)
 
     # -------------------------------------------------------------- encrypt
+    def keygen_public(self, sk: TenSafeSecretKey, seed=None, sk_index: int = 0) -> TenSafePublicKey:
+        """lib.rs:102-110 (ciphertext.rs:114-154): pk = (-a*s + e, a)."""
+        h = C.c_void_p()
+        check(lib().ts_keygen_public(self.handle, sk.handle, int(sk_index), _seed(seed), C.byref(h)),
+              "ts_keygen_public")
+        return TenSafePublicKey(self, h)
+
+    def encrypt_pk(self, data, pk: TenSafePublicKey, seed=None) -> TenSafeCiphertext:
+        """lib.rs:142-164 (ciphertext.rs:240-319); pads / truncates to num_slots."""
+        return self.encrypt_pk_batch(np.atleast_2d(_f64(data)[: self._slots]), pk, [_seed(seed)])
+
+    def encrypt_pk_batch(self, data, pk: TenSafePublicKey, seeds) -> TenSafeCiphertext:
+        """Public-key encryption of each row with its own seed (B200 batch API)."""
+        x = np.ascontiguousarray(np.atleast_2d(np.asarray(data, dtype=np.float64)))
+        s = np.ascontiguousarray(seeds, dtype=np.uint64)
+        if s.size != x.shape[0]:
+            raise ValueError("one seed per row required")
+        h = C.c_void_p()
+        check(lib().ts_encrypt_pk(self.handle, pk.handle, x.ctypes.data if x.size else None, x.shape[0], x.shape[1],
+                                  x.shape[1], ptr(s, C.c_uint64), 0, C.byref(h)), "ts_encrypt_pk")
+        return TenSafeCiphertext(self, h)
+
+    def rescale(self, ct: "TenSafeCiphertext") -> "TenSafeCiphertext":
+        """lib.rs:218-225 (ciphertext.rs:476-535): drop the last limb, scale / q_last.
+        ValueError with one limb (the reference panics)."""
+        h = C.c_void_p()
+        check(lib().ts_rescale(self.handle, ct.handle, C.byref(h)), "ts_rescale")
+        return TenSafeCiphertext(self, h)
+
     def encrypt(self, data, sk: TenSafeSecretKey, seed=None) -> TenSafeCiphertext:
         x = _f64(data)
         h = C.c_void_p()

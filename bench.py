@@ -46,6 +46,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=2048, help="hidden states per GPU per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-micro", action="store_true", help="skip the NTT / Hadamard microbenchmarks")
+    ap.add_argument("--no-c3", action="store_true", help="skip the HE decode-step (Qwen-shaped) measurement")
     return ap.parse_args()
 
 
@@ -368,6 +369,10 @@ def run_ours(args):
     if rank == 0 and not args.no_micro:
         micro = ntt_micro(dev, peak)
 
+    c3 = None
+    if rank == 0 and world == 1 and not args.no_c3:
+        c3 = c3_leg(dev)
+
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = cpu_baseline_leg()
@@ -386,6 +391,8 @@ def run_ours(args):
         }
         if micro:
             line["ntt_c2"] = micro
+        if c3:
+            line["c3"] = c3
         print(json.dumps(line))
     if world > 1:
         dist.barrier()
@@ -400,6 +407,50 @@ def ntt_micro(dev, peak):
     out = microbench.ntt(1024, 10, dev.index, peak)
     out["hadamard"] = microbench.hadamard(1024, 4, dev.index, peak)
     return out
+
+
+def c3_leg(dev, tokens: int = 16):
+    """C3: HE tok/s of greedy decode on a random-init Qwen2.5-1.5B-shaped
+    model (28 layers, bf16) with encrypted LoRA (rank 16, 3 CryptoMOE
+    experts, top-1 router over uniform logits) on q_proj and v_proj of every
+    layer and post-transformer DP noise (C = 1, eps = 1, delta = 1e-5),
+    N = 16384.  Timed with CUDA events around whole generate() calls on
+    torch's stream, which the library shares; the same decode without HE is
+    timed beside it."""
+    import torch
+
+    from provenloop_b200 import tensafe_he
+    from provenloop_b200.decode_step import HeLoraDecoder, build_model
+
+    with torch.cuda.device(dev):
+        model = build_model(device=dev, seed=2)
+        ctx = tensafe_he.CkksContext(16384, device=dev.index)
+        dec = HeLoraDecoder(model, ctx, ctx.keygen(2), rank=16, experts=3, seed=2)
+        prompt = [151643]
+
+        def timed(enabled):
+            dec.enabled = enabled
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            torch.cuda.synchronize(dev)
+            ev[0].record()
+            dec.generate(prompt, tokens=tokens)
+            ev[1].record()
+            torch.cuda.synchronize(dev)
+            return ev[0].elapsed_time(ev[1])
+
+        timed(True)  # warm-up: kernels, caches, allocator
+        timed(False)
+        plain_ms = timed(False)
+        he_ms = timed(True)
+        dec.remove()
+        del model
+        torch.cuda.empty_cache()
+    return {"workload": "Qwen2.5-1.5B-shaped greedy decode, random init bf16, 28 layers; HE-LoRA r=16 on q_proj "
+                        "and v_proj of every layer (one encryption per layer shared by q and v), 3 experts, "
+                        "post-transformer DP noise; CKKS N=16384",
+            "tokens": tokens, "batch": 1, "he_tok_s": tokens / (he_ms / 1e3),
+            "plain_tok_s": tokens / (plain_ms / 1e3), "he_ms_per_token": he_ms / tokens,
+            "plain_ms_per_token": plain_ms / tokens, "he_ms_per_layer": (he_ms - plain_ms) / tokens / 28}
 
 
 def main():

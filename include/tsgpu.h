@@ -217,7 +217,9 @@ int ts_lora_delta_batch(ts_ctx* ctx, const ts_sk* sk, const ts_lora* lora, const
 
 /* Post-transformer DP noise (inference_engine.py:1436-1456) on the device:
  * clip each row of h [n][d] to L2 norm <= clip, add N(0, sigma^2) drawn from
- * the ChaCha20 stream of seeds[i] (Box-Muller as rng.rs:152-157). */
+ * the ChaCha20 stream of seeds[i] (Box-Muller as rng.rs:152-157).  With
+ * on_device = 1, h is a device pointer and the call returns without waiting:
+ * the result is ready in stream order on the context's stream. */
 int ts_dp_noise(ts_ctx* ctx, double* h, uint32_t n, uint32_t d, double clip, double sigma, const uint64_t* seeds,
                 int on_device);
 

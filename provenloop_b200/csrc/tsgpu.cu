@@ -190,9 +190,15 @@ struct ts_ctx {
     // grow-only scratch
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
-    void* pinned = nullptr;
-    size_t pinned_bytes = 0;
-    cudaEvent_t pinned_free = nullptr;  // recorded after the last copy out of `pinned`
+    // Ring of pinned staging slots for the small per-call inputs (seeds,
+    // indexes).  A call takes the next slot and waits only until that slot's
+    // previous copy has left it, so back-to-back calls (one per layer of a
+    // decode step) do not wait for the GPU.
+    static constexpr int kPinnedSlots = 8;
+    void* pinned[kPinnedSlots] = {};
+    size_t pinned_bytes[kPinnedSlots] = {};
+    cudaEvent_t pinned_free[kPinnedSlots] = {};  // recorded after the copy out of the slot
+    int pinned_next = 0;
 };
 
 struct ts_sk {
@@ -277,17 +283,22 @@ int ensure_scratch(ts_ctx* c, size_t bytes) {
 
 // Pinned staging buffer for small per-call inputs; waits until the previous
 // asynchronous copy out of it has executed before it is reused.
-int ensure_pinned(ts_ctx* c, size_t bytes) {
-    if (!c->pinned_free) CU(cudaEventCreateWithFlags(&c->pinned_free, cudaEventDisableTiming));
-    CU(cudaEventSynchronize(c->pinned_free));
-    if (bytes <= c->pinned_bytes) return TS_OK;
-    if (c->pinned) {
-        CU(cudaFreeHost(c->pinned));
-        c->pinned = nullptr;
-        c->pinned_bytes = 0;
+// Next pinned staging slot of at least `bytes`; *slot receives its index.
+// The caller records pinned_free[*slot] after its copy out of the slot.
+int ensure_pinned(ts_ctx* c, size_t bytes, int* slot) {
+    const int k = c->pinned_next;
+    c->pinned_next = (k + 1) % ts_ctx::kPinnedSlots;
+    if (!c->pinned_free[k]) CU(cudaEventCreateWithFlags(&c->pinned_free[k], cudaEventDisableTiming));
+    CU(cudaEventSynchronize(c->pinned_free[k]));
+    *slot = k;
+    if (bytes <= c->pinned_bytes[k]) return TS_OK;
+    if (c->pinned[k]) {
+        CU(cudaFreeHost(c->pinned[k]));
+        c->pinned[k] = nullptr;
+        c->pinned_bytes[k] = 0;
     }
-    CU(cudaMallocHost(&c->pinned, bytes));
-    c->pinned_bytes = bytes;
+    CU(cudaMallocHost(&c->pinned[k], bytes));
+    c->pinned_bytes[k] = bytes;
     return TS_OK;
 }
 
@@ -648,8 +659,10 @@ int ts_ctx_destroy(ts_ctx* c) {
     if (c->own) cudaStreamSynchronize(c->own);
     if (c->stream && c->stream != c->own) cudaStreamSynchronize(c->stream);
     if (c->scratch) cudaFree(c->scratch);
-    if (c->pinned) cudaFreeHost(c->pinned);
-    if (c->pinned_free) cudaEventDestroy(c->pinned_free);
+    for (int k = 0; k < ts_ctx::kPinnedSlots; k++) {
+        if (c->pinned[k]) cudaFreeHost(c->pinned[k]);
+        if (c->pinned_free[k]) cudaEventDestroy(c->pinned_free[k]);
+    }
     cudaFree(c->d_tw);
     cudaFree(c->d_tabs);
     cudaFree(c->d_fft);
@@ -1279,9 +1292,10 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
     const double scale2 = c->dc.scale * c->dc.scale;
     // small per-delta inputs: staged once through pinned memory (async H2D)
     const size_t sm_bytes = (size_t)n * 8 + (size_t)n * 4 * 2 + 512;
-    rc = ensure_pinned(c, sm_bytes);
+    int slot = 0;
+    rc = ensure_pinned(c, sm_bytes, &slot);
     if (rc) return rc;
-    uint64_t* p_seeds = static_cast<uint64_t*>(c->pinned);
+    uint64_t* p_seeds = static_cast<uint64_t*>(c->pinned[slot]);
     int* p_ex = reinterpret_cast<int*>(p_seeds + n);
     int* p_sk = p_ex + n;
     memcpy(p_seeds, seeds, (size_t)n * 8);
@@ -1290,8 +1304,8 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
     void* small = nullptr;
     rc = dev_alloc(c, &small, sm_bytes);
     if (rc) return rc;
-    CU(cudaMemcpyAsync(small, c->pinned, sm_bytes - 512, cudaMemcpyHostToDevice, c->stream));
-    CU(cudaEventRecord(c->pinned_free, c->stream));
+    CU(cudaMemcpyAsync(small, c->pinned[slot], sm_bytes - 512, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaEventRecord(c->pinned_free[slot], c->stream));
     const uint64_t* d_seeds_all = static_cast<uint64_t*>(small);
     const int* d_ex_all = reinterpret_cast<const int*>(d_seeds_all + n);
     const int* d_sk_all = d_ex_all + n;
@@ -1371,11 +1385,18 @@ int ts_dp_noise(ts_ctx* c, double* h, uint32_t n, uint32_t d, double clip, doubl
     double* dh = on_device ? h : static_cast<double*>(buf);
     uint64_t* ds = reinterpret_cast<uint64_t*>(static_cast<char*>(buf) + (on_device ? 0 : (((size_t)n * d * 8 + 255) & ~(size_t)255)));
     if (!on_device) rc = h2d_small(c, dh, h, (size_t)n * d);
-    if (!rc) rc = h2d_small(c, ds, seeds, n);
+    // seeds through a pinned slot, so that device-resident calls never wait
+    int slot = 0;
+    if (!rc) rc = ensure_pinned(c, (size_t)n * 8, &slot);
     if (!rc) {
-        cudaError_t e = launch_dp_noise(dh, (int)n, (int)d, clip, sigma, ds, c->stream);
-        if (e == cudaSuccess && !on_device) e = cudaMemcpyAsync(h, dh, (size_t)n * d * 8, cudaMemcpyDeviceToHost, c->stream);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+        memcpy(c->pinned[slot], seeds, (size_t)n * 8);
+        cudaError_t e = cudaMemcpyAsync(ds, c->pinned[slot], (size_t)n * 8, cudaMemcpyHostToDevice, c->stream);
+        if (e == cudaSuccess) e = cudaEventRecord(c->pinned_free[slot], c->stream);
+        if (e == cudaSuccess) e = launch_dp_noise(dh, (int)n, (int)d, clip, sigma, ds, c->stream);
+        if (e == cudaSuccess && !on_device) {
+            e = cudaMemcpyAsync(h, dh, (size_t)n * d * 8, cudaMemcpyDeviceToHost, c->stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+        }
         if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "dp_noise: %s", cudaGetErrorString(e));
     }
     cudaFreeAsync(buf, c->stream);

@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-micro", action="store_true", help="skip the NTT / Hadamard microbenchmarks")
     ap.add_argument("--no-c3", action="store_true", help="skip the HE decode-step (Qwen-shaped) measurement")
+    ap.add_argument("--config", default="c1", choices=["c1", "c4"],
+                    help="c1: the headline single-key N=16384 workload; c4: 256 users with their own keys, "
+                         "N=32768 on [60,40,40,40,60], 28 layers x 2 projections of rank-32 adapters")
     return ap.parse_args()
 
 
@@ -453,10 +456,123 @@ def c3_leg(dev, tokens: int = 16):
             "plain_ms_per_token": plain_ms / tokens, "he_ms_per_layer": (he_ms - plain_ms) / tokens / 28}
 
 
+C4_USERS, C4_ADAPTERS, C4_R, C4_N = 256, 56, 32, 32768
+C4_BITS = [60, 40, 40, 40, 60]
+
+
+def run_c4(args):
+    """C4: multi-user batched HE-LoRA at N = 32768 (custom [60,40,40,40,60],
+    scale 2^40).  256 users, each with an independent secret key (seed 3 +
+    user id) and 28 layers x 2 projections of rank-32 adapters (d = 1536,
+    cols = 10, 4 plaintext batches); every step computes all 256 x 56 deltas
+    once.  Users are block-sharded over the ranks (weak scaling in users
+    would change the problem, so the total is fixed: strong scaling), and
+    rank 0 gathers the decrypted deltas over NCCL."""
+    import torch
+    import torch.distributed as dist
+
+    from provenloop_b200 import _lib, multigpu, tensafe_he
+    from provenloop_b200.backend import ZeroMoaiLora
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    u0, u1 = multigpu.user_block(C4_USERS, world, rank)
+    nu = u1 - u0
+    batch = nu * C4_ADAPTERS
+    rng = np.random.default_rng(3)
+    A = (rng.standard_normal((C4_ADAPTERS, C4_R, D)) * 0.02).astype(np.float32)
+    B = (rng.standard_normal((C4_ADAPTERS, D, C4_R)) * 0.02).astype(np.float32)
+    H = np.random.default_rng(3000 + rank).standard_normal((batch, D))
+    ctx = tensafe_he.CkksContext.custom(C4_N, C4_BITS, device=local)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    _lib.check(_lib.lib().ts_ctx_set_stream(ctx.handle, stream.cuda_stream), "set_stream")
+    sk = ctx.keygen_batch([3 + u for u in range(u0, u1)])
+    lora = ZeroMoaiLora(ctx, A, B)
+    h_dev = torch.from_numpy(H).to(dev)
+    delta_dev = torch.empty((batch, D), dtype=torch.float64, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    adapter = np.tile(np.arange(C4_ADAPTERS, dtype=np.int32), nu)
+    user_ix = np.repeat(np.arange(nu, dtype=np.int32), C4_ADAPTERS)
+    gid = (u0 + user_ix.astype(np.int64)) * C4_ADAPTERS + adapter   # global delta id
+
+    def step(i):
+        seeds = np.asarray([multigpu.stream_seed(int(g), i, C4_USERS * C4_ADAPTERS) for g in gid], dtype=np.uint64)
+        lora.delta_device(sk, h_dev, seeds, delta_dev, expert=adapter, sk_index=user_ix)
+        multigpu.gather_rows(delta_dev, world, rank)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = _lib.launch_count()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for k in range(args.steps):
+        flush.zero_()
+        ev[k][0].record(stream)
+        step(args.warmup + k)
+        ev[k][1].record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    launches = _lib.launch_count() - launches0
+    clk = clocks.stop()
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b in ev)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    total = C4_USERS * C4_ADAPTERS
+    value = total * args.steps / (max_ms / 1000.0)
+    # end to end through the host API (pinned host buffers), one step
+    h_pin = torch.from_numpy(H).pin_memory()
+    d_pin = torch.empty((batch, D), dtype=torch.float64).pin_memory()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    seeds = np.asarray([multigpu.stream_seed(int(g), 999, total) for g in gid], dtype=np.uint64)
+    lora.delta(sk, h_pin.numpy(), seeds, expert=adapter, sk_index=user_ix, out=d_pin.numpy(), want_inter=False)
+    e2e = torch.tensor([(time.perf_counter() - t0) * 1000.0], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        line = {
+            "metric": "encrypted LoRA deltas/sec (CKKS N=32768, [60,40,40,40,60], r=32, 256 users x 56 adapters)",
+            "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "u64", "data": "synthetic",
+            "config": {"workload": "C4 multi-user: 256 users (own keys) x 28 layers x 2 projections, one delta each "
+                                   "per step", "poly_degree": C4_N, "moduli_bits": C4_BITS, "scale_bits": 40,
+                       "d": D, "r": C4_R, "cols_per_ct": 10, "pt_batches": 4, "adapters": C4_ADAPTERS,
+                       "users": C4_USERS, "global_batch": total,
+                       "parallelism": "replicas" if world == 1 else f"users sharded over {world} ranks, NCCL gather"},
+            "e2e": {"value": total / (float(e2e.item()) / 1000.0), "unit": UNIT,
+                    "h2d_bytes_per_step": batch * D * 8, "d2h_bytes_per_step": batch * D * 8},
+            "clocks": clk, "gpu_launches": launches,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "c4":
+        run_c4(args)
     else:
         run_ours(args)
 

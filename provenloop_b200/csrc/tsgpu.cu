@@ -5,6 +5,7 @@
 // kernels.cu.  Parameter and table construction restates
 // tensafe-he-core/src/params.rs, rns.rs and encoding.rs (cited inline); all
 // per-ciphertext arithmetic runs on the GPU.
+#include <atomic>
 #include <algorithm>
 #include <cmath>
 #include <cstdarg>
@@ -173,6 +174,11 @@ static void fft_tables(uint32_t n, double* twist_re, double* twist_im, double* t
 // =====================================================================
 struct ts_ctx {
     std::mutex mu;
+    // One reference for the context handle and one per live key, public key,
+    // ciphertext, plaintext and adapter object: the context's memory is
+    // released when the last of them is destroyed, in whatever order that
+    // happens (a garbage collector may destroy a context before its objects).
+    std::atomic<int> refs{1};
     int device = 0;
     uint32_t n = 0, slots = 0, L = 0, scale_bits = 40;
     int logn = 0;
@@ -653,8 +659,11 @@ int ts_ctx_create_moduli(uint32_t poly_degree, const uint64_t* moduli, uint32_t 
     return build_ctx(poly_degree, moduli, num_limbs, 40, device, out);
 }
 
-int ts_ctx_destroy(ts_ctx* c) {
-    if (!c) return TS_OK;
+}  // extern "C"
+
+namespace {
+
+void ctx_free(ts_ctx* c) {
     cudaSetDevice(c->device);
     if (c->own) cudaStreamSynchronize(c->own);
     if (c->stream && c->stream != c->own) cudaStreamSynchronize(c->stream);
@@ -669,6 +678,26 @@ int ts_ctx_destroy(ts_ctx* c) {
     cudaFree(c->d_stats);
     if (c->own) cudaStreamDestroy(c->own);
     delete c;
+}
+
+}  // namespace
+
+// Reference bookkeeping of child objects (see ts_ctx::refs).
+template <class T>
+T* ctx_adopt(T* o) {
+    o->ctx->refs.fetch_add(1);
+    return o;
+}
+
+void ctx_release(ts_ctx* c) {
+    if (c->refs.fetch_sub(1) == 1) ctx_free(c);
+}
+
+extern "C" {
+
+int ts_ctx_destroy(ts_ctx* c) {
+    if (!c) return TS_OK;
+    ctx_release(c);
     return TS_OK;
 }
 
@@ -785,7 +814,7 @@ int ts_keygen_batch(ts_ctx* c, const uint64_t* seeds, uint32_t count, ts_sk** ou
         delete sk;
         return rc;
     }
-    *out = sk;
+    *out = ctx_adopt(sk);
     return TS_OK;
 }
 
@@ -793,10 +822,14 @@ int ts_keygen(ts_ctx* c, uint64_t seed, ts_sk** out) { return ts_keygen_batch(c,
 
 int ts_sk_destroy(ts_sk* sk) {
     if (!sk) return TS_OK;
-    Lock lk(sk->ctx);
-    cudaSetDevice(sk->ctx->device);
-    cudaFreeAsync(sk->d, sk->ctx->stream);
-    delete sk;
+    ts_ctx* c = sk->ctx;
+    {
+        Lock lk(c);
+        cudaSetDevice(c->device);
+        cudaFreeAsync(sk->d, c->stream);
+        delete sk;
+    }
+    ctx_release(c);
     return TS_OK;
 }
 
@@ -867,7 +900,7 @@ static int encrypt_impl(ts_ctx* c, const ts_sk* sk, const double* data, size_t c
         delete ct;
         return rc;
     }
-    *out = ct;
+    *out = ctx_adopt(ct);
     return TS_OK;
 }
 
@@ -886,10 +919,14 @@ int ts_encrypt_batch(ts_ctx* c, const ts_sk* sk, const double* data, size_t coun
 
 int ts_ct_destroy(ts_ct* ct) {
     if (!ct) return TS_OK;
-    Lock lk(ct->ctx);
-    cudaSetDevice(ct->ctx->device);
-    cudaFreeAsync(ct->d, ct->ctx->stream);
-    delete ct;
+    ts_ctx* c = ct->ctx;
+    {
+        Lock lk(c);
+        cudaSetDevice(c->device);
+        cudaFreeAsync(ct->d, c->stream);
+        delete ct;
+    }
+    ctx_release(c);
     return TS_OK;
 }
 
@@ -927,7 +964,7 @@ int ts_ct_import(ts_ctx* c, const uint64_t* c0, const uint64_t* c1, uint32_t lim
     CU(cudaMemcpyAsync(ct->d, c0, words * 8, cudaMemcpyHostToDevice, c->stream));
     CU(cudaMemcpyAsync(ct->d + words, c1, words * 8, cudaMemcpyHostToDevice, c->stream));
     CU(cudaStreamSynchronize(c->stream));
-    *out = ct;
+    *out = ctx_adopt(ct);
     return TS_OK;
 }
 
@@ -941,7 +978,7 @@ int ts_ct_select(ts_ctx* c, const ts_ct* ct, uint32_t index, ts_ct** out) {
     if (rc) return rc;
     const size_t words = (size_t)2 * ct->limbs * c->n;
     CU(cudaMemcpyAsync(o->d, ct->d + index * words, words * 8, cudaMemcpyDeviceToDevice, c->stream));
-    *out = o;
+    *out = ctx_adopt(o);
     return TS_OK;
 }
 
@@ -1049,16 +1086,20 @@ int ts_encode_ntt(ts_ctx* c, const double* pts, size_t count, size_t len, size_t
         delete pt;
         return rc;
     }
-    *out = pt;
+    *out = ctx_adopt(pt);
     return TS_OK;
 }
 
 int ts_pt_destroy(ts_pt* pt) {
     if (!pt) return TS_OK;
-    Lock lk(pt->ctx);
-    cudaSetDevice(pt->ctx->device);
-    cudaFreeAsync(pt->d, pt->ctx->stream);
-    delete pt;
+    ts_ctx* c = pt->ctx;
+    {
+        Lock lk(c);
+        cudaSetDevice(c->device);
+        cudaFreeAsync(pt->d, c->stream);
+        delete pt;
+    }
+    ctx_release(c);
     return TS_OK;
 }
 
@@ -1085,7 +1126,7 @@ static int ct_pt_mul_dev(ts_ctx* c, const ts_ct* ct, const uint64_t* d_pt, ts_ct
         delete o;
         return fail(TS_ERR_CUDA, "ct_pt_mul: %s", cudaGetErrorString(e));
     }
-    *out = o;
+    *out = ctx_adopt(o);
     return TS_OK;
 }
 
@@ -1138,7 +1179,7 @@ static int ct_addsub(ts_ctx* c, const ts_ct* a, const ts_ct* b, ts_ct** out, boo
         delete o;
         return fail(TS_ERR_CUDA, "ct_add: %s", cudaGetErrorString(e));
     }
-    *out = o;
+    *out = ctx_adopt(o);
     return TS_OK;
 }
 
@@ -1246,18 +1287,22 @@ int ts_lora_load(ts_ctx* c, const float* A, const float* B, uint32_t experts, ui
         delete lo;
         return rc;
     }
-    *out = lo;
+    *out = ctx_adopt(lo);
     return TS_OK;
 }
 
 int ts_lora_destroy(ts_lora* lo) {
     if (!lo) return TS_OK;
-    Lock lk(lo->ctx);
-    cudaSetDevice(lo->ctx->device);
-    cudaFreeAsync(lo->d_pt, lo->ctx->stream);
-    cudaFreeAsync(lo->d_b, lo->ctx->stream);
-    if (lo->d_w) cudaFreeAsync(lo->d_w, lo->ctx->stream);
-    delete lo;
+    ts_ctx* c = lo->ctx;
+    {
+        Lock lk(c);
+        cudaSetDevice(c->device);
+        cudaFreeAsync(lo->d_pt, c->stream);
+        cudaFreeAsync(lo->d_b, c->stream);
+        if (lo->d_w) cudaFreeAsync(lo->d_w, c->stream);
+        delete lo;
+    }
+    ctx_release(c);
     return TS_OK;
 }
 
@@ -1443,16 +1488,20 @@ int ts_keygen_public(ts_ctx* c, const ts_sk* sk, uint32_t sk_index, uint64_t see
         delete pk;
         return rc;
     }
-    *out = pk;
+    *out = ctx_adopt(pk);
     return TS_OK;
 }
 
 int ts_pk_destroy(ts_pk* pk) {
     if (!pk) return TS_OK;
-    Lock lk(pk->ctx);
-    cudaSetDevice(pk->ctx->device);
-    cudaFreeAsync(pk->d, pk->ctx->stream);
-    delete pk;
+    ts_ctx* c = pk->ctx;
+    {
+        Lock lk(c);
+        cudaSetDevice(c->device);
+        cudaFreeAsync(pk->d, c->stream);
+        delete pk;
+    }
+    ctx_release(c);
     return TS_OK;
 }
 
@@ -1535,7 +1584,7 @@ int ts_encrypt_pk(ts_ctx* c, const ts_pk* pk, const double* data, size_t count, 
         delete ct;
         return rc;
     }
-    *out = ct;
+    *out = ctx_adopt(ct);
     return TS_OK;
 }
 
@@ -1575,7 +1624,7 @@ int ts_rescale(ts_ctx* c, const ts_ct* ct, ts_ct** out) {
         delete o;
         return rc;
     }
-    *out = o;
+    *out = ctx_adopt(o);
     return TS_OK;
 }
 
@@ -1683,7 +1732,7 @@ int ts_encrypt_stream(ts_ctx* c, const ts_sk* sk, const double* data, size_t cou
         delete ct;
         return rc;
     }
-    *out = ct;
+    *out = ctx_adopt(ct);
     return TS_OK;
 }
 

@@ -15,6 +15,7 @@ Use it where the inference engine does ``import tensafe_he``
 from __future__ import annotations
 
 import ctypes as C
+import sys
 import os
 import struct
 
@@ -65,6 +66,10 @@ class _Handle:
             self._destroy(h)
 
     def __del__(self):
+        # at interpreter exit the CUDA runtime may already be torn down; the
+        # process releases everything anyway
+        if sys.is_finalizing():
+            return
         try:
             self.close()
         except Exception:

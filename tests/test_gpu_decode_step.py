@@ -40,6 +40,7 @@ def test_decode_step_deltas_match_plaintext(T):
         assert np.abs(dq - ref_q).max() < 1e-4
         assert np.abs(dv - ref_v).max() < 1e-4
     assert len(seen) == 3
+    dec.remove()
 
 
 def test_device_dp_noise_matches_host(T):

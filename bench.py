@@ -529,6 +529,20 @@ def run_c4(args):
     launches = _lib.launch_count() - launches0
     clk = clocks.stop()
     t = torch.tensor([sum(a.elapsed_time(b) for a, b in ev)], dtype=torch.float64, device=dev)
+    # per-kernel time: the same steps again, every launch bracketed by events
+    _lib.profile_reset()
+    _lib.profile_enable(True)
+    for k in range(args.steps):
+        flush.zero_()
+        step(args.warmup + args.steps + k)
+    torch.cuda.synchronize(dev)
+    _lib.profile_enable(False)
+    kern = {}
+    for name in ("encode", "encode_a", "encode_b", "enc_a", "enc_u", "plan", "gauss_fix", "enc_a_fix", "enc_u_fix",
+                 "decrypt_limb", "crt_seg", "dec_fused", "gather_inter", "bmat"):
+        ms, n = _lib.profile_read(name)
+        if n:
+            kern[name] = ms / args.steps
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     max_ms = float(t.item())
@@ -559,7 +573,7 @@ def run_c4(args):
                        "parallelism": "replicas" if world == 1 else f"users sharded over {world} ranks, NCCL gather"},
             "e2e": {"value": total / (float(e2e.item()) / 1000.0), "unit": UNIT,
                     "h2d_bytes_per_step": batch * D * 8, "d2h_bytes_per_step": batch * D * 8},
-            "clocks": clk, "gpu_launches": launches,
+            "clocks": clk, "gpu_launches": launches, "kernels_ms_per_step": kern,
         }
         print(json.dumps(line))
     if world > 1:

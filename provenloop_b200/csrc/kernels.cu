@@ -356,9 +356,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
         if constexpr (C::CL == 2) cluster_sync();  // the transform reads both shares
         else __syncthreads();
         uint64_t* out = sk + (((size_t)key * L + limb) << LOGN);
-        const SmemView<LOGN> in = ntt_smem_view<LOGN>(sm);
-        ntt_forward_block<LOGN>(
-            sm, T, [&](int j) { return in(j); }, [&](int j, uint64_t x) { out[j] = x; });
+        ntt_forward_from_smem<LOGN>(sm, T, [&](int j, uint64_t x) { out[j] = x; });
         __syncthreads();
     }
 }
@@ -819,9 +817,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
         }
         if constexpr (C::CL == 2) cluster_sync();  // the transform reads both shares
         else __syncthreads();
-        const SmemView<LOGN> in = ntt_smem_view<LOGN>(sm);
-        ntt_forward_block<LOGN>(
-            sm, T, [&](int j) { return in(j); }, [&](int j, uint64_t x) { c1[j] = x; });
+        ntt_forward_from_smem<LOGN>(sm, T, [&](int j, uint64_t x) { c1[j] = x; });
         __syncthreads();
     }
 }
@@ -1179,8 +1175,8 @@ template <int LOGN>
 __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     k_decrypt_limb(uint64_t* __restrict__ M, int nl, const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs,
                    const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
-                   const uint64_t* __restrict__ pt, const int* __restrict__ pt_sel, int per_ct,
-                   const LimbTab* __restrict__ tabs, int L) {
+                   const uint64_t* __restrict__ pt, const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel,
+                   int per_ct, const LimbTab* __restrict__ tabs, int L) {
     extern __shared__ __align__(16) uint64_t sm[];
     const int limb = blockIdx.x / NttCfg<LOGN>::CL, v = blockIdx.y;
     const LimbTab T = tabs[limb];
@@ -1191,14 +1187,18 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     const uint64_t* s = sk + so;
     const uint64_t* sp = sks + so;
     const uint64_t* p = nullptr;
+    const uint64_t* pp = nullptr;
     if (pt) {
         const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
         p = pt + (((size_t)pv * L + limb) << LOGN);
+        if (pts) pp = pts + (((size_t)pv * L + limb) << LOGN);
     }
     uint64_t* out = M + (((size_t)v * nl + limb) << LOGN);
     ntt_inverse_block<LOGN>(
         sm, T,
         [&](int j) {
+            if (pp)  // p*(c0 + c1*s) = c0*p + (c1*p)*s: two Shoup products, in [0, 4q)
+                return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q);
             uint64_t a0 = c0[j], a1 = c1[j];
             if (p) {
                 const uint64_t pj = p[j];
@@ -1212,7 +1212,8 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
 
 cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uint64_t* cts, long long ct_stride,
                                  int ct_limbs, const uint64_t* sk, const uint64_t* sks, const int* sk_of,
-                                 const uint64_t* pt, const int* pt_sel, int per_ct, int nvec, cudaStream_t s) {
+                                 const uint64_t* pt, const int* pt_sel, int per_ct, int nvec, cudaStream_t s,
+                                 const uint64_t* pts) {
     if (nvec <= 0) return cudaSuccess;
     TSG_LOGN_SWITCH(c.logn, {
         constexpr size_t smem = ntt_smem_bytes<LG>();
@@ -1221,7 +1222,7 @@ cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uin
         if (er != cudaSuccess) return er;
         KScope ks("decrypt_limb", s);
         return launch_cl(CL, k_decrypt_limb<LG>, dim3(nl * CL, nvec), NttCfg<LG>::NT, smem, s, M, nl, cts, ct_stride,
-                         ct_limbs, sk, sks, sk_of, pt, pt_sel, per_ct, c.tabs, c.L);
+                         ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L);
     });
     return cudaGetLastError();
 }
@@ -1373,10 +1374,11 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     constexpr int N = C::N, NT = C::NT, CL = C::CL;
     const int tid = threadIdx.x;
     // persistent over transform groups (one CTA, or a cluster pair for
-    // CL = 2); each CTA keeps one limb-0 buffer, reused for every vector,
+    // CL = 2); each group keeps one limb-0 buffer, reused for every vector,
     // so the round trip stays in L2
     const int grp = blockIdx.x / CL, ngrp = gridDim.x / CL;
-    uint64_t* m0v = M0 + ((size_t)blockIdx.x << LOGN);
+    const int h = ntt_rank<LOGN>();
+    uint64_t* m0v = M0 + ((size_t)grp << LOGN);
     for (int v = grp; v < nvec; v += ngrp) {
         const int ci = v / per_ct;
         const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
@@ -1421,37 +1423,26 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
             auto ld = [&](int j) {
                 return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q);
             };
-            if constexpr (CL == 1) {
-                // the last pass parks element j in sm[pad(j)], a slot only
-                // this thread reads or writes from then on
-                auto st = [&](int j, uint64_t x) { sm[pad(j)] = x; };
-                ntt_inverse_impl<LOGN, NC1>(sm, T, ld, st);
-            } else {
-                // the last pass's elements span both halves: combine each
-                // with its limb-0 value (written by this thread) on the spot
-                auto st = [&](int j, uint64_t x) {
-                    const double coeff = __dmul_rn(crt_coeff(m0v[j], x, K), inv_scale);
-#pragma unroll
-                    for (int c = 0; c < kMaxSegCols; c++)
-                        if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
-                };
-                ntt_inverse_impl<LOGN, NC1>(sm, T, ld, st);
-            }
+            // the last pass parks element j in the shared memory of the CTA
+            // that holds j (its own for CL = 1, either for CL = 2); for CL = 2
+            // both CTAs' parks (and limb-0 writes) are complete on return
+            ntt_inverse_to_smem<LOGN, NC1>(sm, T, ld);
         }
-        if constexpr (CL == 1) {
-            // CRT, / Delta^2 and the segment functionals over this thread's
-            // elements j = tid + k * NT; limb-0 loads issued in groups of 8
-            // ahead of their arithmetic
+        // CRT, / Delta^2 and the segment functionals over this CTA's share
+        // j = h*H + tid + k*NT; limb-0 loads issued in groups of 8 ahead of
+        // their arithmetic
+        {
             constexpr int G = 8;
 #pragma unroll 1
-            for (int k0 = 0; k0 < N / NT; k0 += G) {
+            for (int k0 = 0; k0 < C::E; k0 += G) {
                 uint64_t m0r[G];
 #pragma unroll
-                for (int kk = 0; kk < G; kk++) m0r[kk] = m0v[tid + (k0 + kk) * NT];
+                for (int kk = 0; kk < G; kk++) m0r[kk] = m0v[h * C::H + tid + (k0 + kk) * NT];
 #pragma unroll
                 for (int kk = 0; kk < G; kk++) {
-                    const int j = tid + (k0 + kk) * NT;
-                    const double coeff = __dmul_rn(crt_coeff(m0r[kk], sm[pad(j)], K), inv_scale);
+                    const int jl = tid + (k0 + kk) * NT;
+                    const int j = h * C::H + jl;
+                    const double coeff = __dmul_rn(crt_coeff(m0r[kk], sm[pad(jl)], K), inv_scale);
 #pragma unroll
                     for (int c = 0; c < kMaxSegCols; c++)
                         if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
@@ -1506,7 +1497,7 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
         constexpr size_t smem = ntt_smem_bytes<LG>();
         constexpr int CL = NttCfg<LG>::CL;
         // one CTA per SM (the padded share fills most of shared memory); M0
-        // holds one limb per CTA
+        // holds one limb per group (CTA, or cluster pair)
         const int groups = nvec < c.sms / CL ? nvec : c.sms / CL;
         auto kern = nc0 ? (nc1 ? k_dec_fused<LG, true, true> : k_dec_fused<LG, true, false>)
                         : (nc1 ? k_dec_fused<LG, false, true> : k_dec_fused<LG, false, false>);
@@ -1516,6 +1507,50 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
         return launch_cl(CL, kern, dim3(groups * CL), NttCfg<LG>::NT, smem, s, cts, ct_stride, ct_limbs, sk, sks,
                          sk_of, pt, pts, pt_sel, per_ct, nvec, c.tabs, c.L, c.crt, inv_scale, W, seg_cols, M0, seg_out);
     });
+    return cudaGetLastError();
+}
+
+// CRT of limbs 0/1, / scale and the segment functionals, for decrypts whose
+// INTT ran separately (N = 32768: one limb per CTA pair keeps the cluster
+// kernel lean).  One block per vector v of M [nvec][2][n].
+__global__ void __launch_bounds__(256)
+    k_crt_seg(const uint64_t* __restrict__ M, int logn, CrtConst K, double inv_scale, const double* __restrict__ W,
+              int cols, double* __restrict__ seg_out) {
+    const int n = 1 << logn, v = blockIdx.x, tid = threadIdx.x;
+    const uint64_t* m0 = M + ((size_t)v * 2 << logn);
+    const uint64_t* m1 = m0 + n;
+    double acc[kMaxSegCols];
+#pragma unroll
+    for (int c = 0; c < kMaxSegCols; c++) acc[c] = 0.0;
+    for (int j = tid; j < n; j += blockDim.x) {
+        const double coeff = __dmul_rn(crt_coeff(m0[j], m1[j], K), inv_scale);
+#pragma unroll
+        for (int c = 0; c < kMaxSegCols; c++)
+            if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * n + j), acc[c]);
+    }
+    __shared__ double red[8][kMaxSegCols];
+    const int lane = tid & 31, wid = tid >> 5;
+#pragma unroll
+    for (int c = 0; c < kMaxSegCols; c++) {
+        double a = acc[c];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) red[wid][c] = a;
+    }
+    __syncthreads();
+    if (tid < cols) {
+        double a = 0.0;
+        for (int w = 0; w < 8; w++) a += red[w][tid];
+        seg_out[(size_t)v * cols + tid] = a;
+    }
+}
+
+cudaError_t launch_crt_seg(const DevCtx& c, const uint64_t* M, int nvec, double inv_scale, const double* W,
+                           int seg_cols, double* seg_out, cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    if (seg_cols < 1 || seg_cols > kMaxSegCols || c.L < 2) return cudaErrorInvalidValue;
+    KScope ks("crt_seg", s);
+    k_crt_seg<<<nvec, 256, 0, s>>>(M, c.logn, c.crt, inv_scale, W, seg_cols, seg_out);
     return cudaGetLastError();
 }
 

@@ -159,13 +159,15 @@ cudaError_t launch_keygen_fix(const DevCtx& c, uint64_t* sk, const uint64_t* see
 // Decrypt front half: M[v][j][n] = INTT( c0 (+) c1*s ) for limbs j < nl, where
 // the ciphertext of vector v is cts + ct_of(v)*ct_stride and, when pt !=
 // null, both components are first multiplied by pt + pt_of(v)*L*n
-// (ct x pt fused into decrypt; ciphertext.rs:408-429 then :327-349).
+// (ct x pt fused into decrypt; ciphertext.rs:408-429 then :327-349).  With
+// pts (the plaintexts' Shoup companions) the product is formed as
+// p*(c0 + c1*s) with two Shoup products.
 // ct_of(v) = v / per_ct, pt_of(v) = (pt_sel ? pt_sel[v / per_ct] : 0)*per_ct + v % per_ct.
 // sks holds the keys' Shoup companions.
 cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uint64_t* cts, long long ct_stride,
                                  int ct_limbs, const uint64_t* sk, const uint64_t* sks, const int* sk_of,
-                                 const uint64_t* pt,
-                                 const int* pt_sel, int per_ct, int nvec, cudaStream_t s);
+                                 const uint64_t* pt, const int* pt_sel, int per_ct, int nvec, cudaStream_t s,
+                                 const uint64_t* pts = nullptr);
 
 // Decrypt back half (ciphertext.rs:351-399 + encoding.rs:219-315): CRT of
 // limbs 0/1 (crt) or limb-0 centring, / scale, canonical embedding.
@@ -181,13 +183,19 @@ cudaError_t launch_decode(const DevCtx& c, const uint64_t* M, int nl, bool crt, 
 // of the decoded slots as the linear functional seg[c] = sum_j coeff_j W[c][j]
 // (W[c][j] = sum over the segment's slots k of cos(pi j (2k+1) / N)).
 // sks / pts hold the Shoup companions of the keys / plaintexts.
-// Supports seg_cols <= kMaxSegCols; M0 is [min(nvec, sms)][n] u64 scratch.
+// Supports seg_cols <= kMaxSegCols; M0 is [min(nvec, sms)][n] u64 scratch
+// (one limb per persistent group).
 constexpr int kMaxSegCols = 10;
 cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_stride, int ct_limbs,
                              const uint64_t* sk, const uint64_t* sks, const int* sk_of, const uint64_t* pt,
                              const uint64_t* pts, const int* pt_sel, int per_ct,
                              int nvec, double inv_scale, const double* W, int seg_cols, uint64_t* M0, double* seg_out,
                              cudaStream_t s);
+
+// seg_out[v][c] = sum_j CRT(M[v][0][j], M[v][1][j]) * inv_scale * W[c][j]:
+// the back half of the fused decrypt for INTT outputs already in M.
+cudaError_t launch_crt_seg(const DevCtx& c, const uint64_t* M, int nvec, double inv_scale, const double* W,
+                           int seg_cols, double* seg_out, cudaStream_t s);
 
 // delta[i][d] = sum_k B[d][k] * inter[i][k] (inference_engine.py:1392).
 cudaError_t launch_bmat(const float* B, const double* inter, double* delta, int nvec, int d, int r,

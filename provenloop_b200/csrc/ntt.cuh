@@ -131,6 +131,15 @@ __device__ __forceinline__ uint64_t* cluster_smem(uint64_t* sm, int rank) {
     return cooperative_groups::this_cluster().map_shared_rank(sm, rank);
 }
 
+// Padded local offset of element k*JS of a cross-half set, k < E/2.  A
+// set base sigma < JS has no bits in common with k*JS (a multiple of JS), so
+// pad(sigma + k*JS) = pad(sigma) + xoff(k): one base register per half plus
+// compile-time offsets.
+template <int LOGN>
+__host__ __device__ constexpr int xoff(int k) {
+    return k * NttCfg<LOGN>::JS + ((k * NttCfg<LOGN>::JS) >> 4);
+}
+
 // Rank of this CTA within its transform (0 unless CL = 2).
 template <int LOGN>
 __device__ __forceinline__ int ntt_rank() {
@@ -283,10 +292,10 @@ __device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulon
         static_assert(R == 5 && C::E == 32, "cluster NTT expects radix-32 passes");
         cluster_sync();
         const int sg = Geo<LOGN, R, TLOG>::sigma(h, tid, 0);
-        uint64_t* s0 = cluster_smem(sm, 0);
-        uint64_t* s1 = cluster_smem(sm, 1);
+        uint64_t* s0 = cluster_smem(sm, 0) + pad(sg);
+        uint64_t* s1 = cluster_smem(sm, 1) + pad(sg);
 #pragma unroll
-        for (int k = 0; k < C::E; k++) (k < C::E / 2 ? s0 : s1)[pad(sg + (k & (C::E / 2 - 1)) * C::JS)] = v[k];
+        for (int k = 0; k < C::E; k++) (k < C::E / 2 ? s0 : s1)[xoff<LOGN>(k & (C::E / 2 - 1))] = v[k];
     } else {
         smem_store<LOGN, R, TLOG>(sm, v, h, tid);
     }
@@ -301,8 +310,10 @@ __device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulon
 // that reuses `sm` afterwards must __syncthreads() first.  If ld reads `sm`,
 // each thread may only read the positions of its own first-pass elements
 // (through ntt_smem_view for CL = 2, after a cluster_sync).
-template <int LOGN, bool NC, class Ld, class St>
-__device__ __forceinline__ void ntt_forward_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
+// first(k, sigma) supplies element sigma + k*JS of the first-pass set
+// (k is a compile-time constant after unrolling).
+template <int LOGN, bool NC, class First, class St>
+__device__ __forceinline__ void ntt_forward_core(uint64_t* sm, const LimbTab& T, First& first, St& st) {
     using C = NttCfg<LOGN>;
     static_assert(LOGN >= 10 && LOGN <= 15, "NTT supports N in [1024, 32768]");
     static_assert(C::fwd_r(0) == C::RMAX, "the first pass takes RMAX stages");
@@ -313,7 +324,7 @@ __device__ __forceinline__ void ntt_forward_impl(uint64_t* sm, const LimbTab& T,
     // first pass: one set per thread, elements sigma + k*JS
     const int sg = h * C::NT + tid;
 #pragma unroll
-    for (int k = 0; k < C::E; k++) v[k] = ld(sg + k * C::JS);
+    for (int k = 0; k < C::E; k++) v[k] = first(k, sg);
     fwd_passes<LOGN, 0, NC>(sm, v, fw, T.q, h, tid);
     __syncthreads();
     // own share, coalesced: j = h*H + tid + k*NT
@@ -321,6 +332,31 @@ __device__ __forceinline__ void ntt_forward_impl(uint64_t* sm, const LimbTab& T,
     for (int k = 0; k < C::E; k++) {
         const int jl = tid + k * C::NT;
         st(h * C::H + jl, NC ? mod_u64(sm[pad(jl)], T.q, T.mu64) : canon8(sm[pad(jl)], T.q));
+    }
+}
+
+template <int LOGN, bool NC, class Ld, class St>
+__device__ __forceinline__ void ntt_forward_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
+    auto first = [&](int k, int sg) { return ld(sg + k * NttCfg<LOGN>::JS); };
+    ntt_forward_core<LOGN, NC>(sm, T, first, st);
+}
+
+// Forward transform of a poly-limb already staged in shared memory: each
+// CTA's share at its own padded local positions, complete (__syncthreads,
+// or cluster_sync for CL = 2) before the call.  The first pass reads it with
+// the half chosen at compile time, so no per-element address selection.
+template <int LOGN, class St>
+__device__ __forceinline__ void ntt_forward_from_smem(uint64_t* sm, const LimbTab& T, St st) {
+    using C = NttCfg<LOGN>;
+    if constexpr (C::CL == 2) {
+        const int sg0 = ntt_rank<LOGN>() * C::NT + threadIdx.x;
+        const uint64_t* s0 = cluster_smem(sm, 0) + pad(sg0);
+        const uint64_t* s1 = cluster_smem(sm, 1) + pad(sg0);
+        auto first = [&](int k, int) { return (k < C::E / 2 ? s0 : s1)[xoff<LOGN>(k & (C::E / 2 - 1))]; };
+        ntt_forward_core<LOGN, false>(sm, T, first, st);
+    } else {
+        auto first = [&](int k, int sg) { return sm[pad(sg + k * C::JS)]; };
+        ntt_forward_core<LOGN, false>(sm, T, first, st);
     }
 }
 
@@ -348,10 +384,10 @@ __device__ __forceinline__ void inv_passes(uint64_t* sm, uint64_t* v, const ulon
         static_assert(R == 5 && C::E == 32, "cluster NTT expects radix-32 passes");
         cluster_sync();
         const int sg = Geo<LOGN, R, TLOG>::sigma(h, tid, 0);
-        const uint64_t* s0 = cluster_smem(sm, 0);
-        const uint64_t* s1 = cluster_smem(sm, 1);
+        const uint64_t* s0 = cluster_smem(sm, 0) + pad(sg);
+        const uint64_t* s1 = cluster_smem(sm, 1) + pad(sg);
 #pragma unroll
-        for (int k = 0; k < C::E; k++) v[k] = (k < C::E / 2 ? s0 : s1)[pad(sg + (k & (C::E / 2 - 1)) * C::JS)];
+        for (int k = 0; k < C::E; k++) v[k] = (k < C::E / 2 ? s0 : s1)[xoff<LOGN>(k & (C::E / 2 - 1))];
         cluster_sync();
     } else {
         __syncthreads();
@@ -368,8 +404,9 @@ __device__ __forceinline__ void inv_passes(uint64_t* sm, uint64_t* v, const ulon
 // element j (< 4q) for j = rank*H + tid + k*NT, st(j, v) receives canonical
 // output j for j = sigma + k*JS, sigma = rank*NT + tid.  A caller that reuses
 // `sm` afterwards must __syncthreads() first.
-template <int LOGN, bool NC, class Ld, class St>
-__device__ __forceinline__ void ntt_inverse_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
+// sink(k, sigma, x) receives canonical output sigma + k*JS.
+template <int LOGN, bool NC, class Ld, class Sink>
+__device__ __forceinline__ void ntt_inverse_core(uint64_t* sm, const LimbTab& T, Ld& ld, Sink& sink) {
     using C = NttCfg<LOGN>;
     static_assert(LOGN >= 10 && LOGN <= 15, "NTT supports N in [1024, 32768]");
     const int tid = threadIdx.x;
@@ -386,7 +423,33 @@ __device__ __forceinline__ void ntt_inverse_impl(uint64_t* sm, const LimbTab& T,
     // last-pass set: elements sigma + k*JS (for CL = 1, sigma = tid)
     const int sg = h * C::NT + tid;
 #pragma unroll
-    for (int k = 0; k < C::E; k++) st(sg + k * C::JS, canon4(v[k], T.q));
+    for (int k = 0; k < C::E; k++) sink(k, sg, canon4(v[k], T.q));
+}
+
+template <int LOGN, bool NC, class Ld, class St>
+__device__ __forceinline__ void ntt_inverse_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
+    auto sink = [&](int k, int sg, uint64_t x) { st(sg + k * NttCfg<LOGN>::JS, x); };
+    ntt_inverse_core<LOGN, NC>(sm, T, ld, sink);
+}
+
+// Inverse transform whose canonical output is parked in shared memory: each
+// CTA's share at its own padded local positions (through DSMEM for CL = 2,
+// complete on return; for CL = 1 a thread's outputs are the positions
+// pad(tid + k*NT) it alone reads afterwards).
+template <int LOGN, bool NC, class Ld>
+__device__ __forceinline__ void ntt_inverse_to_smem(uint64_t* sm, const LimbTab& T, Ld& ld) {
+    using C = NttCfg<LOGN>;
+    if constexpr (C::CL == 2) {
+        const int sg0 = ntt_rank<LOGN>() * C::NT + threadIdx.x;
+        uint64_t* s0 = cluster_smem(sm, 0) + pad(sg0);
+        uint64_t* s1 = cluster_smem(sm, 1) + pad(sg0);
+        auto sink = [&](int k, int, uint64_t x) { (k < C::E / 2 ? s0 : s1)[xoff<LOGN>(k & (C::E / 2 - 1))] = x; };
+        ntt_inverse_core<LOGN, NC>(sm, T, ld, sink);
+        cluster_sync();
+    } else {
+        auto sink = [&](int k, int sg, uint64_t x) { sm[pad(sg + k * C::JS)] = x; };
+        ntt_inverse_core<LOGN, NC>(sm, T, ld, sink);
+    }
 }
 
 // Inverse transform, with the correction-free butterflies when

@@ -1362,9 +1362,9 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
                      i_ct = cv.add(nv * 2 * L * N * 8), i_m = cv.add(nv * N * 8), i_e = cv.add(nv * N),
                      i_fe = cv.add(nv * 2 * N * 8), i_fl = cv.add((2 * nv + 1) * 4),
                      i_pl = cv.add(nv * sizeof(StreamPlan)),
-                     // fused decrypt: one limb-0 buffer per CTA; otherwise both limbs of
-                     // every vector and the FFT scratch of the decode
-                     i_M = cv.add(lo->d_w ? (size_t)c->dc.sms * N * 8 : nv * nb * 2 * N * 8),
+                     // fused decrypt (N <= 16384): one limb-0 buffer per CTA; otherwise
+                     // both limbs of every vector (and the FFT scratch of the decode)
+                     i_M = cv.add(lo->d_w && c->logn < 15 ? (size_t)c->dc.sms * N * 8 : nv * nb * 2 * N * 8),
                      i_fd = cv.add(lo->d_w ? 0 : nv * nb * 2 * N * 8), i_sg = cv.add(nv * nb * cols * 8);
         rc = ensure_scratch(c, cv.total());
         if (rc) break;
@@ -1387,7 +1387,15 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         rc = encrypt_core(c, src, nv, ds, sk_index ? dsk : nullptr, sk->d, sk_shoup(sk), ct,
                           enc_work(cv, S, nv, eidx));
         if (rc) break;
-        if (lo->d_w) {
+        if (lo->d_w && c->logn == 15) {
+            // N = 32768: the limb-0 and limb-1 INTTs of every (delta, batch)
+            // run as separate cluster pairs, then one light kernel does the
+            // CRT and the segment functionals (:1311-1386)
+            CU(launch_decrypt_limbs(c->dc, M, 2, ct, (long long)2 * L * N, (int)L, sk->d, sk_shoup(sk),
+                                    sk_index ? dsk : nullptr, lo->d_pt, expert ? dex : nullptr, (int)nb,
+                                    (int)(nv * nb), c->stream, lo->d_pt + (size_t)lo->experts * nb * L * N));
+            CU(launch_crt_seg(c->dc, M, (int)(nv * nb), 1.0 / scale2, lo->d_w, (int)cols, sg, c->stream));
+        } else if (lo->d_w) {
             // 2+3. per (delta, batch): ct x packed_pt (limbs 0/1), c0 + c1*s, INTT,
             // CRT / Delta^2 and the segment sums of the decoded slots (:1311-1386)
             CU(launch_dec_fused(c->dc, ct, (long long)2 * L * N, (int)L, sk->d, sk_shoup(sk), sk_index ? dsk : nullptr,

@@ -417,9 +417,10 @@ def c3_leg(dev, tokens: int = 16):
     model (28 layers, bf16) with encrypted LoRA (rank 16, 3 CryptoMOE
     experts, top-1 router over uniform logits) on q_proj and v_proj of every
     layer and post-transformer DP noise (C = 1, eps = 1, delta = 1e-5),
-    N = 16384.  Timed with CUDA events around whole generate() calls on
-    torch's stream, which the library shares; the same decode without HE is
-    timed beside it."""
+    N = 16384.  The whole decode step (transformer, 28 HE-LoRA calls, DP
+    noise, greedy pick) is one CUDA graph replayed per token; timed with CUDA
+    events on its stream, beside the same graph without HE and the eager
+    (uncaptured) HE decode."""
     import torch
 
     from provenloop_b200 import tensafe_he
@@ -429,31 +430,43 @@ def c3_leg(dev, tokens: int = 16):
         model = build_model(device=dev, seed=2)
         ctx = tensafe_he.CkksContext(16384, device=dev.index)
         dec = HeLoraDecoder(model, ctx, ctx.keygen(2), rank=16, experts=3, seed=2)
-        prompt = [151643]
+        prompt = 151643
 
-        def timed(enabled):
-            dec.enabled = enabled
+        def timed(run):
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
             torch.cuda.synchronize(dev)
-            ev[0].record()
-            dec.generate(prompt, tokens=tokens)
-            ev[1].record()
+            ev[0].record(run.stream)
+            run(prompt, tokens)
+            ev[1].record(run.stream)
             torch.cuda.synchronize(dev)
             return ev[0].elapsed_time(ev[1])
 
-        timed(True)  # warm-up: kernels, caches, allocator
-        timed(False)
-        plain_ms = timed(False)
-        he_ms = timed(True)
+        he_run = dec.capture(max_len=tokens + 8)
+        timed(he_run)                        # warm replay
+        he_ms = timed(he_run)
+        dec.enabled = False
+        plain_run = dec.capture(max_len=tokens + 8)
+        timed(plain_run)
+        plain_ms = timed(plain_run)
+        dec.enabled = True
+        dec.generate([prompt], tokens=2)     # eager warm-up
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda.synchronize(dev)
+        ev[0].record()
+        dec.generate([prompt], tokens=tokens)
+        ev[1].record()
+        torch.cuda.synchronize(dev)
+        eager_ms = ev[0].elapsed_time(ev[1])
         dec.remove()
-        del model
+        del he_run, plain_run, model
         torch.cuda.empty_cache()
     return {"workload": "Qwen2.5-1.5B-shaped greedy decode, random init bf16, 28 layers; HE-LoRA r=16 on q_proj "
                         "and v_proj of every layer (one encryption per layer shared by q and v), 3 experts, "
-                        "post-transformer DP noise; CKKS N=16384",
+                        "post-transformer DP noise; CKKS N=16384; one CUDA graph per decode step",
             "tokens": tokens, "batch": 1, "he_tok_s": tokens / (he_ms / 1e3),
             "plain_tok_s": tokens / (plain_ms / 1e3), "he_ms_per_token": he_ms / tokens,
-            "plain_ms_per_token": plain_ms / tokens, "he_ms_per_layer": (he_ms - plain_ms) / tokens / 28}
+            "plain_ms_per_token": plain_ms / tokens, "he_ms_per_layer": (he_ms - plain_ms) / tokens / 28,
+            "eager_he_tok_s": tokens / (eager_ms / 1e3)}
 
 
 C4_USERS, C4_ADAPTERS, C4_R, C4_N = 256, 56, 32, 32768

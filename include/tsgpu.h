@@ -210,7 +210,12 @@ int ts_lora_info(const ts_lora* lora, uint32_t* experts, uint32_t* r, uint32_t* 
  * by expert expert[i]'s packed plaintexts, decrypt, sum each d-slot segment,
  * and apply B (inference_engine.py:1244-1392).  delta [n][d] f64,
  * intermediate [n][r] f64 (may be NULL).  expert / sk_index may be NULL (0).
- * io_on_device: h / delta / intermediate are device pointers. */
+ * io_on_device: 1 -- h / delta / intermediate are device pointers (the call
+ * returns once the work is queued on the context's stream); 2 -- seeds,
+ * expert and sk_index are device arrays as well, and the call then only
+ * enqueues stream work (no host copies or waits, so it can be captured in a
+ * CUDA graph once a first call has sized the context's scratch); their
+ * values are not range-checked on the host. */
 int ts_lora_delta_batch(ts_ctx* ctx, const ts_sk* sk, const ts_lora* lora, const double* h, uint32_t n,
                         const int32_t* expert, const int32_t* sk_index, const uint64_t* seeds, double* delta,
                         double* intermediate, int io_on_device);
@@ -219,7 +224,8 @@ int ts_lora_delta_batch(ts_ctx* ctx, const ts_sk* sk, const ts_lora* lora, const
  * clip each row of h [n][d] to L2 norm <= clip, add N(0, sigma^2) drawn from
  * the ChaCha20 stream of seeds[i] (Box-Muller as rng.rs:152-157).  With
  * on_device = 1, h is a device pointer and the call returns without waiting:
- * the result is ready in stream order on the context's stream. */
+ * the result is ready in stream order on the context's stream; with
+ * on_device = 2 the seeds are a device array too (stream work only). */
 int ts_dp_noise(ts_ctx* ctx, double* h, uint32_t n, uint32_t d, double clip, double sigma, const uint64_t* seeds,
                 int on_device);
 

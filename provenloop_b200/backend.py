@@ -151,6 +151,26 @@ class ZeroMoaiLora:
                                         1), "ts_lora_delta_batch")
 
 
+def _dptr(t, ctype=None):
+    if t is None:
+        return None
+    return t.data_ptr() if ctype is None else C.cast(t.data_ptr(), C.POINTER(ctype))
+
+
+def lora_delta_graphable(lora: "ZeroMoaiLora", sk, h_dev, seeds_dev, delta_dev, expert_dev=None, sk_index_dev=None,
+                         inter_dev=None):
+    """``ZeroMoaiLora.delta_device`` with the seeds (int64 / uint64 CUDA
+    tensor) and the optional expert / key indexes (int32 CUDA tensors) on the
+    device as well: the call only enqueues work on the context's stream, so
+    it can be captured in a CUDA graph after one uncaptured call of the same
+    size.  Indexes are not range-checked."""
+    n = int(h_dev.shape[0])
+    check(lib().ts_lora_delta_batch(lora._ctx.handle, sk.handle, lora.handle, h_dev.data_ptr(), n,
+                                    _dptr(expert_dev, C.c_int32), _dptr(sk_index_dev, C.c_int32),
+                                    _dptr(seeds_dev, C.c_uint64), delta_dev.data_ptr(), _dptr(inter_dev), 2),
+          "ts_lora_delta_batch")
+
+
 def he_lora_delta(ctx, sk, lora: ZeroMoaiLora, h_plain, seed=None, expert: int = 0):
     """``_he_lora_delta``'s encrypted branch for one hidden state
     (inference_engine.py:1244-1392).  Returns (delta, compute_ms, decrypt_ms,

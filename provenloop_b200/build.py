@@ -55,11 +55,12 @@ def build(force: bool = False, verbose: bool = False) -> str:
     nvcc = nvcc_path()
     objs = []
     procs = []
-    # the sources compile in parallel; --split-compile spreads the device
-    # optimisation of the large kernel file over the host's cores
+    # the sources compile in parallel (not --split-compile: its partitioning
+    # of the kernel file measured 10-20 % slower, run-to-run unstable code for
+    # the fused decrypt kernel)
     for s in SOURCES:
         obj = os.path.join(CSRC, s.replace(".cu", ".o"))
-        cmd = [nvcc, "-c", os.path.join(CSRC, s), "-o", obj, "--split-compile=0"] + flags(verbose)
+        cmd = [nvcc, "-c", os.path.join(CSRC, s), "-o", obj] + flags(verbose)
         procs.append((s, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
         objs.append(obj)
     for s, p in procs:

@@ -827,7 +827,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     k_enc_u(uint64_t* __restrict__ ct, const int64_t* __restrict__ m, const int8_t* __restrict__ e,
             const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
             const LimbTab* __restrict__ tabs, int L,
-            int nvec, const uint32_t* __restrict__ flags, int list_mode) {
+            int nvec, const uint32_t* __restrict__ flags, int list_mode, int sub) {
     extern __shared__ __align__(16) uint64_t sm[];
     using C = NttCfg<LOGN>;
     const int limb = blockIdx.x / C::CL;
@@ -843,7 +843,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
         const uint64_t* sp = sks + so;
         const int64_t* mv = m + ((size_t)v << LOGN);
         const int8_t* ev = e + ((size_t)v << LOGN);
-        if (threadIdx.x == 0) prefetch_l2(c1 + h0, (unsigned)C::H * 8u);  // this CTA's share, read by the epilogue
+        if (sub && threadIdx.x == 0) prefetch_l2(c1 + h0, (unsigned)C::H * 8u);  // this CTA's share, read by the epilogue
         ntt_forward_block<LOGN>(
             sm, T,
             [&](int j) {
@@ -852,11 +852,35 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
                 return add_mod(signed_residue(mv[j], T.q, T.mu64), ej >= 0 ? (uint64_t)ej : T.q + ej, T.q);
             },
             [&](int j, uint64_t x) {
+                if (!sub) {  // x alone; k_enc_combine subtracts c1*s later
+                    c0[j] = x;
+                    return;
+                }
                 // x - c1*s with the product in [0, 4q): x + 4q - as lies in [1, 5q)
                 const uint64_t as = mul_shoup4(c1[j], s[j], sp[j], T.q);
                 c0[j] = canon8(x + 4 * T.q - as, T.q);
             });
         __syncthreads();
+    }
+}
+
+// c0 -= c1*s over every limb of nvec ciphertexts, c0 holding NTT(m + e)
+// (the second half of k_enc_u when the two transforms ran concurrently).
+__global__ void k_enc_combine(uint64_t* __restrict__ ct, const uint64_t* __restrict__ sk,
+                              const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
+                              const LimbTab* __restrict__ tabs, int L, int logn, long long total) {
+    for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
+         t += (long long)gridDim.x * blockDim.x) {
+        const int j = (int)(t & ((1 << logn) - 1));
+        const long long vl = t >> logn;
+        const int l = (int)(vl % L);
+        const long long v = vl / L;
+        const uint64_t q = tabs[l].q;
+        uint64_t* c0 = ct + ((v * 2 * L + l) << logn);
+        const uint64_t* c1 = ct + ((v * 2 * L + L + l) << logn);
+        const size_t so = ((size_t)(sk_of ? sk_of[v] : 0) * L + l) << logn;
+        const uint64_t as = mul_shoup4(c1[j], sk[so + j], sks[so + j], q);
+        c0[j] = canon8(c0[j] + 4 * q - as, q);
     }
 }
 
@@ -881,8 +905,43 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
         }
         KScope ks(plan_mode ? "enc_u_fix" : "enc_u", s);
         return launch_cl(CL, k_enc_u<LG>, dim3(c.L * CL, gy), NttCfg<LG>::NT, smem, s, ct, m, e, sk, sks, sk_of, c.tabs,
-                         c.L, nvec, (const uint32_t*)flags, plan_mode ? 1 : 0);
+                         c.L, nvec, (const uint32_t*)flags, plan_mode ? 1 : 0, 1);
     });
+    return cudaGetLastError();
+}
+
+cudaError_t launch_encrypt_split(const DevCtx& c, uint64_t* ct, const int64_t* m, const int8_t* e, const uint64_t* sk,
+                                 const uint64_t* sks, const int* sk_of, const uint64_t* seeds, int nvec,
+                                 uint32_t* flags, const StreamPlan* plans, cudaStream_t s_a, cudaStream_t s_x) {
+    if (nvec <= 0) return cudaSuccess;
+    TSG_LOGN_SWITCH(c.logn, {
+        constexpr size_t smem = ntt_smem_bytes<LG>();
+        constexpr int CL = NttCfg<LG>::CL;
+        cudaError_t er = ensure_smem(k_enc_a<LG>, smem + kEncPlanWinBytes);
+        if (er != cudaSuccess) return er;
+        er = ensure_smem(k_enc_u<LG>, smem);
+        if (er != cudaSuccess) return er;
+        {
+            KScope ks("enc_a", s_a);
+            er = launch_cl(CL, k_enc_a<LG>, dim3(c.L * CL, nvec), NttCfg<LG>::NT, smem, s_a, ct, seeds, c.tabs, c.L,
+                           nvec, flags, plans, 0);
+            if (er != cudaSuccess) return er;
+        }
+        KScope ks("enc_x", s_x);
+        return launch_cl(CL, k_enc_u<LG>, dim3(c.L * CL, nvec), NttCfg<LG>::NT, smem, s_x, ct, m, e, sk, sks, sk_of,
+                         c.tabs, c.L, nvec, (const uint32_t*)flags, 0, 0);
+    });
+    return cudaGetLastError();
+}
+
+cudaError_t launch_enc_combine(const DevCtx& c, uint64_t* ct, const uint64_t* sk, const uint64_t* sks,
+                               const int* sk_of, int nvec, cudaStream_t s) {
+    if (nvec <= 0) return cudaSuccess;
+    const long long total = (long long)nvec * c.L << c.logn;
+    const long long blocks = (total + 255) / 256;
+    KScope ks("enc_combine", s);
+    k_enc_combine<<<(int)(blocks < 8 * 148 ? blocks : 8 * 148), 256, 0, s>>>(ct, sk, sks, sk_of, c.tabs, c.L, c.logn,
+                                                                             total);
     return cudaGetLastError();
 }
 

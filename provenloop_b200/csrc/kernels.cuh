@@ -110,6 +110,15 @@ cudaError_t launch_encode(const DevCtx& c, const SlotSrc& src, int nvec, int64_t
 // pt_ntt[v][L][n] = NTT(residues of m[v]) (ciphertext.rs:539-545).
 cudaError_t launch_ntt_signed(const DevCtx& c, uint64_t* out, const int64_t* m, int nvec, cudaStream_t s);
 
+// The speculative encryption split for latency (small batches): c1 = NTT(a)
+// on stream s_a concurrently with c0 = NTT(m + e) on stream s_x; the caller
+// joins the streams and runs launch_enc_combine (c0 -= c1*s) after both.
+cudaError_t launch_encrypt_split(const DevCtx& c, uint64_t* ct, const int64_t* m, const int8_t* e, const uint64_t* sk,
+                                 const uint64_t* sks, const int* sk_of, const uint64_t* seeds, int nvec,
+                                 uint32_t* flags, const StreamPlan* plans, cudaStream_t s_a, cudaStream_t s_x);
+cudaError_t launch_enc_combine(const DevCtx& c, uint64_t* ct, const uint64_t* sk, const uint64_t* sks,
+                               const int* sk_of, int nvec, cudaStream_t s);
+
 // Shoup companions out[i] = floor(in[i] * 2^64 / q_l) of canonical
 // residues, for `polys` consecutive poly-limbs whose limb index is poly % L.
 cudaError_t launch_shoup_companion(const DevCtx& c, uint64_t* out, const uint64_t* in, long long polys,

@@ -193,6 +193,10 @@ struct ts_ctx {
     unsigned long long* d_stats = nullptr;
     DevCtx dc{};
     cudaStream_t own = nullptr, stream = nullptr;
+    // second stream and fork / join events of the small-batch encryption,
+    // created by its first use
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     // grow-only scratch
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
@@ -524,8 +528,29 @@ int encrypt_core(ts_ctx* c, const SlotSrc& src, size_t count, const uint64_t* d_
         const int* skof = d_skof ? d_skof + v0 : nullptr;
         uint64_t* ct = d_ct + v0 * 2 * c->L * n;
         CU(cudaMemsetAsync(w.fl, 0, (2 * nv + 1) * 4, c->stream));
-        CU(launch_encode(c->dc, s, (int)nv, w.m, w.e, seeds, 2ULL * c->L * n, w.f, c->stream));
-        CU(launch_encrypt_limbs(c->dc, ct, w.m, w.e, d_sk, d_sks, skof, seeds, (int)nv, w.fl, w.pl, false, c->stream));
+        const int cl = c->logn >= 15 ? 2 : 1;
+        if ((int)(nv * c->L * cl * 2) <= c->dc.sms) {
+            // small batch (a decode step): latency, not throughput, matters.
+            // c1 = NTT(a) runs on a side stream while the encode and
+            // NTT(m + e) run on the context's stream; c0 -= c1*s after the join
+            if (!c->side) {
+                CU(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
+                CU(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
+                CU(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming));
+            }
+            CU(cudaEventRecord(c->ev_fork, c->stream));
+            CU(cudaStreamWaitEvent(c->side, c->ev_fork, 0));
+            CU(launch_encode(c->dc, s, (int)nv, w.m, w.e, seeds, 2ULL * c->L * n, w.f, c->stream));
+            CU(launch_encrypt_split(c->dc, ct, w.m, w.e, d_sk, d_sks, skof, seeds, (int)nv, w.fl, w.pl, c->side,
+                                    c->stream));
+            CU(cudaEventRecord(c->ev_join, c->side));
+            CU(cudaStreamWaitEvent(c->stream, c->ev_join, 0));
+            CU(launch_enc_combine(c->dc, ct, d_sk, d_sks, skof, (int)nv, c->stream));
+        } else {
+            CU(launch_encode(c->dc, s, (int)nv, w.m, w.e, seeds, 2ULL * c->L * n, w.f, c->stream));
+            CU(launch_encrypt_limbs(c->dc, ct, w.m, w.e, d_sk, d_sks, skof, seeds, (int)nv, w.fl, w.pl, false,
+                                    c->stream));
+        }
         // exact repair of the (rare) streams that met a rejection
         CU(launch_plan(c->dc, seeds, (int)nv, w.fl, w.pl, encrypt_segs(c->L), c->stream));
         CU(launch_gauss_fix(c->dc, w.e, seeds, (int)nv, w.fl, w.pl, (int)c->L, c->stream));
@@ -676,6 +701,12 @@ void ctx_free(ts_ctx* c) {
     cudaFree(c->d_tabs);
     cudaFree(c->d_fft);
     cudaFree(c->d_stats);
+    if (c->side) {
+        cudaStreamSynchronize(c->side);
+        cudaStreamDestroy(c->side);
+        cudaEventDestroy(c->ev_fork);
+        cudaEventDestroy(c->ev_join);
+    }
     if (c->own) cudaStreamDestroy(c->own);
     delete c;
 }
@@ -1324,9 +1355,13 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
     if (io_on_device && (!aligned(h, 8) || !aligned(delta, 8) || !aligned(inter, 8)))
         return fail(TS_ERR_ARG, "device buffers must be 8-byte aligned");
     if (c->L < 2) return fail(TS_ERR_ARG, "the ct x pt decrypt needs at least 2 limbs (CRT)");
-    for (uint32_t i = 0; expert && i < n; i++)
+    if (io_on_device < 0 || io_on_device > 2) return fail(TS_ERR_ARG, "io_on_device must be 0, 1 or 2");
+    // io_on_device == 2: seeds / expert / sk_index are device arrays too (the
+    // call then issues stream work only, with no host copy or wait)
+    const bool idx_dev = io_on_device == 2;
+    for (uint32_t i = 0; !idx_dev && expert && i < n; i++)
         if (expert[i] < 0 || (uint32_t)expert[i] >= lo->experts) return fail(TS_ERR_ARG, "expert index out of range");
-    for (uint32_t i = 0; sk_index && i < n; i++)
+    for (uint32_t i = 0; !idx_dev && sk_index && i < n; i++)
         if (sk_index[i] < 0 || (uint32_t)sk_index[i] >= sk->count) return fail(TS_ERR_ARG, "sk_index out of range");
     Lock lk(c);
     int rc = set_device(c);
@@ -1336,24 +1371,29 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
     const size_t CH = 2048;
     const double scale2 = c->dc.scale * c->dc.scale;
     // small per-delta inputs: staged once through pinned memory (async H2D)
-    const size_t sm_bytes = (size_t)n * 8 + (size_t)n * 4 * 2 + 512;
-    int slot = 0;
-    rc = ensure_pinned(c, sm_bytes, &slot);
-    if (rc) return rc;
-    uint64_t* p_seeds = static_cast<uint64_t*>(c->pinned[slot]);
-    int* p_ex = reinterpret_cast<int*>(p_seeds + n);
-    int* p_sk = p_ex + n;
-    memcpy(p_seeds, seeds, (size_t)n * 8);
-    if (expert) memcpy(p_ex, expert, (size_t)n * 4);
-    if (sk_index) memcpy(p_sk, sk_index, (size_t)n * 4);
     void* small = nullptr;
-    rc = dev_alloc(c, &small, sm_bytes);
-    if (rc) return rc;
-    CU(cudaMemcpyAsync(small, c->pinned[slot], sm_bytes - 512, cudaMemcpyHostToDevice, c->stream));
-    CU(cudaEventRecord(c->pinned_free[slot], c->stream));
-    const uint64_t* d_seeds_all = static_cast<uint64_t*>(small);
-    const int* d_ex_all = reinterpret_cast<const int*>(d_seeds_all + n);
-    const int* d_sk_all = d_ex_all + n;
+    const uint64_t* d_seeds_all = seeds;
+    const int* d_ex_all = expert;
+    const int* d_sk_all = sk_index;
+    if (!idx_dev) {
+        const size_t sm_bytes = (size_t)n * 8 + (size_t)n * 4 * 2 + 512;
+        int slot = 0;
+        rc = ensure_pinned(c, sm_bytes, &slot);
+        if (rc) return rc;
+        uint64_t* p_seeds = static_cast<uint64_t*>(c->pinned[slot]);
+        int* p_ex = reinterpret_cast<int*>(p_seeds + n);
+        int* p_sk = p_ex + n;
+        memcpy(p_seeds, seeds, (size_t)n * 8);
+        if (expert) memcpy(p_ex, expert, (size_t)n * 4);
+        if (sk_index) memcpy(p_sk, sk_index, (size_t)n * 4);
+        rc = dev_alloc(c, &small, sm_bytes);
+        if (rc) return rc;
+        CU(cudaMemcpyAsync(small, c->pinned[slot], sm_bytes - 512, cudaMemcpyHostToDevice, c->stream));
+        CU(cudaEventRecord(c->pinned_free[slot], c->stream));
+        d_seeds_all = static_cast<uint64_t*>(small);
+        d_ex_all = reinterpret_cast<const int*>(d_seeds_all + n);
+        d_sk_all = d_ex_all + n;
+    }
     for (size_t v0 = 0; v0 < n && !rc; v0 += CH) {
         const size_t nv = n - v0 < CH ? n - v0 : CH;
         Carve cv;
@@ -1373,8 +1413,8 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         double* dout = io_on_device ? delta + v0 * d : cv.at<double>(S, i_o);
         double* dinter = (io_on_device && inter) ? inter + v0 * r : cv.at<double>(S, i_in);
         const uint64_t* ds = d_seeds_all + v0;
-        const int* dex = d_ex_all + v0;
-        const int* dsk = d_sk_all + v0;
+        const int* dex = expert ? d_ex_all + v0 : nullptr;
+        const int* dsk = sk_index ? d_sk_all + v0 : nullptr;
         uint64_t* ct = cv.at<uint64_t>(S, i_ct);
         uint64_t* M = cv.at<uint64_t>(S, i_M);
         double* fd = cv.at<double>(S, i_fd);
@@ -1387,9 +1427,11 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         rc = encrypt_core(c, src, nv, ds, sk_index ? dsk : nullptr, sk->d, sk_shoup(sk), ct,
                           enc_work(cv, S, nv, eidx));
         if (rc) break;
-        if (lo->d_w && c->logn == 15) {
-            // N = 32768: the limb-0 and limb-1 INTTs of every (delta, batch)
-            // run as separate cluster pairs, then one light kernel does the
+        const int cl = c->logn >= 15 ? 2 : 1;
+        if (lo->d_w && (c->logn == 15 || (int)(nv * nb * 2 * cl) <= c->dc.sms)) {
+            // N = 32768, or a batch too small to fill the GPU: the limb-0 and
+            // limb-1 INTTs of every (delta, batch) run as separate CTAs
+            // (cluster pairs at N = 32768), then one light kernel does the
             // CRT and the segment functionals (:1311-1386)
             CU(launch_decrypt_limbs(c->dc, M, 2, ct, (long long)2 * L * N, (int)L, sk->d, sk_shoup(sk),
                                     sk_index ? dsk : nullptr, lo->d_pt, expert ? dex : nullptr, (int)nb,
@@ -1420,7 +1462,7 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
             if (inter) CU(cudaMemcpyAsync(inter + v0 * r, dinter, nv * r * 8, cudaMemcpyDeviceToHost, c->stream));
         }
     }
-    cudaFreeAsync(small, c->stream);
+    if (small) cudaFreeAsync(small, c->stream);
     if (rc) return rc;
     if (!io_on_device) return check_stats(c);
     return TS_OK;
@@ -1429,9 +1471,14 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
 int ts_dp_noise(ts_ctx* c, double* h, uint32_t n, uint32_t d, double clip, double sigma, const uint64_t* seeds,
                 int on_device) {
     if (!c || !h || !seeds || n == 0 || d == 0) return fail(TS_ERR_ARG, "bad dp_noise arguments");
+    if (on_device < 0 || on_device > 2) return fail(TS_ERR_ARG, "on_device must be 0, 1 or 2");
     Lock lk(c);
     int rc = set_device(c);
     if (rc) return rc;
+    if (on_device == 2) {  // h and seeds on the device: stream work only
+        cudaError_t e = launch_dp_noise(h, (int)n, (int)d, clip, sigma, seeds, c->stream);
+        return e == cudaSuccess ? TS_OK : fail(TS_ERR_CUDA, "dp_noise: %s", cudaGetErrorString(e));
+    }
     void* buf = nullptr;
     rc = dev_alloc(c, &buf, (on_device ? 0 : (size_t)n * d * 8) + n * 8 + 256);
     if (rc) return rc;

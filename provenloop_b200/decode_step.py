@@ -19,7 +19,10 @@ Per layer and token:
 - the q delta applied by the library (B_q), the v delta from the decrypted
   intermediate (B_v has 256 outputs, not d).
 
-Everything stays on the device, so a token costs no host synchronisation.
+Seeds, the routed expert and the DP seed are derived on the device from a
+token counter, so a decode step issues stream work only: ``capture`` records
+the whole step -- transformer, 28 HE-LoRA calls, DP noise, greedy pick -- as
+one CUDA graph that is replayed per token.
 """
 from __future__ import annotations
 
@@ -28,12 +31,14 @@ import ctypes as C
 import numpy as np
 
 from . import tensafe_he
-from ._lib import check, lib, ptr
-from .backend import ZeroMoaiLora, dp_sigma
+from ._lib import check, lib
+from .backend import ZeroMoaiLora, dp_sigma, lora_delta_graphable
 
 QWEN25_15B = dict(hidden_size=1536, intermediate_size=8960, num_hidden_layers=28, num_attention_heads=12,
                   num_key_value_heads=2, vocab_size=151936, max_position_embeddings=32768, rope_theta=1000000.0,
                   rms_norm_eps=1e-6, tie_word_embeddings=True)
+
+_SEED_TOKEN, _SEED_LAYER, _SEED_BASE, _DP_LAYER = 1_000_003, 7919, 17, 10_000
 
 
 def build_model(device="cuda", seed: int = 2, layers: int = 28):
@@ -48,9 +53,14 @@ def build_model(device="cuda", seed: int = 2, layers: int = 28):
     return model.to(torch.bfloat16).eval()
 
 
+def encryption_seed(token: int, layer: int) -> int:
+    """Seed of (token, layer)'s encryption (the device computes the same)."""
+    return token * _SEED_TOKEN + layer * _SEED_LAYER + _SEED_BASE
+
+
 class HeLoraDecoder:
     """HE-LoRA (q_proj, v_proj) on every layer of ``model``, CryptoMOE
-    experts chosen per token by a top-1 router over random logits."""
+    experts chosen per token by a top-1 router over hash-uniform logits."""
 
     def __init__(self, model, ctx: "tensafe_he.CkksContext", sk, rank: int = 16, experts: int = 3, seed: int = 2,
                  dp=(1.0, 1.0, 1e-5)):
@@ -78,34 +88,43 @@ class HeLoraDecoder:
             self.bv.append(torch.from_numpy(bv.astype(np.float64)).to(self.dev))
         self.clip, eps, delta = dp
         self.sigma = dp_sigma(eps, delta, self.clip)
-        self._h = torch.zeros((1, d), dtype=torch.float64, device=self.dev)
-        self._dq = torch.zeros((1, d), dtype=torch.float64, device=self.dev)
-        self._inter = torch.zeros((1, 2 * rank), dtype=torch.float64, device=self.dev)
-        self._fin = torch.zeros((1, d), dtype=torch.float64, device=self.dev)
-        self._dv = None
-        self._token = 0
-        self._expert = 0
-        self._rng = np.random.default_rng(seed + 1)
+        f64 = dict(dtype=torch.float64, device=self.dev)
+        self._h = torch.zeros((1, d), **f64)
+        self._dq = torch.zeros((1, d), **f64)
+        self._dv = torch.zeros((1, dv), **f64)
+        self._inter = torch.zeros((1, 2 * rank), **f64)
+        self._fin = torch.zeros((1, d), **f64)
+        self.token = torch.zeros((1,), dtype=torch.int64, device=self.dev)   # device token counter
+        self.expert = torch.zeros((1,), dtype=torch.int32, device=self.dev)
+        self._seed = torch.zeros((1,), dtype=torch.int64, device=self.dev)
+        self._eidx = torch.arange(experts, dtype=torch.float64, device=self.dev)
         self._hooks = []
         self.enabled = True
+        self._hooks.append(model.model.embed_tokens.register_forward_hook(self._route_hook))
         for li, layer in enumerate(model.model.layers):
             self._hooks.append(layer.self_attn.q_proj.register_forward_hook(self._q_hook(li)))
             self._hooks.append(layer.self_attn.v_proj.register_forward_hook(self._v_hook))
         self._hooks.append(model.model.norm.register_forward_hook(self._dp_hook))
-        # the library works on torch's stream: no host synchronisation per layer
-        self._stream = None
 
-    def _seed(self, layer: int) -> int:
-        return (self._token * 1_000_003 + layer * 7919 + 17) & 0xFFFFFFFFFFFFFFFF
+    # ---------------------------------------------------------------- hooks
+    def _route_hook(self, module, inp, out):
+        # top-1 router over uniform logits: hash-uniform values of (token, e)
+        import torch
+        if self.enabled:
+            x = torch.sin(self.token.double() * 12.9898 + self._eidx * 78.233) * 43758.5453
+            self.expert.copy_(torch.argmax(x - torch.floor(x)).view(1).to(torch.int32))
+        return out
 
     def _q_hook(self, li):
         def hook(module, inp, out):
             if not self.enabled:
                 return out
             self._h.copy_(inp[0][:, -1, :])
-            self.loras[li].delta_device(self.sk, self._h, [self._seed(li)], self._dq, expert=[self._expert],
-                                        inter_dev=self._inter)
-            self._dv = self._inter[:, self.rank:] @ self.bv[li][self._expert].T
+            self._seed.copy_(self.token * _SEED_TOKEN + (li * _SEED_LAYER + _SEED_BASE))
+            lora_delta_graphable(self.loras[li], self.sk, self._h, self._seed, self._dq, expert_dev=self.expert,
+                                 inter_dev=self._inter)
+            bv = self.bv[li].index_select(0, self.expert.long())[0]
+            self._dv.copy_(self._inter[:, self.rank:] @ bv.T)
             out[:, -1, :] += self._dq.to(out.dtype)
             return out
         return hook
@@ -120,20 +139,23 @@ class HeLoraDecoder:
         if not self.enabled:
             return out
         self._fin.copy_(out[:, -1, :])
-        s = np.array([self._seed(10_000)], dtype=np.uint64)
+        self._seed.copy_(self.token * _SEED_TOKEN + (_DP_LAYER * _SEED_LAYER + _SEED_BASE))
         check(lib().ts_dp_noise(self.ctx.handle, self._fin.data_ptr(), 1, self._fin.shape[1], float(self.clip),
-                                float(self.sigma), ptr(s, C.c_uint64), 1), "ts_dp_noise")
+                                float(self.sigma), C.cast(self._seed.data_ptr(), C.POINTER(C.c_uint64)), 2),
+              "ts_dp_noise")
         out[:, -1, :] = self._fin.to(out.dtype)
         return out
 
-    def bind_stream(self):
+    # ---------------------------------------------------------------- decode
+    def bind_stream(self, stream=None):
+        """Run the library on ``stream`` (default: torch's current stream)."""
         import torch
-        check(lib().ts_ctx_set_stream(self.ctx.handle, torch.cuda.current_stream(self.dev).cuda_stream),
-              "ts_ctx_set_stream")
+        s = stream if stream is not None else torch.cuda.current_stream(self.dev)
+        check(lib().ts_ctx_set_stream(self.ctx.handle, s.cuda_stream), "ts_ctx_set_stream")
 
     def generate(self, prompt_ids, tokens: int = 16):
-        """Greedy decode of ``tokens`` tokens; every forward pass (the prompt
-        step and each decode step) runs HE-LoRA on all layers."""
+        """Greedy decode, eager (DynamicCache); every forward pass runs
+        HE-LoRA on all layers."""
         import torch
         from transformers import DynamicCache
 
@@ -142,14 +164,65 @@ class HeLoraDecoder:
         cache = DynamicCache()
         out_ids = []
         with torch.no_grad():
-            for t in range(tokens):
-                self._expert = int(np.argmax(self._rng.random(self.experts)))  # top-1 over uniform logits
+            for _ in range(tokens):
                 res = self.model(input_ids=ids, past_key_values=cache, use_cache=True)
-                nxt = res.logits[:, -1, :].argmax(dim=-1, keepdim=True)
-                out_ids.append(nxt)
-                ids = nxt
-                self._token += 1
+                ids = res.logits[:, -1, :].argmax(dim=-1, keepdim=True)
+                out_ids.append(ids)
+                self.token += 1
         return torch.cat(out_ids, dim=1)
+
+    def capture(self, max_len: int = 64, warmup: int = 2):
+        """Capture one decode step (static KV cache) as a CUDA graph on a
+        side stream; returns run(prompt_id, n) that decodes n tokens from a
+        one-token prompt by replaying it."""
+        import torch
+        from transformers import StaticCache
+
+        cfg = self.model.config
+        cache = StaticCache(config=cfg, max_batch_size=1, max_cache_len=max_len, device=self.dev,
+                            dtype=torch.bfloat16)
+        ids = torch.zeros((1, 1), dtype=torch.long, device=self.dev)
+        pos = torch.zeros((1,), dtype=torch.long, device=self.dev)
+        outs = torch.zeros((1, max_len), dtype=torch.long, device=self.dev)
+        stream = torch.cuda.Stream(device=self.dev)
+        self.bind_stream(stream)
+
+        def step():
+            r = self.model(input_ids=ids, cache_position=pos, position_ids=pos.view(1, 1), past_key_values=cache,
+                           use_cache=True)
+            nxt = r.logits[:, -1, :].argmax(dim=-1, keepdim=True)
+            outs.index_copy_(1, pos, nxt)
+            ids.copy_(nxt)
+            pos.add_(1)
+            self.token.add_(1)
+
+        stream.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.no_grad(), torch.cuda.stream(stream):
+            for _ in range(warmup):  # sizes the library's scratch, loads kernels
+                step()
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step()
+        torch.cuda.synchronize(self.dev)
+
+        def run(prompt_id: int, n: int, start_token: int = 0):
+            if n > max_len:
+                raise ValueError(f"at most {max_len} tokens per capture")
+            with torch.cuda.stream(stream):
+                # the static cache keeps its own device write position
+                # (cumulative_length), which must restart with pos
+                cache.reset()
+                ids.fill_(int(prompt_id))
+                pos.zero_()
+                self.token.fill_(int(start_token))
+                for _ in range(n):
+                    graph.replay()
+            return outs[:, :n]
+
+        run.stream = stream
+        run.graph = graph
+        return run
 
     def remove(self):
         for h in self._hooks:

@@ -946,6 +946,65 @@ cudaError_t launch_enc_combine(const DevCtx& c, uint64_t* ct, const uint64_t* sk
 }
 
 // ======================================================================
+// L2 warm-up for latency-bound small batches.  A decode step runs one delta
+// per layer between weight streams that evict L2, so a small batch would
+// otherwise take an HBM round trip on every dependent twiddle, key and
+// plaintext load of its one-CTA-per-limb kernels.  Pieces of kL2Piece bytes
+// are spread over the grid; each is one cp.async.bulk.prefetch.L2 (16-byte
+// aligned start and length, rounded inwards).
+// ======================================================================
+constexpr long long kL2Piece = 8192;
+
+__device__ __forceinline__ long long l2_pieces(const L2Range& R) {
+    return (long long)R.rows * R.reps * ((R.bytes + kL2Piece - 1) / kL2Piece);
+}
+
+__global__ void __launch_bounds__(128) k_prefetch_l2(L2List L) {
+    long long first[kMaxL2Ranges + 1];
+    first[0] = 0;
+    for (int k = 0; k < L.n; k++) first[k + 1] = first[k] + l2_pieces(L.r[k]);
+    const long long total = first[L.n];
+    for (long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x; p < total;
+         p += (long long)gridDim.x * blockDim.x) {
+        int k = 0;
+        while (p >= first[k + 1]) k++;
+        const L2Range& R = L.r[k];
+        long long q = p - first[k];
+        const long long chunks = (R.bytes + kL2Piece - 1) / kL2Piece;
+        const long long chunk = q % chunks;
+        q /= chunks;
+        const int rep = (int)(q % R.reps), row = (int)(q / R.reps);
+        long long off = (long long)rep * R.rep_stride + chunk * kL2Piece;
+        if (R.idx) {
+            const int i = R.idx[row];
+            if (i < 0 || i >= R.idx_max) continue;
+            off += (long long)i * R.idx_stride;
+        }
+        const long long len = R.bytes - chunk * kL2Piece < kL2Piece ? R.bytes - chunk * kL2Piece : kL2Piece;
+        const size_t a = __cvta_generic_to_global(static_cast<const char*>(R.base) + off);
+        const size_t lo = (a + 15) & ~(size_t)15, hi = (a + (size_t)len) & ~(size_t)15;
+        if (hi > lo)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"((unsigned)(hi - lo)) : "memory");
+    }
+}
+
+cudaError_t launch_prefetch_l2(const L2List& list, cudaStream_t s) {
+    if (list.n <= 0) return cudaSuccess;
+    if (list.n > kMaxL2Ranges) return cudaErrorInvalidValue;
+    long long total = 0;
+    for (int k = 0; k < list.n; k++) {
+        const L2Range& R = list.r[k];
+        if (!R.base || R.rows < 1 || R.reps < 1 || R.bytes < 0 || (!R.idx && R.rows != 1)) return cudaErrorInvalidValue;
+        total += (long long)R.rows * R.reps * ((R.bytes + kL2Piece - 1) / kL2Piece);
+    }
+    if (total == 0) return cudaSuccess;
+    const long long blocks = (total + 127) / 128;
+    KScope ks("prefetch_l2", s);
+    k_prefetch_l2<<<(int)(blocks < 148 ? blocks : 148), 128, 0, s>>>(list);
+    return cudaGetLastError();
+}
+
+// ======================================================================
 // Public-key encryption (ciphertext.rs:240-319): c0 = b*u + NTT(m + e0),
 // c1 = a*u + NTT(e1), with u = NTT(ternary) computed by the key-generation
 // kernel from the same stream (the reference's u mapping composed with its
@@ -1570,24 +1629,33 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
 }
 
 // CRT of limbs 0/1, / scale and the segment functionals, for decrypts whose
-// INTT ran separately (N = 32768: one limb per CTA pair keeps the cluster
-// kernel lean).  One block per vector v of M [nvec][2][n].
+// INTT ran separately (N = 32768, and small batches at any N).  One cluster
+// of kCrtCl CTAs per vector v of M [nvec][2][n]: each CTA takes an n/kCrtCl
+// slice, reduces it in shared memory, and cluster rank 0 adds the kCrtCl
+// partials in rank order through distributed shared memory, so the sum order
+// is fixed.  A small batch (the decode step's 7 vectors) thus spreads over
+// 8x the SMs instead of running one block per vector.
+constexpr int kCrtCl = 8;
+
 __global__ void __launch_bounds__(256)
     k_crt_seg(const uint64_t* __restrict__ M, int logn, CrtConst K, double inv_scale, const double* __restrict__ W,
               int cols, double* __restrict__ seg_out) {
-    const int n = 1 << logn, v = blockIdx.x, tid = threadIdx.x;
+    const int n = 1 << logn, tid = threadIdx.x;
+    const int v = blockIdx.x / kCrtCl, rank = blockIdx.x % kCrtCl;
+    const int slice = n / kCrtCl, j0 = rank * slice;
     const uint64_t* m0 = M + ((size_t)v * 2 << logn);
     const uint64_t* m1 = m0 + n;
     double acc[kMaxSegCols];
 #pragma unroll
     for (int c = 0; c < kMaxSegCols; c++) acc[c] = 0.0;
-    for (int j = tid; j < n; j += blockDim.x) {
+    for (int j = j0 + tid; j < j0 + slice; j += blockDim.x) {
         const double coeff = __dmul_rn(crt_coeff(m0[j], m1[j], K), inv_scale);
 #pragma unroll
         for (int c = 0; c < kMaxSegCols; c++)
             if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * n + j), acc[c]);
     }
     __shared__ double red[8][kMaxSegCols];
+    __shared__ double part[kMaxSegCols];
     const int lane = tid & 31, wid = tid >> 5;
 #pragma unroll
     for (int c = 0; c < kMaxSegCols; c++) {
@@ -1600,17 +1668,25 @@ __global__ void __launch_bounds__(256)
     if (tid < cols) {
         double a = 0.0;
         for (int w = 0; w < 8; w++) a += red[w][tid];
+        part[tid] = a;
+    }
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();  // every slice's partial is in its CTA's shared memory
+    if (rank == 0 && tid < cols) {
+        double a = 0.0;
+        for (int r = 0; r < kCrtCl; r++) a += cl.map_shared_rank(part, r)[tid];
         seg_out[(size_t)v * cols + tid] = a;
     }
+    cl.sync();  // the other CTAs keep their shared memory until rank 0 has read it
 }
 
 cudaError_t launch_crt_seg(const DevCtx& c, const uint64_t* M, int nvec, double inv_scale, const double* W,
                            int seg_cols, double* seg_out, cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
-    if (seg_cols < 1 || seg_cols > kMaxSegCols || c.L < 2) return cudaErrorInvalidValue;
+    if (seg_cols < 1 || seg_cols > kMaxSegCols || c.L < 2 || (c.n % kCrtCl) != 0) return cudaErrorInvalidValue;
     KScope ks("crt_seg", s);
-    k_crt_seg<<<nvec, 256, 0, s>>>(M, c.logn, c.crt, inv_scale, W, seg_cols, seg_out);
-    return cudaGetLastError();
+    return launch_cl(kCrtCl, k_crt_seg, dim3((unsigned)(nvec * kCrtCl)), 256, 0, s, M, c.logn, c.crt, inv_scale, W,
+                     seg_cols, seg_out);
 }
 
 // ======================================================================
@@ -1633,6 +1709,7 @@ cudaError_t launch_gather_inter(const double* seg, double* inter, int ndelta, in
     return cudaGetLastError();
 }
 
+// delta[i][row] = sum_k B[row][k] * inter[i][k], one FMA chain in k order.
 __global__ void k_bmat(const float* __restrict__ B, const double* __restrict__ inter, double* __restrict__ delta,
                        int nvec, int d, int r, const int* __restrict__ b_sel, long long b_stride) {
     const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -1641,8 +1718,31 @@ __global__ void k_bmat(const float* __restrict__ B, const double* __restrict__ i
     const float* Bm = B + (b_sel ? (long long)b_sel[i] * b_stride : 0) + (long long)row * r;
     const double* x = inter + (size_t)i * r;
     double acc = 0.0;
-    for (int k = 0; k < r; k++) acc += (double)__ldg(Bm + k) * x[k];
+    for (int k = 0; k < r; k++) acc = fma((double)__ldg(Bm + k), x[k], acc);
     delta[t] = acc;
+}
+
+// The same products for small batches, one warp per output: the lanes load
+// 32 consecutive k of the row (one coalesced line) and every lane runs the
+// k-order FMA chain on broadcast values, so the result is bit-identical to
+// k_bmat's while the loads of a row are one request instead of r.
+__global__ void k_bmat_warp(const float* __restrict__ B, const double* __restrict__ inter, double* __restrict__ delta,
+                            int nvec, int d, int r, const int* __restrict__ b_sel, long long b_stride) {
+    const long long t = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (t >= (long long)nvec * d) return;
+    const int i = (int)(t / d), row = (int)(t % d);
+    const float* Bm = B + (b_sel ? (long long)b_sel[i] * b_stride : 0) + (long long)row * r;
+    const double* x = inter + (size_t)i * r;
+    double acc = 0.0;
+    for (int k0 = 0; k0 < r; k0 += 32) {
+        const int kn = r - k0 < 32 ? r - k0 : 32;
+        const double bl = lane < kn ? (double)__ldg(Bm + k0 + lane) : 0.0;
+        const double xl = lane < kn ? x[k0 + lane] : 0.0;
+        for (int k = 0; k < kn; k++)
+            acc = fma(__shfl_sync(0xffffffffu, bl, k), __shfl_sync(0xffffffffu, xl, k), acc);
+    }
+    if (lane == 0) delta[t] = acc;
 }
 
 cudaError_t launch_bmat(const float* B, const double* inter, double* delta, int nvec, int d, int r, const int* b_sel,
@@ -1650,7 +1750,11 @@ cudaError_t launch_bmat(const float* B, const double* inter, double* delta, int 
     const long long tot = (long long)nvec * d;
     if (tot <= 0) return cudaSuccess;
     KScope ks("bmat", s);
-    k_bmat<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(B, inter, delta, nvec, d, r, b_sel, b_stride);
+    if (tot <= 16384) {  // up to ~10 deltas: latency, not throughput
+        k_bmat_warp<<<(unsigned)((tot * 32 + 255) / 256), 256, 0, s>>>(B, inter, delta, nvec, d, r, b_sel, b_stride);
+    } else {
+        k_bmat<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(B, inter, delta, nvec, d, r, b_sel, b_stride);
+    }
     return cudaGetLastError();
 }
 

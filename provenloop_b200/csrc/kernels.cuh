@@ -119,6 +119,28 @@ cudaError_t launch_encrypt_split(const DevCtx& c, uint64_t* ct, const int64_t* m
 cudaError_t launch_enc_combine(const DevCtx& c, uint64_t* ct, const uint64_t* sk, const uint64_t* sks,
                                const int* sk_of, int nvec, cudaStream_t s);
 
+// L2 warm-up of the tables a small batch reads (latency mode): each range is
+// `rows` x `reps` blocks of `bytes` at base + idx[row]*idx_stride +
+// rep*rep_stride (idx[row] outside [0, idx_max) skips the row; idx null:
+// row 0 only, no offset).  Issued as bulk L2 prefetches, so it moves no data
+// through the SMs and has no visible effect besides cache state.
+constexpr int kMaxL2Ranges = 12;
+struct L2Range {
+    const void* base;
+    const int* idx;
+    long long idx_stride;
+    int idx_max;
+    int rows;
+    int reps;
+    long long rep_stride;
+    long long bytes;
+};
+struct L2List {
+    L2Range r[kMaxL2Ranges];
+    int n;
+};
+cudaError_t launch_prefetch_l2(const L2List& list, cudaStream_t s);
+
 // Shoup companions out[i] = floor(in[i] * 2^64 / q_l) of canonical
 // residues, for `polys` consecutive poly-limbs whose limb index is poly % L.
 cudaError_t launch_shoup_companion(const DevCtx& c, uint64_t* out, const uint64_t* in, long long polys,

@@ -196,7 +196,7 @@ struct ts_ctx {
     // second stream and fork / join events of the small-batch encryption,
     // created by its first use
     cudaStream_t side = nullptr;
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_gauss = nullptr;
     // grow-only scratch
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
@@ -517,8 +517,12 @@ EncWork enc_work(const Carve& cv, void* base, size_t cap, const size_t idx[5]) {
 // Core of every secret-key encryption: `count` vectors already on the device
 // (SlotSrc), seeds / key indexes on the device, output ct [count][2][L][n].
 // Uses only the work buffers in `w` (callers own the scratch layout).
+// `warm` (optional) lists tables the caller's later kernels read; in the
+// small-batch branch they are prefetched into L2 on the side stream ahead of
+// c1 = NTT(a), together with the encryption's own tables.
 int encrypt_core(ts_ctx* c, const SlotSrc& src, size_t count, const uint64_t* d_seeds, const int* d_skof,
-                 const uint64_t* d_sk, const uint64_t* d_sks, uint64_t* d_ct, const EncWork& w) {
+                 const uint64_t* d_sk, const uint64_t* d_sks, uint64_t* d_ct, const EncWork& w,
+                 const L2List* warm = nullptr) {
     const size_t n = c->n;
     for (size_t v0 = 0; v0 < count; v0 += w.cap) {
         const size_t nv = count - v0 < w.cap ? count - v0 : w.cap;
@@ -537,10 +541,31 @@ int encrypt_core(ts_ctx* c, const SlotSrc& src, size_t count, const uint64_t* d_
                 CU(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
                 CU(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
                 CU(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming));
+                CU(cudaEventCreateWithFlags(&c->ev_gauss, cudaEventDisableTiming));
             }
             CU(cudaEventRecord(c->ev_fork, c->stream));
             CU(cudaStreamWaitEvent(c->side, c->ev_fork, 0));
-            CU(launch_encode(c->dc, s, (int)nv, w.m, w.e, seeds, 2ULL * c->L * n, w.f, c->stream));
+            {
+                // NTT twiddles, FFT tables and the key(s), then the caller's
+                L2List pl = warm ? *warm : L2List{};
+                const int room = kMaxL2Ranges - pl.n;
+                if (room >= 4) {
+                    const long long limb = (long long)n * 8;
+                    pl.r[pl.n++] = L2Range{c->d_fft, nullptr, 0, 0, 1, 1, 0, 4 * limb};
+                    pl.r[pl.n++] = L2Range{c->d_tw, nullptr, 0, 0, 1, 1, 0, 4 * (long long)c->L * limb};
+                    if (!d_skof) {  // one key for the whole batch
+                        pl.r[pl.n++] = L2Range{d_sk, nullptr, 0, 0, 1, 1, 0, (long long)c->L * limb};
+                        pl.r[pl.n++] = L2Range{d_sks, nullptr, 0, 0, 1, 1, 0, (long long)c->L * limb};
+                    }
+                }
+                CU(launch_prefetch_l2(pl, c->side));
+            }
+            // the Gaussian error (words 2LN.. of each stream) on the side
+            // stream too, off the encode's critical path
+            CU(launch_gauss_gen(c->dc, w.e, seeds, (int)nv, 2ULL * c->L * n, c->side));
+            CU(cudaEventRecord(c->ev_gauss, c->side));
+            CU(launch_encode(c->dc, s, (int)nv, w.m, nullptr, seeds, 0, w.f, c->stream));
+            CU(cudaStreamWaitEvent(c->stream, c->ev_gauss, 0));
             CU(launch_encrypt_split(c->dc, ct, w.m, w.e, d_sk, d_sks, skof, seeds, (int)nv, w.fl, w.pl, c->side,
                                     c->stream));
             CU(cudaEventRecord(c->ev_join, c->side));
@@ -706,6 +731,7 @@ void ctx_free(ts_ctx* c) {
         cudaStreamDestroy(c->side);
         cudaEventDestroy(c->ev_fork);
         cudaEventDestroy(c->ev_join);
+        cudaEventDestroy(c->ev_gauss);
     }
     if (c->own) cudaStreamDestroy(c->own);
     delete c;
@@ -1424,8 +1450,23 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         // 1. encrypt the cols-fold replicated hidden states (:1267-1272)
         SlotSrc src{dh, 0, (int)d, (long long)d, (int)d, (int)cols};
         const size_t eidx[5] = {i_m, i_e, i_fe, i_fl, i_pl};
+        // tables of the decrypt side, warmed into L2 during the encryption
+        // when the batch is small: limbs 0/1 of the routed expert's packed
+        // plaintexts and their companions, the segment functionals, B
+        L2List warm{};
+        {
+            const int rows = expert ? (int)nv : 1;
+            const long long limb = (long long)N * 8, lstride = (long long)L * limb;
+            const long long per_expert = (long long)nb * lstride, bbytes = (long long)(d * r * 4);
+            const uint64_t* pts = lo->d_pt + (size_t)lo->experts * nb * L * N;
+            const int* ex = expert ? dex : nullptr;
+            warm.r[warm.n++] = L2Range{lo->d_pt, ex, per_expert, (int)lo->experts, rows, (int)nb, lstride, 2 * limb};
+            warm.r[warm.n++] = L2Range{pts, ex, per_expert, (int)lo->experts, rows, (int)nb, lstride, 2 * limb};
+            if (lo->d_w) warm.r[warm.n++] = L2Range{lo->d_w, nullptr, 0, 0, 1, 1, 0, (long long)cols * limb};
+            warm.r[warm.n++] = L2Range{lo->d_b, ex, bbytes, (int)lo->experts, rows, 1, 0, bbytes};
+        }
         rc = encrypt_core(c, src, nv, ds, sk_index ? dsk : nullptr, sk->d, sk_shoup(sk), ct,
-                          enc_work(cv, S, nv, eidx));
+                          enc_work(cv, S, nv, eidx), &warm);
         if (rc) break;
         const int cl = c->logn >= 15 ? 2 : 1;
         if (lo->d_w && (c->logn == 15 || (int)(nv * nb * 2 * cl) <= c->dc.sms)) {

@@ -4,6 +4,7 @@ used for ncu captures).
     python -m provenloop_b200.microbench ntt [--polys 1024] [--reps 10]
     python -m provenloop_b200.microbench hadamard [--polys 1024] [--reps 4]
     python -m provenloop_b200.microbench delta [--batch 256] [--reps 3]
+    python -m provenloop_b200.microbench latency [--batch 1] [--reps 50]
 
 `ntt` is the C2 configuration: `polys` polynomials x 3 limbs x N = 16384 with
 the three largest distinct 50-bit primes == 1 mod 2N, forward then inverse
@@ -143,9 +144,115 @@ def delta(batch=256, reps=3, device=0):
             "launches_total": _lib.launch_count()}
 
 
+def latency(batch=1, reps=50, rank=32, device=0):
+    """Latency of one small delta batch (the decode-step case: rank 2r = 32
+    stacked q/v rows, 7 plaintext batches, 3 experts), device-resident
+    inputs with device seeds: per-call time from CUDA events, and per-kernel
+    time from the library's event-bracketed profile."""
+    import torch
+
+    from . import _lib
+    from .backend import ZeroMoaiLora, lora_delta_graphable
+
+    dev = torch.device("cuda", device)
+    ctx, stream = _ctx(None, device)
+    rng = np.random.default_rng(0)
+    A = (rng.standard_normal((3, rank, 1536)) * 0.02).astype(np.float32)
+    B = (rng.standard_normal((3, 1536, rank)) * 0.02).astype(np.float32)
+    with torch.cuda.stream(stream):
+        sk = ctx.keygen(0)
+        lora = ZeroMoaiLora(ctx, A, B)
+        h = torch.from_numpy(rng.standard_normal((batch, 1536))).to(dev)
+        d = torch.empty_like(h)
+        inter = torch.empty((batch, rank), dtype=torch.float64, device=dev)
+        seeds = torch.arange(batch, dtype=torch.int64, device=dev)
+        ex = torch.ones(batch, dtype=torch.int32, device=dev)
+        for _ in range(3):
+            lora_delta_graphable(lora, sk, h, seeds, d, expert_dev=ex, inter_dev=inter)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        stream.synchronize()
+        ev[0].record(stream)
+        for i in range(reps):
+            seeds.add_(batch)
+            lora_delta_graphable(lora, sk, h, seeds, d, expert_dev=ex, inter_dev=inter)
+        ev[1].record(stream)
+        stream.synchronize()
+        per_call = ev[0].elapsed_time(ev[1]) / reps
+        # the same calls replayed from one CUDA graph (the decode step's form)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(8):
+                seeds.add_(batch)
+                lora_delta_graphable(lora, sk, h, seeds, d, expert_dev=ex, inter_dev=inter)
+        graph.replay()
+        stream.synchronize()
+        ev[0].record(stream)
+        for i in range(reps):
+            graph.replay()
+        ev[1].record(stream)
+        stream.synchronize()
+        per_call_graph = ev[0].elapsed_time(ev[1]) / (reps * 8)
+        # cold L2: a 256 MiB write between calls (as a decode step's weight
+        # stream evicts the tables between layers), minus the writes alone
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+        def graph_of(with_delta):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(8):
+                    flush.fill_(i)
+                    if with_delta:
+                        seeds.add_(batch)
+                        lora_delta_graphable(lora, sk, h, seeds, d, expert_dev=ex, inter_dev=inter)
+            return g
+
+        cold = []
+        for g in (graph_of(True), graph_of(False)):
+            g.replay()
+            stream.synchronize()
+            ev[0].record(stream)
+            for i in range(reps):
+                g.replay()
+            ev[1].record(stream)
+            stream.synchronize()
+            cold.append(ev[0].elapsed_time(ev[1]) / (reps * 8))
+        per_call_cold = cold[0] - cold[1]
+        _lib.profile_reset()
+        _lib.profile_enable(True)
+        for i in range(reps):
+            lora_delta_graphable(lora, sk, h, seeds, d, expert_dev=ex, inter_dev=inter)
+        stream.synchronize()
+        _lib.profile_enable(False)
+    names = ("prefetch_l2", "gauss_gen", "encode", "enc_a", "enc_x", "enc_combine", "enc_u", "plan", "gauss_fix",
+             "enc_a_fix", "enc_u_fix", "dec_fused", "decrypt_limb", "crt_seg", "gather_inter", "bmat")
+
+    def read():
+        out = {}
+        for name in names:
+            ms, n = _lib.profile_read(name)
+            if n:
+                out[name] = ms / reps
+        return out
+
+    kern = read()
+    # the same with L2 flushed before every call
+    with torch.cuda.stream(stream):
+        _lib.profile_reset()
+        _lib.profile_enable(True)
+        for i in range(reps):
+            flush.fill_(i)
+            lora_delta_graphable(lora, sk, h, seeds, d, expert_dev=ex, inter_dev=inter)
+        stream.synchronize()
+        _lib.profile_enable(False)
+    kern_cold = read()
+    return {"kernel": "lora_delta_latency", "batch": batch, "rank": rank, "ms_per_call": per_call,
+            "graph_ms_per_call": per_call_graph, "graph_cold_l2_ms_per_call": per_call_cold,
+            "kernels_ms_per_call": kern, "kernels_cold_l2_ms_per_call": kern_cold}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["ntt", "hadamard", "delta"])
+    ap.add_argument("what", choices=["ntt", "hadamard", "delta", "latency"])
     ap.add_argument("--polys", type=int, default=1024)
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--reps", type=int, default=None)
@@ -154,6 +261,8 @@ def main():
         r = ntt(a.polys, a.reps or 10)
     elif a.what == "hadamard":
         r = hadamard(a.polys, a.reps or 4)
+    elif a.what == "latency":
+        r = latency(a.batch if a.batch != 256 else 1, a.reps or 50)
     else:
         r = delta(a.batch, a.reps or 3)
     print(json.dumps(r))

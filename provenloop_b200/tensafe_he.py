@@ -65,10 +65,10 @@ class _Handle:
         if h:
             self._destroy(h)
 
-    def __del__(self):
-        # at interpreter exit the CUDA runtime may already be torn down; the
-        # process releases everything anyway
-        if sys.is_finalizing():
+    def __del__(self, _finalizing=sys.is_finalizing):
+        # at interpreter exit the CUDA runtime may already be torn down (and
+        # module globals cleared); the process releases everything anyway
+        if _finalizing():
             return
         try:
             self.close()

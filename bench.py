@@ -47,9 +47,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-micro", action="store_true", help="skip the NTT / Hadamard microbenchmarks")
     ap.add_argument("--no-c3", action="store_true", help="skip the HE decode-step (Qwen-shaped) measurement")
-    ap.add_argument("--config", default="c1", choices=["c1", "c4"],
+    ap.add_argument("--config", default="c1", choices=["c1", "c4", "c5"],
                     help="c1: the headline single-key N=16384 workload; c4: 256 users with their own keys, "
-                         "N=32768 on [60,40,40,40,60], 28 layers x 2 projections of rank-32 adapters")
+                         "N=32768 on [60,40,40,40,60], 28 layers x 2 projections of rank-32 adapters; c5: the "
+                         "sweep over N, batch, d and r (one JSON line with every point)")
     return ap.parse_args()
 
 
@@ -594,12 +595,55 @@ def run_c4(args):
         dist.destroy_process_group()
 
 
+def run_c5(args):
+    """C5: the sweep of provenloop_b200/sweep.py (N x batch x d x r), one
+    JSON line; `value` is its N = 16384, batch 4096, d = 1536, r = 16 point."""
+    import torch
+    import torch.distributed as dist
+
+    from provenloop_b200 import _lib, sweep
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    peak, peak_kind = measured_peaks()
+    launches0 = _lib.launch_count()
+    clocks = ClockSampler(local)
+    clocks.start()
+    pts = sweep.run(args.steps, args.warmup, peak_gbs=peak, device=local)
+    clk = clocks.stop()
+    head = next(p for p in pts if (p["n"], p["batch"], p["d"], p["r"]) == (16384, 4096, 1536, 16))
+    if rank == 0:
+        line = {
+            "metric": "encrypted LoRA deltas/sec, sweep over N, batch, d and r (C5)",
+            "value": head["deltas_per_s"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+            "config": {"workload": "C5 sweep: N in {8192,16384,32768} x batch in {1,16,256,4096} per GPU x d in "
+                                   "{1536,3584} x r in {8,16,32,64}; value = the N=16384/4096/1536/16 point",
+                       "l2": "flushed between timed steps (256 MiB write)", "seed": 4,
+                       "parallelism": "replicas" if world == 1 else f"users sharded over {world} ranks"},
+            "peak_gbs": peak, "peak_kind": peak_kind, "clocks": clk,
+            "gpu_launches": _lib.launch_count() - launches0, "points": pts,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.config == "c4":
         run_c4(args)
+    elif args.config == "c5":
+        run_c5(args)
     else:
         run_ours(args)
 

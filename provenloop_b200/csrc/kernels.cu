@@ -22,8 +22,10 @@ namespace tsg {
 namespace {
 
 std::mutex g_attr_mu;
-std::set<std::pair<const void*, int>> g_attr_done;
+std::map<std::pair<const void*, int>, size_t> g_attr_done;  // (kernel, device) -> dynamic smem limit set
 
+// Raises a kernel's dynamic shared-memory limit to at least `bytes` on the
+// current device (launchers of one kernel may need different sizes).
 template <class K>
 cudaError_t ensure_smem(K* kernel, size_t bytes) {
     if (bytes <= 48 * 1024) return cudaSuccess;
@@ -32,9 +34,10 @@ cudaError_t ensure_smem(K* kernel, size_t bytes) {
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> g(g_attr_mu);
     auto key = std::make_pair((const void*)kernel, dev);
-    if (g_attr_done.count(key)) return cudaSuccess;
+    auto it = g_attr_done.find(key);
+    if (it != g_attr_done.end() && it->second >= bytes) return cudaSuccess;
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-    if (e == cudaSuccess) g_attr_done.insert(key);
+    if (e == cudaSuccess) g_attr_done[key] = bytes;
     return e;
 }
 
@@ -751,15 +754,15 @@ constexpr size_t kEncPlanWinBytes = (2 * kEncPlanRound + 16) * 4;
 // (speculative, no rejection): limb l's candidate i at words 2*l*N + 2i, low
 // word first; the Gaussian block follows at 2*L*N.  In list mode the CTAs
 // walk the flagged streams only, using their exact plans.
-template <int LOGN>
-__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+template <int LOGN, int CLX = ntt_default_cl(LOGN)>
+__global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, 1)
     k_enc_a(uint64_t* __restrict__ ct, const uint64_t* __restrict__ seeds, const LimbTab* __restrict__ tabs, int L,
             int nvec, uint32_t* flags, const StreamPlan* __restrict__ plans, int plan_mode) {
     extern __shared__ __align__(16) uint64_t sm[];
-    using C = NttCfg<LOGN>;
+    using C = NttCfg<LOGN, CLX>;
     constexpr int N = 1 << LOGN, NT = C::NT, H = C::H;
     const int limb = blockIdx.x / C::CL, tid = threadIdx.x;
-    const int h0 = ntt_rank<LOGN>() * H;  // first element of this CTA's share
+    const int h0 = ntt_rank<LOGN, CLX>() * H;  // first element of this CTA's share
     const LimbTab T = tabs[limb];
     const int nwork = plan_mode ? (int)flags[nvec] : 1;
     for (int it = blockIdx.y; it < (plan_mode ? nwork : (int)blockIdx.y + 1); it += gridDim.y) {
@@ -787,7 +790,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
             // accepted candidate cidx lands at output cidx - (# rejected
             // before it).  Words come through a window behind the NTT buffer.
             const StreamPlan& P = plans[v];
-            uint32_t* win = reinterpret_cast<uint32_t*>(sm + NttCfg<LOGN>::SMEM_WORDS);
+            uint32_t* win = reinterpret_cast<uint32_t*>(sm + C::SMEM_WORDS);
             const uint32_t nrej = P.nrej[limb];
             const uint32_t* rej = P.rej[limb];
             const int ncand = N + (int)nrej;
@@ -817,21 +820,21 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
         }
         if constexpr (C::CL == 2) cluster_sync();  // the transform reads both shares
         else __syncthreads();
-        ntt_forward_from_smem<LOGN>(sm, T, [&](int j, uint64_t x) { c1[j] = x; });
+        ntt_forward_from_smem<LOGN, CLX>(sm, T, [&](int j, uint64_t x) { c1[j] = x; });
         __syncthreads();
     }
 }
 
-template <int LOGN>
-__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+template <int LOGN, int CLX = ntt_default_cl(LOGN)>
+__global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, 1)
     k_enc_u(uint64_t* __restrict__ ct, const int64_t* __restrict__ m, const int8_t* __restrict__ e,
             const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
             const LimbTab* __restrict__ tabs, int L,
             int nvec, const uint32_t* __restrict__ flags, int list_mode, int sub) {
     extern __shared__ __align__(16) uint64_t sm[];
-    using C = NttCfg<LOGN>;
+    using C = NttCfg<LOGN, CLX>;
     const int limb = blockIdx.x / C::CL;
-    const int h0 = ntt_rank<LOGN>() * C::H;
+    const int h0 = ntt_rank<LOGN, CLX>() * C::H;
     const LimbTab T = tabs[limb];
     const int nwork = list_mode ? (int)flags[nvec] : 1;
     for (int it = blockIdx.y; it < (list_mode ? nwork : (int)blockIdx.y + 1); it += gridDim.y) {
@@ -844,7 +847,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
         const int64_t* mv = m + ((size_t)v << LOGN);
         const int8_t* ev = e + ((size_t)v << LOGN);
         if (sub && threadIdx.x == 0) prefetch_l2(c1 + h0, (unsigned)C::H * 8u);  // this CTA's share, read by the epilogue
-        ntt_forward_block<LOGN>(
+        ntt_forward_block<LOGN, CLX>(
             sm, T,
             [&](int j) {
                 // |e| < q: the reference's residue of a negative e is q + e
@@ -915,21 +918,23 @@ cudaError_t launch_encrypt_split(const DevCtx& c, uint64_t* ct, const int64_t* m
                                  uint32_t* flags, const StreamPlan* plans, cudaStream_t s_a, cudaStream_t s_x) {
     if (nvec <= 0) return cudaSuccess;
     TSG_LOGN_SWITCH(c.logn, {
-        constexpr size_t smem = ntt_smem_bytes<LG>();
-        constexpr int CL = NttCfg<LG>::CL;
-        cudaError_t er = ensure_smem(k_enc_a<LG>, smem + kEncPlanWinBytes);
+        // each transform on a CTA pair from N = 8192: a small batch leaves
+        // most SMs idle, and the pair halves a transform's latency
+        constexpr int CL = LG >= 13 ? 2 : NttCfg<LG>::CL;
+        constexpr size_t smem = (size_t)NttCfg<LG, CL>::SMEM_WORDS * 8;
+        cudaError_t er = ensure_smem(k_enc_a<LG, CL>, smem);
         if (er != cudaSuccess) return er;
-        er = ensure_smem(k_enc_u<LG>, smem);
+        er = ensure_smem(k_enc_u<LG, CL>, smem);
         if (er != cudaSuccess) return er;
         {
             KScope ks("enc_a", s_a);
-            er = launch_cl(CL, k_enc_a<LG>, dim3(c.L * CL, nvec), NttCfg<LG>::NT, smem, s_a, ct, seeds, c.tabs, c.L,
-                           nvec, flags, plans, 0);
+            er = launch_cl(CL, k_enc_a<LG, CL>, dim3(c.L * CL, nvec), NttCfg<LG, CL>::NT, smem, s_a, ct, seeds, c.tabs,
+                           c.L, nvec, flags, plans, 0);
             if (er != cudaSuccess) return er;
         }
         KScope ks("enc_x", s_x);
-        return launch_cl(CL, k_enc_u<LG>, dim3(c.L * CL, nvec), NttCfg<LG>::NT, smem, s_x, ct, m, e, sk, sks, sk_of,
-                         c.tabs, c.L, nvec, (const uint32_t*)flags, 0, 0);
+        return launch_cl(CL, k_enc_u<LG, CL>, dim3(c.L * CL, nvec), NttCfg<LG, CL>::NT, smem, s_x, ct, m, e, sk, sks,
+                         sk_of, c.tabs, c.L, nvec, (const uint32_t*)flags, 0, 0);
     });
     return cudaGetLastError();
 }
@@ -1289,14 +1294,14 @@ cudaError_t launch_gauss_fix(const DevCtx& c, int8_t* e, const uint64_t* seeds, 
 // ======================================================================
 // Decrypt front half: (ct x pt) then c0 + c1*s, INTT (ciphertext.rs:327-349)
 // ======================================================================
-template <int LOGN>
-__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+template <int LOGN, int CLX = ntt_default_cl(LOGN)>
+__global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, 1)
     k_decrypt_limb(uint64_t* __restrict__ M, int nl, const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs,
                    const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
                    const uint64_t* __restrict__ pt, const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel,
                    int per_ct, const LimbTab* __restrict__ tabs, int L) {
     extern __shared__ __align__(16) uint64_t sm[];
-    const int limb = blockIdx.x / NttCfg<LOGN>::CL, v = blockIdx.y;
+    const int limb = blockIdx.x / NttCfg<LOGN, CLX>::CL, v = blockIdx.y;
     const LimbTab T = tabs[limb];
     const int ci = v / per_ct;
     const uint64_t* c0 = cts + (size_t)ci * ct_stride + ((size_t)limb << LOGN);
@@ -1312,7 +1317,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
         if (pts) pp = pts + (((size_t)pv * L + limb) << LOGN);
     }
     uint64_t* out = M + (((size_t)v * nl + limb) << LOGN);
-    ntt_inverse_block<LOGN>(
+    ntt_inverse_block<LOGN, CLX>(
         sm, T,
         [&](int j) {
             if (pp)  // p*(c0 + c1*s) = c0*p + (c1*p)*s: two Shoup products, in [0, 4q)
@@ -1328,19 +1333,33 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
         [&](int j, uint64_t x) { out[j] = x; });
 }
 
+template <int LG, int CL>
+cudaError_t launch_decrypt_limbs_cl(const DevCtx& c, uint64_t* M, int nl, const uint64_t* cts, long long ct_stride,
+                                    int ct_limbs, const uint64_t* sk, const uint64_t* sks, const int* sk_of,
+                                    const uint64_t* pt, const int* pt_sel, int per_ct, int nvec, cudaStream_t s,
+                                    const uint64_t* pts, const char* scope) {
+    constexpr size_t smem = (size_t)NttCfg<LG, CL>::SMEM_WORDS * 8;
+    cudaError_t er = ensure_smem(k_decrypt_limb<LG, CL>, smem);
+    if (er != cudaSuccess) return er;
+    KScope ks(scope, s);
+    return launch_cl(CL, k_decrypt_limb<LG, CL>, dim3(nl * CL, nvec), NttCfg<LG, CL>::NT, smem, s, M, nl, cts, ct_stride,
+                     ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L);
+}
+
 cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uint64_t* cts, long long ct_stride,
                                  int ct_limbs, const uint64_t* sk, const uint64_t* sks, const int* sk_of,
                                  const uint64_t* pt, const int* pt_sel, int per_ct, int nvec, cudaStream_t s,
-                                 const uint64_t* pts) {
+                                 const uint64_t* pts, const char* scope) {
     if (nvec <= 0) return cudaSuccess;
     TSG_LOGN_SWITCH(c.logn, {
-        constexpr size_t smem = ntt_smem_bytes<LG>();
-        constexpr int CL = NttCfg<LG>::CL;
-        cudaError_t er = ensure_smem(k_decrypt_limb<LG>, smem);
-        if (er != cudaSuccess) return er;
-        KScope ks("decrypt_limb", s);
-        return launch_cl(CL, k_decrypt_limb<LG>, dim3(nl * CL, nvec), NttCfg<LG>::NT, smem, s, M, nl, cts, ct_stride,
-                         ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L);
+        // a batch that leaves SMs idle runs each N >= 8192 transform on a CTA
+        // pair (half the latency); N = 32768 always does
+        constexpr int CLP = LG >= 13 ? 2 : NttCfg<LG>::CL;
+        if (CLP != NttCfg<LG>::CL && (long long)nvec * nl * CLP <= c.sms)
+            return launch_decrypt_limbs_cl<LG, CLP>(c, M, nl, cts, ct_stride, ct_limbs, sk, sks, sk_of, pt, pt_sel,
+                                                    per_ct, nvec, s, pts, scope);
+        return launch_decrypt_limbs_cl<LG, NttCfg<LG>::CL>(c, M, nl, cts, ct_stride, ct_limbs, sk, sks, sk_of, pt,
+                                                           pt_sel, per_ct, nvec, s, pts, scope);
     });
     return cudaGetLastError();
 }
@@ -1681,10 +1700,10 @@ __global__ void __launch_bounds__(256)
 }
 
 cudaError_t launch_crt_seg(const DevCtx& c, const uint64_t* M, int nvec, double inv_scale, const double* W,
-                           int seg_cols, double* seg_out, cudaStream_t s) {
+                           int seg_cols, double* seg_out, cudaStream_t s, const char* scope) {
     if (nvec <= 0) return cudaSuccess;
     if (seg_cols < 1 || seg_cols > kMaxSegCols || c.L < 2 || (c.n % kCrtCl) != 0) return cudaErrorInvalidValue;
-    KScope ks("crt_seg", s);
+    KScope ks(scope, s);
     return launch_cl(kCrtCl, k_crt_seg, dim3((unsigned)(nvec * kCrtCl)), 256, 0, s, M, c.logn, c.crt, inv_scale, W,
                      seg_cols, seg_out);
 }

@@ -195,10 +195,11 @@ cudaError_t launch_keygen_fix(const DevCtx& c, uint64_t* sk, const uint64_t* see
 // p*(c0 + c1*s) with two Shoup products.
 // ct_of(v) = v / per_ct, pt_of(v) = (pt_sel ? pt_sel[v / per_ct] : 0)*per_ct + v % per_ct.
 // sks holds the keys' Shoup companions.
+// `scope` names the launch in the per-kernel profile.
 cudaError_t launch_decrypt_limbs(const DevCtx& c, uint64_t* M, int nl, const uint64_t* cts, long long ct_stride,
                                  int ct_limbs, const uint64_t* sk, const uint64_t* sks, const int* sk_of,
                                  const uint64_t* pt, const int* pt_sel, int per_ct, int nvec, cudaStream_t s,
-                                 const uint64_t* pts = nullptr);
+                                 const uint64_t* pts = nullptr, const char* scope = "decrypt_limb");
 
 // Decrypt back half (ciphertext.rs:351-399 + encoding.rs:219-315): CRT of
 // limbs 0/1 (crt) or limb-0 centring, / scale, canonical embedding.
@@ -226,7 +227,7 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
 // seg_out[v][c] = sum_j CRT(M[v][0][j], M[v][1][j]) * inv_scale * W[c][j]:
 // the back half of the fused decrypt for INTT outputs already in M.
 cudaError_t launch_crt_seg(const DevCtx& c, const uint64_t* M, int nvec, double inv_scale, const double* W,
-                           int seg_cols, double* seg_out, cudaStream_t s);
+                           int seg_cols, double* seg_out, cudaStream_t s, const char* scope = "crt_seg");
 
 // delta[i][d] = sum_k B[d][k] * inter[i][k] (inference_engine.py:1392).
 cudaError_t launch_bmat(const float* B, const double* inter, double* delta, int nvec, int d, int r,

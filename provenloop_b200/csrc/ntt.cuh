@@ -39,6 +39,11 @@
 // and reaching the partner's elements through distributed shared memory;
 // the other two passes are local.  The kernel must then be launched with
 // cluster dimension 2 along x, and block pairs see the same work item.
+// The same split is available from N = 8192 (CL = 2 as a template argument),
+// which halves the work of a lone transform's CTA when a small batch leaves
+// most SMs idle.  Below N = 32768 a pair keeps 16 values per thread (radix-16
+// passes, N/32 threads per CTA), so each CTA still has 16 warps to hide the
+// latency of its loads.
 #pragma once
 #include <cooperative_groups.h>
 
@@ -62,12 +67,19 @@ struct LimbTab {
 // Padded shared-memory index of element j.
 __device__ __forceinline__ int pad(int j) { return j + (j >> 4); }
 
-template <int LOGN>
+// CTAs per transform by default: two from N = 32768 (a poly-limb no longer
+// fits one CTA).  Smaller transforms may also be split over a pair (CL = 2
+// from N = 8192) to halve the latency of a lone transform.
+__host__ __device__ constexpr int ntt_default_cl(int logn) { return logn >= 15 ? 2 : 1; }
+
+template <int LOGN, int CL_ = ntt_default_cl(LOGN)>
 struct NttCfg {
     static constexpr int N = 1 << LOGN;
-    static constexpr int CL = LOGN >= 15 ? 2 : 1;   // CTAs per transform (cluster size)
+    static constexpr int CL = CL_;                  // CTAs per transform (cluster size)
     static constexpr int H = N / CL;                // elements held by one CTA
-    static constexpr int E = LOGN >= 13 ? 32 : 16;  // values per thread
+    // values per thread: 32 from N = 8192, except a pair below N = 32768,
+    // which keeps 512 threads per CTA (16 values) to hide load latency
+    static constexpr int E = LOGN >= 13 && (CL_ == 1 || LOGN >= 15) ? 32 : 16;
     static constexpr int NT = H / E;                // threads per CTA
     static constexpr int JS = N / E;                // element stride of a first-pass set
     static constexpr int RMAX = E == 32 ? 5 : 4;    // stages per pass
@@ -76,6 +88,7 @@ struct NttCfg {
     // stages of forward pass p: RMAX each, the last pass the remainder
     __host__ __device__ static constexpr int fwd_r(int p) { return p < NPASS - 1 ? RMAX : LOGN - RMAX * (NPASS - 1); }
     __host__ __device__ static constexpr int fwd_s0(int p) { return p * RMAX; }
+    static_assert(CL == 1 || (CL == 2 && LOGN >= 13), "pairs from N = 8192");
 };
 
 // Geometry of a radix-2^R pass whose smallest butterfly span is 2^TLOG:
@@ -88,12 +101,12 @@ struct NttCfg {
 // With CL = 2 the CTA of rank h takes sets h*NT*SETS .. (h+1)*NT*SETS - 1.
 // In a local pass (TLOG + R < LOGN) those are exactly the sets whose
 // elements lie in half h, and pbase gives the local padded address.
-template <int LOGN, int R, int TLOG>
+template <int LOGN, int R, int TLOG, int CL = ntt_default_cl(LOGN)>
 struct Geo {
     static constexpr int N = 1 << LOGN;
-    static constexpr int NT = NttCfg<LOGN>::NT;
-    static constexpr int H = NttCfg<LOGN>::H;
-    static constexpr int SETS = NttCfg<LOGN>::E >> R;
+    static constexpr int NT = NttCfg<LOGN, CL>::NT;
+    static constexpr int H = NttCfg<LOGN, CL>::H;
+    static constexpr int SETS = NttCfg<LOGN, CL>::E >> R;
     __device__ __forceinline__ static int sigma(int h, int tid, int u) { return h * NT * SETS + tid + NT * u; }
     __device__ __forceinline__ static int pbase(int sg) {
         return pad((((sg >> TLOG) << (TLOG + R)) + (sg & ((1 << TLOG) - 1))) & (H - 1));
@@ -101,9 +114,9 @@ struct Geo {
     __host__ __device__ static constexpr int koff(int k) { return (k << TLOG) + ((k << TLOG) >> 4); }
 };
 
-template <int LOGN, int R, int TLOG>
+template <int LOGN, int R, int TLOG, int CL>
 __device__ __forceinline__ void smem_load(const uint64_t* sm, uint64_t* v, int h, int tid) {
-    using G = Geo<LOGN, R, TLOG>;
+    using G = Geo<LOGN, R, TLOG, CL>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++) {
         const uint64_t* b = sm + G::pbase(G::sigma(h, tid, u));
@@ -112,9 +125,9 @@ __device__ __forceinline__ void smem_load(const uint64_t* sm, uint64_t* v, int h
     }
 }
 
-template <int LOGN, int R, int TLOG>
+template <int LOGN, int R, int TLOG, int CL>
 __device__ __forceinline__ void smem_store(uint64_t* sm, const uint64_t* v, int h, int tid) {
-    using G = Geo<LOGN, R, TLOG>;
+    using G = Geo<LOGN, R, TLOG, CL>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++) {
         uint64_t* b = sm + G::pbase(G::sigma(h, tid, u));
@@ -135,41 +148,16 @@ __device__ __forceinline__ uint64_t* cluster_smem(uint64_t* sm, int rank) {
 // set base sigma < JS has no bits in common with k*JS (a multiple of JS), so
 // pad(sigma + k*JS) = pad(sigma) + xoff(k): one base register per half plus
 // compile-time offsets.
-template <int LOGN>
+template <int LOGN, int CL>
 __host__ __device__ constexpr int xoff(int k) {
-    return k * NttCfg<LOGN>::JS + ((k * NttCfg<LOGN>::JS) >> 4);
+    return k * NttCfg<LOGN, CL>::JS + ((k * NttCfg<LOGN, CL>::JS) >> 4);
 }
 
 // Rank of this CTA within its transform (0 unless CL = 2).
-template <int LOGN>
+template <int LOGN, int CL = ntt_default_cl(LOGN)>
 __device__ __forceinline__ int ntt_rank() {
-    if constexpr (NttCfg<LOGN>::CL == 2) return cluster_rank();
+    if constexpr (CL == 2) return cluster_rank();
     return 0;
-}
-
-// A poly-limb staged in the shared memory of the transform's CTAs (each
-// CTA its own share, at padded local positions): element j for callers
-// whose first-pass loader reads shared memory.
-template <int LOGN>
-struct SmemView {
-    using C = NttCfg<LOGN>;
-    uint64_t* part[C::CL];
-    __device__ __forceinline__ uint64_t operator()(int j) const {
-        if constexpr (C::CL == 2) return (j < C::H ? part[0] : part[1])[pad(j & (C::H - 1))];
-        return part[0][pad(j)];
-    }
-};
-
-template <int LOGN>
-__device__ __forceinline__ SmemView<LOGN> ntt_smem_view(uint64_t* sm) {
-    SmemView<LOGN> v;
-    if constexpr (NttCfg<LOGN>::CL == 2) {
-        v.part[0] = cluster_smem(sm, 0);
-        v.part[1] = cluster_smem(sm, 1);
-    } else {
-        v.part[0] = sm;
-    }
-    return v;
 }
 
 // One forward CT stage (sub-stage r of a radix-2^R pass starting at stage
@@ -198,11 +186,11 @@ __device__ __forceinline__ void fwd_stage(uint64_t* x, int g, const ulonglong2* 
     if constexpr (r + 1 < R) fwd_stage<R, S0, r + 1, NC>(x, g, fw, q, q4);
 }
 
-template <int LOGN, int R, int S0, bool NC>
+template <int LOGN, int R, int S0, bool NC, int CL>
 __device__ __forceinline__ void fwd_compute(uint64_t* v, const ulonglong2* __restrict__ fw, uint64_t q, int h,
                                             int tid) {
     constexpr int TLOG = LOGN - S0 - R;
-    using G = Geo<LOGN, R, TLOG>;
+    using G = Geo<LOGN, R, TLOG, CL>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++)
         fwd_stage<R, S0, 0, NC>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, fw, q, 4 * q);
@@ -249,10 +237,10 @@ __device__ __forceinline__ void inv_stage(uint64_t* x, int g, const ulonglong2* 
     if constexpr (r + 1 < R) inv_stage<LOGN, R, TLOG, r + 1, NC>(x, g, iw, T, q4);
 }
 
-template <int LOGN, int R, int TLOG, bool NC>
+template <int LOGN, int R, int TLOG, bool NC, int CL>
 __device__ __forceinline__ void inv_compute(uint64_t* v, const ulonglong2* __restrict__ iw, const LimbTab& T, int h,
                                             int tid) {
-    using G = Geo<LOGN, R, TLOG>;
+    using G = Geo<LOGN, R, TLOG, CL>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++)
         inv_stage<LOGN, R, TLOG, 0, NC>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, iw, T, 4 * T.q);
@@ -274,32 +262,32 @@ __device__ __forceinline__ uint64_t canon4(uint64_t x, uint64_t q) {
 // Forward pass P (stages fwd_s0(P) ..) and the ones after it.  Pass 0's
 // values are already in v; every pass stores its results back to the
 // positions it read (its own sets), so one barrier between passes suffices.
-template <int LOGN, int P, bool NC>
+template <int LOGN, int P, bool NC, int CL>
 __device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulonglong2* fw, uint64_t q, int h,
                                            int tid) {
-    using C = NttCfg<LOGN>;
+    using C = NttCfg<LOGN, CL>;
     constexpr int R = C::fwd_r(P), S0 = C::fwd_s0(P), TLOG = LOGN - S0 - R;
     if constexpr (P > 0) {
         if constexpr (C::CL == 2 && P == 1) cluster_sync();  // both halves written
         else __syncthreads();
-        smem_load<LOGN, R, TLOG>(sm, v, h, tid);
+        smem_load<LOGN, R, TLOG, CL>(sm, v, h, tid);
     }
-    fwd_compute<LOGN, R, S0, NC>(v, fw, q, h, tid);
+    fwd_compute<LOGN, R, S0, NC, CL>(v, fw, q, h, tid);
     if constexpr (C::CL == 2 && P == 0) {
         // the first pass's sets span both halves: element sigma + k*JS goes
         // to CTA k / (E/2).  The partner must be done reading its shared
         // memory (the previous transform, or a loader that reads it) first.
-        static_assert(R == 5 && C::E == 32, "cluster NTT expects radix-32 passes");
+        static_assert((1 << R) == C::E, "the cross-half pass holds a whole set per thread");
         cluster_sync();
-        const int sg = Geo<LOGN, R, TLOG>::sigma(h, tid, 0);
+        const int sg = Geo<LOGN, R, TLOG, CL>::sigma(h, tid, 0);
         uint64_t* s0 = cluster_smem(sm, 0) + pad(sg);
         uint64_t* s1 = cluster_smem(sm, 1) + pad(sg);
 #pragma unroll
-        for (int k = 0; k < C::E; k++) (k < C::E / 2 ? s0 : s1)[xoff<LOGN>(k & (C::E / 2 - 1))] = v[k];
+        for (int k = 0; k < C::E; k++) (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))] = v[k];
     } else {
-        smem_store<LOGN, R, TLOG>(sm, v, h, tid);
+        smem_store<LOGN, R, TLOG, CL>(sm, v, h, tid);
     }
-    if constexpr (P + 1 < C::NPASS) fwd_passes<LOGN, P + 1, NC>(sm, v, fw, q, h, tid);
+    if constexpr (P + 1 < C::NPASS) fwd_passes<LOGN, P + 1, NC, CL>(sm, v, fw, q, h, tid);
 }
 
 // Forward transform of one poly-limb.  ld(j) returns element j (< 8q, e.g.
@@ -307,25 +295,24 @@ __device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulon
 // CL = 2); st(j, v) receives canonical output j for j = rank*H + tid + k*NT,
 // coalesced.  `sm` holds NttCfg<LOGN>::SMEM_WORDS u64.  All NT threads of
 // the block (both blocks of the cluster for CL = 2) must call this; a caller
-// that reuses `sm` afterwards must __syncthreads() first.  If ld reads `sm`,
-// each thread may only read the positions of its own first-pass elements
-// (through ntt_smem_view for CL = 2, after a cluster_sync).
+// that reuses `sm` afterwards must __syncthreads() first.  A caller whose
+// input is staged in shared memory uses ntt_forward_from_smem instead.
 // first(k, sigma) supplies element sigma + k*JS of the first-pass set
 // (k is a compile-time constant after unrolling).
-template <int LOGN, bool NC, class First, class St>
+template <int LOGN, bool NC, int CL = ntt_default_cl(LOGN), class First, class St>
 __device__ __forceinline__ void ntt_forward_core(uint64_t* sm, const LimbTab& T, First& first, St& st) {
-    using C = NttCfg<LOGN>;
+    using C = NttCfg<LOGN, CL>;
     static_assert(LOGN >= 10 && LOGN <= 15, "NTT supports N in [1024, 32768]");
     static_assert(C::fwd_r(0) == C::RMAX, "the first pass takes RMAX stages");
     const int tid = threadIdx.x;
-    const int h = ntt_rank<LOGN>();
+    const int h = ntt_rank<LOGN, CL>();
     const ulonglong2* fw = reinterpret_cast<const ulonglong2*>(T.tw);
     uint64_t v[C::E];
     // first pass: one set per thread, elements sigma + k*JS
     const int sg = h * C::NT + tid;
 #pragma unroll
     for (int k = 0; k < C::E; k++) v[k] = first(k, sg);
-    fwd_passes<LOGN, 0, NC>(sm, v, fw, T.q, h, tid);
+    fwd_passes<LOGN, 0, NC, CL>(sm, v, fw, T.q, h, tid);
     __syncthreads();
     // own share, coalesced: j = h*H + tid + k*NT
 #pragma unroll
@@ -335,68 +322,68 @@ __device__ __forceinline__ void ntt_forward_core(uint64_t* sm, const LimbTab& T,
     }
 }
 
-template <int LOGN, bool NC, class Ld, class St>
+template <int LOGN, bool NC, int CL = ntt_default_cl(LOGN), class Ld, class St>
 __device__ __forceinline__ void ntt_forward_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
-    auto first = [&](int k, int sg) { return ld(sg + k * NttCfg<LOGN>::JS); };
-    ntt_forward_core<LOGN, NC>(sm, T, first, st);
+    auto first = [&](int k, int sg) { return ld(sg + k * NttCfg<LOGN, CL>::JS); };
+    ntt_forward_core<LOGN, NC, CL>(sm, T, first, st);
 }
 
 // Forward transform of a poly-limb already staged in shared memory: each
 // CTA's share at its own padded local positions, complete (__syncthreads,
 // or cluster_sync for CL = 2) before the call.  The first pass reads it with
 // the half chosen at compile time, so no per-element address selection.
-template <int LOGN, class St>
+template <int LOGN, int CL = ntt_default_cl(LOGN), class St>
 __device__ __forceinline__ void ntt_forward_from_smem(uint64_t* sm, const LimbTab& T, St st) {
-    using C = NttCfg<LOGN>;
-    if constexpr (C::CL == 2) {
-        const int sg0 = ntt_rank<LOGN>() * C::NT + threadIdx.x;
+    using C = NttCfg<LOGN, CL>;
+    if constexpr (CL == 2) {
+        const int sg0 = ntt_rank<LOGN, CL>() * C::NT + threadIdx.x;
         const uint64_t* s0 = cluster_smem(sm, 0) + pad(sg0);
         const uint64_t* s1 = cluster_smem(sm, 1) + pad(sg0);
-        auto first = [&](int k, int) { return (k < C::E / 2 ? s0 : s1)[xoff<LOGN>(k & (C::E / 2 - 1))]; };
-        ntt_forward_core<LOGN, false>(sm, T, first, st);
+        auto first = [&](int k, int) { return (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))]; };
+        ntt_forward_core<LOGN, false, CL>(sm, T, first, st);
     } else {
         auto first = [&](int k, int sg) { return sm[pad(sg + k * C::JS)]; };
-        ntt_forward_core<LOGN, false>(sm, T, first, st);
+        ntt_forward_core<LOGN, false, CL>(sm, T, first, st);
     }
 }
 
 // Forward transform.  The correction-free variant (NC) measured no faster
 // here: the forward butterfly is bound by the IMAD pipe, not by the ALU
 // instructions NC removes, so every limb uses the corrected butterflies.
-template <int LOGN, class Ld, class St>
+template <int LOGN, int CL = ntt_default_cl(LOGN), class Ld, class St>
 __device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
-    ntt_forward_impl<LOGN, false>(sm, T, ld, st);
+    ntt_forward_impl<LOGN, false, CL>(sm, T, ld, st);
 }
 
 // Inverse pass P in GS order (spans 1 .. N/2) mirrors forward pass
 // NPASS-1-P.  Its values are in shared memory on entry; the last pass keeps
 // its results (elements tid + k*NT) in v.
-template <int LOGN, int P, bool NC>
+template <int LOGN, int P, bool NC, int CL>
 __device__ __forceinline__ void inv_passes(uint64_t* sm, uint64_t* v, const ulonglong2* iw, const LimbTab& T, int h,
                                            int tid) {
-    using C = NttCfg<LOGN>;
+    using C = NttCfg<LOGN, CL>;
     constexpr int FP = C::NPASS - 1 - P;
     constexpr int R = C::fwd_r(FP), TLOG = LOGN - C::fwd_s0(FP) - R;
     if constexpr (C::CL == 2 && FP == 0) {
         // the last pass's sets span both halves: element sigma + k*JS is in
         // CTA k / (E/2); once both CTAs hold their values in registers the
         // partner may reuse its shared memory
-        static_assert(R == 5 && C::E == 32, "cluster NTT expects radix-32 passes");
+        static_assert((1 << R) == C::E, "the cross-half pass holds a whole set per thread");
         cluster_sync();
-        const int sg = Geo<LOGN, R, TLOG>::sigma(h, tid, 0);
+        const int sg = Geo<LOGN, R, TLOG, CL>::sigma(h, tid, 0);
         const uint64_t* s0 = cluster_smem(sm, 0) + pad(sg);
         const uint64_t* s1 = cluster_smem(sm, 1) + pad(sg);
 #pragma unroll
-        for (int k = 0; k < C::E; k++) v[k] = (k < C::E / 2 ? s0 : s1)[xoff<LOGN>(k & (C::E / 2 - 1))];
+        for (int k = 0; k < C::E; k++) v[k] = (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))];
         cluster_sync();
     } else {
         __syncthreads();
-        smem_load<LOGN, R, TLOG>(sm, v, h, tid);
+        smem_load<LOGN, R, TLOG, CL>(sm, v, h, tid);
     }
-    inv_compute<LOGN, R, TLOG, NC>(v, iw, T, h, tid);
+    inv_compute<LOGN, R, TLOG, NC, CL>(v, iw, T, h, tid);
     if constexpr (P + 1 < C::NPASS) {
-        smem_store<LOGN, R, TLOG>(sm, v, h, tid);
-        inv_passes<LOGN, P + 1, NC>(sm, v, iw, T, h, tid);
+        smem_store<LOGN, R, TLOG, CL>(sm, v, h, tid);
+        inv_passes<LOGN, P + 1, NC, CL>(sm, v, iw, T, h, tid);
     }
 }
 
@@ -405,12 +392,12 @@ __device__ __forceinline__ void inv_passes(uint64_t* sm, uint64_t* v, const ulon
 // output j for j = sigma + k*JS, sigma = rank*NT + tid.  A caller that reuses
 // `sm` afterwards must __syncthreads() first.
 // sink(k, sigma, x) receives canonical output sigma + k*JS.
-template <int LOGN, bool NC, class Ld, class Sink>
+template <int LOGN, bool NC, int CL = ntt_default_cl(LOGN), class Ld, class Sink>
 __device__ __forceinline__ void ntt_inverse_core(uint64_t* sm, const LimbTab& T, Ld& ld, Sink& sink) {
-    using C = NttCfg<LOGN>;
+    using C = NttCfg<LOGN, CL>;
     static_assert(LOGN >= 10 && LOGN <= 15, "NTT supports N in [1024, 32768]");
     const int tid = threadIdx.x;
-    const int h = ntt_rank<LOGN>();
+    const int h = ntt_rank<LOGN, CL>();
     const ulonglong2* iw = reinterpret_cast<const ulonglong2*>(T.tw) + C::N;
     uint64_t v[C::E];
     // own share: j = h*H + tid + k*NT
@@ -419,47 +406,47 @@ __device__ __forceinline__ void ntt_inverse_core(uint64_t* sm, const LimbTab& T,
         const int jl = tid + k * C::NT;
         sm[pad(jl)] = ld(h * C::H + jl);
     }
-    inv_passes<LOGN, 0, NC>(sm, v, iw, T, h, tid);
+    inv_passes<LOGN, 0, NC, CL>(sm, v, iw, T, h, tid);
     // last-pass set: elements sigma + k*JS (for CL = 1, sigma = tid)
     const int sg = h * C::NT + tid;
 #pragma unroll
     for (int k = 0; k < C::E; k++) sink(k, sg, canon4(v[k], T.q));
 }
 
-template <int LOGN, bool NC, class Ld, class St>
+template <int LOGN, bool NC, int CL = ntt_default_cl(LOGN), class Ld, class St>
 __device__ __forceinline__ void ntt_inverse_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
-    auto sink = [&](int k, int sg, uint64_t x) { st(sg + k * NttCfg<LOGN>::JS, x); };
-    ntt_inverse_core<LOGN, NC>(sm, T, ld, sink);
+    auto sink = [&](int k, int sg, uint64_t x) { st(sg + k * NttCfg<LOGN, CL>::JS, x); };
+    ntt_inverse_core<LOGN, NC, CL>(sm, T, ld, sink);
 }
 
 // Inverse transform whose canonical output is parked in shared memory: each
 // CTA's share at its own padded local positions (through DSMEM for CL = 2,
 // complete on return; for CL = 1 a thread's outputs are the positions
 // pad(tid + k*NT) it alone reads afterwards).
-template <int LOGN, bool NC, class Ld>
+template <int LOGN, bool NC, int CL = ntt_default_cl(LOGN), class Ld>
 __device__ __forceinline__ void ntt_inverse_to_smem(uint64_t* sm, const LimbTab& T, Ld& ld) {
-    using C = NttCfg<LOGN>;
-    if constexpr (C::CL == 2) {
-        const int sg0 = ntt_rank<LOGN>() * C::NT + threadIdx.x;
+    using C = NttCfg<LOGN, CL>;
+    if constexpr (CL == 2) {
+        const int sg0 = ntt_rank<LOGN, CL>() * C::NT + threadIdx.x;
         uint64_t* s0 = cluster_smem(sm, 0) + pad(sg0);
         uint64_t* s1 = cluster_smem(sm, 1) + pad(sg0);
-        auto sink = [&](int k, int, uint64_t x) { (k < C::E / 2 ? s0 : s1)[xoff<LOGN>(k & (C::E / 2 - 1))] = x; };
-        ntt_inverse_core<LOGN, NC>(sm, T, ld, sink);
+        auto sink = [&](int k, int, uint64_t x) { (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))] = x; };
+        ntt_inverse_core<LOGN, NC, CL>(sm, T, ld, sink);
         cluster_sync();
     } else {
         auto sink = [&](int k, int sg, uint64_t x) { sm[pad(sg + k * C::JS)] = x; };
-        ntt_inverse_core<LOGN, NC>(sm, T, ld, sink);
+        ntt_inverse_core<LOGN, NC, CL>(sm, T, ld, sink);
     }
 }
 
 // Inverse transform, with the correction-free butterflies when
 // 4q * 2^LOGN * 2 fits 64 bits (a uniform branch per CTA).
-template <int LOGN, class Ld, class St>
+template <int LOGN, int CL = ntt_default_cl(LOGN), class Ld, class St>
 __device__ __forceinline__ void ntt_inverse_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
     if (T.q < (1ULL << (61 - LOGN)))
-        ntt_inverse_impl<LOGN, true>(sm, T, ld, st);
+        ntt_inverse_impl<LOGN, true, CL>(sm, T, ld, st);
     else
-        ntt_inverse_impl<LOGN, false>(sm, T, ld, st);
+        ntt_inverse_impl<LOGN, false, CL>(sm, T, ld, st);
 }
 
 }  // namespace tsg

@@ -194,9 +194,10 @@ struct ts_ctx {
     DevCtx dc{};
     cudaStream_t own = nullptr, stream = nullptr;
     // second stream and fork / join events of the small-batch encryption,
-    // created by its first use
-    cudaStream_t side = nullptr;
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_gauss = nullptr;
+    // and a third stream for the decrypt side's code warm-up; created by
+    // their first use
+    cudaStream_t side = nullptr, warm = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_gauss = nullptr, ev_warm0 = nullptr, ev_warm1 = nullptr;
     // grow-only scratch
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
@@ -514,6 +515,16 @@ EncWork enc_work(const Carve& cv, void* base, size_t cap, const size_t idx[5]) {
                    cv.at<uint32_t>(base, idx[3]), cv.at<StreamPlan>(base, idx[4]), cap};
 }
 
+// The side streams and events of the small-batch forms (first use).
+int ensure_side_streams(ts_ctx* c) {
+    if (c->side) return TS_OK;
+    CU(cudaStreamCreateWithFlags(&c->warm, cudaStreamNonBlocking));
+    for (cudaEvent_t* e : {&c->ev_fork, &c->ev_join, &c->ev_gauss, &c->ev_warm0, &c->ev_warm1})
+        CU(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+    CU(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
+    return TS_OK;
+}
+
 // Core of every secret-key encryption: `count` vectors already on the device
 // (SlotSrc), seeds / key indexes on the device, output ct [count][2][L][n].
 // Uses only the work buffers in `w` (callers own the scratch layout).
@@ -537,12 +548,7 @@ int encrypt_core(ts_ctx* c, const SlotSrc& src, size_t count, const uint64_t* d_
             // small batch (a decode step): latency, not throughput, matters.
             // c1 = NTT(a) runs on a side stream while the encode and
             // NTT(m + e) run on the context's stream; c0 -= c1*s after the join
-            if (!c->side) {
-                CU(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
-                CU(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
-                CU(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming));
-                CU(cudaEventCreateWithFlags(&c->ev_gauss, cudaEventDisableTiming));
-            }
+            if (int rc = ensure_side_streams(c)) return rc;
             CU(cudaEventRecord(c->ev_fork, c->stream));
             CU(cudaStreamWaitEvent(c->side, c->ev_fork, 0));
             {
@@ -726,13 +732,13 @@ void ctx_free(ts_ctx* c) {
     cudaFree(c->d_tabs);
     cudaFree(c->d_fft);
     cudaFree(c->d_stats);
-    if (c->side) {
-        cudaStreamSynchronize(c->side);
-        cudaStreamDestroy(c->side);
-        cudaEventDestroy(c->ev_fork);
-        cudaEventDestroy(c->ev_join);
-        cudaEventDestroy(c->ev_gauss);
-    }
+    for (cudaStream_t st : {c->side, c->warm})
+        if (st) {
+            cudaStreamSynchronize(st);
+            cudaStreamDestroy(st);
+        }
+    for (cudaEvent_t e : {c->ev_fork, c->ev_join, c->ev_gauss, c->ev_warm0, c->ev_warm1})
+        if (e) cudaEventDestroy(e);
     if (c->own) cudaStreamDestroy(c->own);
     delete c;
 }
@@ -1432,6 +1438,17 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
                      // both limbs of every vector (and the FFT scratch of the decode)
                      i_M = cv.add(lo->d_w && c->logn < 15 ? (size_t)c->dc.sms * N * 8 : nv * nb * 2 * N * 8),
                      i_fd = cv.add(lo->d_w ? 0 : nv * nb * 2 * N * 8), i_sg = cv.add(nv * nb * cols * 8);
+        // Small batches (a decode step): the weight stream of the model
+        // between two calls evicts the kernels' code from L2, and a lone
+        // transform's CTA then stalls on instruction fetches from HBM.  A
+        // copy of the decrypt-side kernels on one vector of this call's
+        // buffers (outputs to scratch) runs on a third stream from the start
+        // of the call and brings their code back into L2 before the real
+        // launches need it.
+        const int cl = c->logn >= 15 ? 2 : 1;
+        const bool code_warm = lo->d_w && (int)(nv * L * cl * 2) <= c->dc.sms &&
+                          (c->logn == 15 || (c->logn >= 13 && (int)(nv * nb * 2 * 2) <= c->dc.sms));
+        const size_t i_wm = cv.add(code_warm ? 2 * N * 8 + kMaxSegCols * 8 : 0);
         rc = ensure_scratch(c, cv.total());
         if (rc) break;
         void* S = c->scratch;
@@ -1447,6 +1464,19 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         double* sg = cv.at<double>(S, i_sg);
         if (!io_on_device) rc = h2d_small(c, dh, h + v0 * d, nv * d);
         if (rc) break;
+        if (code_warm) {
+            rc = ensure_side_streams(c);
+            if (rc) break;
+            uint64_t* wm = cv.at<uint64_t>(S, i_wm);
+            CU(cudaEventRecord(c->ev_warm0, c->stream));
+            CU(cudaStreamWaitEvent(c->warm, c->ev_warm0, 0));
+            CU(launch_decrypt_limbs(c->dc, wm, 2, ct, (long long)2 * L * N, (int)L, sk->d, sk_shoup(sk), nullptr,
+                                    lo->d_pt, nullptr, (int)nb, 1, c->warm,
+                                    lo->d_pt + (size_t)lo->experts * nb * L * N, "warm_decrypt_limb"));
+            CU(launch_crt_seg(c->dc, wm, 1, 1.0 / scale2, lo->d_w, (int)cols, reinterpret_cast<double*>(wm + 2 * N),
+                              c->warm, "warm_crt_seg"));
+            CU(cudaEventRecord(c->ev_warm1, c->warm));
+        }
         // 1. encrypt the cols-fold replicated hidden states (:1267-1272)
         SlotSrc src{dh, 0, (int)d, (long long)d, (int)d, (int)cols};
         const size_t eidx[5] = {i_m, i_e, i_fe, i_fl, i_pl};
@@ -1468,7 +1498,6 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         rc = encrypt_core(c, src, nv, ds, sk_index ? dsk : nullptr, sk->d, sk_shoup(sk), ct,
                           enc_work(cv, S, nv, eidx), &warm);
         if (rc) break;
-        const int cl = c->logn >= 15 ? 2 : 1;
         if (lo->d_w && (c->logn == 15 || (int)(nv * nb * 2 * cl) <= c->dc.sms)) {
             // N = 32768, or a batch too small to fill the GPU: the limb-0 and
             // limb-1 INTTs of every (delta, batch) run as separate CTAs
@@ -1494,6 +1523,7 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
             CU(launch_decode(c->dc, M, 2, true, scale2, (int)(nv * nb), nullptr, sg, (int)d, (int)cols, fd,
                              c->stream));
         }
+        if (code_warm) CU(cudaStreamWaitEvent(c->stream, c->ev_warm1, 0));  // join the warm-up stream
         CU(launch_gather_inter(sg, dinter, (int)nv, (int)nb, (int)cols, (int)r, c->stream));
         // 4. delta = B @ intermediate (:1392)
         CU(launch_bmat(lo->d_b, dinter, dout, (int)nv, (int)d, (int)r, expert ? dex : nullptr, (long long)d * r,

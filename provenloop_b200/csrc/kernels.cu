@@ -230,6 +230,13 @@ cudaError_t launch_cl(int cl, void (*kern)(KArgs...), dim3 grid, unsigned block,
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// Whether a kernel instantiation carries the FP64 transform mode: yes for
+// the throughput instantiations; no for the CTA-pair variants below
+// N = 32768, which serve small batches, where the second code path's
+// instruction fetches cost more than its faster butterflies save.
+template <int LOGN, int CL>
+constexpr bool kPairFp = CL == ntt_default_cl(LOGN);
+
 // Shared-memory bytes of one NTT CTA (its padded share of a poly-limb).
 template <int LOGN>
 constexpr size_t ntt_smem_bytes() {
@@ -820,7 +827,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, 1)
         }
         if constexpr (C::CL == 2) cluster_sync();  // the transform reads both shares
         else __syncthreads();
-        ntt_forward_from_smem<LOGN, CLX>(sm, T, [&](int j, uint64_t x) { c1[j] = x; });
+        ntt_forward_from_smem<LOGN, CLX, kPairFp<LOGN, CLX>>(sm, T, [&](int j, uint64_t x) { c1[j] = x; });
         __syncthreads();
     }
 }
@@ -847,7 +854,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, 1)
         const int64_t* mv = m + ((size_t)v << LOGN);
         const int8_t* ev = e + ((size_t)v << LOGN);
         if (sub && threadIdx.x == 0) prefetch_l2(c1 + h0, (unsigned)C::H * 8u);  // this CTA's share, read by the epilogue
-        ntt_forward_block<LOGN, CLX>(
+        ntt_forward_block<LOGN, CLX, kPairFp<LOGN, CLX>>(
             sm, T,
             [&](int j) {
                 // |e| < q: the reference's residue of a negative e is q + e
@@ -1317,7 +1324,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, 1)
         if (pts) pp = pts + (((size_t)pv * L + limb) << LOGN);
     }
     uint64_t* out = M + (((size_t)v * nl + limb) << LOGN);
-    ntt_inverse_block<LOGN, CLX>(
+    ntt_inverse_block<LOGN, CLX, kPairFp<LOGN, CLX>>(
         sm, T,
         [&](int j) {
             if (pp)  // p*(c0 + c1*s) = c0*p + (c1*p)*s: two Shoup products, in [0, 4q)
@@ -1542,7 +1549,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
                 return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q);
             };
             auto st = [&](int j, uint64_t x) { m0v[j] = x; };
-            ntt_inverse_impl<LOGN, NC0>(sm, T, ld, st);
+            ntt_inverse_impl<LOGN, NC0, NttCfg<LOGN>::CL, false>(sm, T, ld, st);
         }
         __syncthreads();
         double acc[kMaxSegCols];
@@ -1563,7 +1570,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
             // the last pass parks element j in the shared memory of the CTA
             // that holds j (its own for CL = 1, either for CL = 2); for CL = 2
             // both CTAs' parks (and limb-0 writes) are complete on return
-            ntt_inverse_to_smem<LOGN, NC1>(sm, T, ld);
+            ntt_inverse_to_smem<LOGN, NC1, NttCfg<LOGN>::CL, false>(sm, T, ld);
         }
         // CRT, / Delta^2 and the segment functionals over this CTA's share
         // j = h*H + tid + k*NT; limb-0 loads issued in groups of 8 ahead of
@@ -1628,7 +1635,9 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
                              cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
     if (seg_cols < 1 || seg_cols > kMaxSegCols || c.L < 2) return cudaErrorInvalidValue;
-    // correction-free INTT where the modulus leaves the headroom (as in ntt_inverse_block)
+    // correction-free INTT where the modulus leaves the headroom (as in
+    // ntt_inverse_block); this kernel stays integer-only (its FP64 variant
+    // spilled 648 bytes and ran 15% slower)
     const bool nc0 = c.q0 < (1ULL << (61 - c.logn)), nc1 = c.q1 < (1ULL << (61 - c.logn));
     TSG_LOGN_SWITCH(c.logn, {
         constexpr size_t smem = ntt_smem_bytes<LG>();

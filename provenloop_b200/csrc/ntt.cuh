@@ -47,6 +47,8 @@
 #pragma once
 #include <cooperative_groups.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace tsg {
@@ -61,7 +63,7 @@ struct LimbTab {
     uint64_t bmu;          // Barrett floor(2^(2k) / q)
     uint64_t thresh;       // 2^64 mod q: range_u64 rejection threshold (rng.rs:126)
     int bk;                // bitlen(q)
-    int pad;
+    int fp;                // q < 2^50: the transforms run in FP64 (below); tables at tw + 4n
 };
 
 // Padded shared-memory index of element j.
@@ -114,25 +116,38 @@ struct Geo {
     __host__ __device__ static constexpr int koff(int k) { return (k << TLOG) + ((k << TLOG) >> 4); }
 };
 
-template <int LOGN, int R, int TLOG, int CL>
-__device__ __forceinline__ void smem_load(const uint64_t* sm, uint64_t* v, int h, int tid) {
+// Values of a transform: u64 residues (integer modes) or FP64 integers
+// (FP64 mode); shared memory holds their 64-bit patterns either way.
+constexpr int kModeInt = 0, kModeNC = 1, kModeFp = 2;
+template <int M>
+using NttV = typename std::conditional<M == kModeFp, double, uint64_t>::type;
+__device__ __forceinline__ uint64_t vbits(uint64_t x) { return x; }
+__device__ __forceinline__ uint64_t vbits(double x) { return (uint64_t)__double_as_longlong(x); }
+template <class V>
+__device__ __forceinline__ V vfrom(uint64_t b) {
+    if constexpr (std::is_same<V, double>::value) return __longlong_as_double((long long)b);
+    else return b;
+}
+
+template <int LOGN, int R, int TLOG, int CL, class V>
+__device__ __forceinline__ void smem_load(const uint64_t* sm, V* v, int h, int tid) {
     using G = Geo<LOGN, R, TLOG, CL>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++) {
         const uint64_t* b = sm + G::pbase(G::sigma(h, tid, u));
 #pragma unroll
-        for (int k = 0; k < (1 << R); k++) v[u * (1 << R) + k] = b[G::koff(k)];
+        for (int k = 0; k < (1 << R); k++) v[u * (1 << R) + k] = vfrom<V>(b[G::koff(k)]);
     }
 }
 
-template <int LOGN, int R, int TLOG, int CL>
-__device__ __forceinline__ void smem_store(uint64_t* sm, const uint64_t* v, int h, int tid) {
+template <int LOGN, int R, int TLOG, int CL, class V>
+__device__ __forceinline__ void smem_store(uint64_t* sm, const V* v, int h, int tid) {
     using G = Geo<LOGN, R, TLOG, CL>;
 #pragma unroll
     for (int u = 0; u < G::SETS; u++) {
         uint64_t* b = sm + G::pbase(G::sigma(h, tid, u));
 #pragma unroll
-        for (int k = 0; k < (1 << R); k++) b[G::koff(k)] = v[u * (1 << R) + k];
+        for (int k = 0; k < (1 << R); k++) b[G::koff(k)] = vbits(v[u * (1 << R) + k]);
     }
 }
 
@@ -186,14 +201,115 @@ __device__ __forceinline__ void fwd_stage(uint64_t* x, int g, const ulonglong2* 
     if constexpr (r + 1 < R) fwd_stage<R, S0, r + 1, NC>(x, g, fw, q, q4);
 }
 
-template <int LOGN, int R, int S0, bool NC, int CL>
-__device__ __forceinline__ void fwd_compute(uint64_t* v, const ulonglong2* __restrict__ fw, uint64_t q, int h,
-                                            int tid) {
+// ---------------------------------------------------------------- FP64 mode
+// Limbs with q < 2^50 run their butterflies on the FP64 pipe, which issues
+// these products at about 2.5x the rate of the 64-bit integer Shoup product
+// (measured on register-resident radix-32 passes, 50-bit modulus).  Values
+// are integers held exactly in doubles, balanced around 0; twiddles are
+// balanced too (|w| <= q/2) and stored with wq = fl(w / q).
+//
+// fp_mulmod(y, w, wq): b = rint(fl(y * wq)), T = y*w - b*q with y*w = h + l
+// split exactly by an FMA (h = fl(y*w), l = fma(y, w, -h)).  For |y| <= 2^52
+// and q < 2^50: |fl(y*wq) - y*w/q| <= |y| * 2^-53, so |T| <= q(1/2 + |y|2^-53)
+// <= q; h - b*q is an integer below 2^53 in magnitude, hence fma(-b, q, h)
+// and the final + l are exact.  T is congruent to y*w mod q, so every
+// butterfly is exact modular arithmetic, and the canonical outputs equal the
+// integer path's bit for bit.
+//
+// Bounds (B = largest |value|, q < 2^50 so q * 2^-53 < 1/8):
+//   forward CT: B' = B + q(1/2 + B 2^-53).  From B = q/2 at the start of a
+//     pass, five stages reach 1.06q, 1.70q, 2.41q, 3.21q, 4.11q: products
+//     see |y| <= 3.21q <= 2^52, and every value stays below 2^53.
+//   inverse GS: the sums double per stage, so the sum outputs of the
+//     second and fourth stage of a pass are reduced; products then see
+//     |y| <= 3.5q.
+// Every pass ends with a reduction to |v| <= q/2 (plus a rounding sliver),
+// so each pass starts from the same bound.
+__device__ __forceinline__ double fp_mulmod(double y, double w, double wq, double q) {
+    const double h = __dmul_rn(y, w);
+    const double l = __fma_rn(y, w, -h);
+    const double b = rint(__dmul_rn(y, wq));
+    return __dadd_rn(__fma_rn(-b, q, h), l);
+}
+
+// v - q*rint(v/q): |result| <= q/2 + a sliver, exact (an integer < 2^53)
+__device__ __forceinline__ double fp_reduce(double v, double q, double qinv) {
+    return __fma_rn(-rint(__dmul_rn(v, qinv)), q, v);
+}
+
+// Per-transform FP64 constants, derived from the limb's table entry: the
+// (w, w/q) pairs at tw + 4n (forward) and tw + 6n (inverse), q, fl(1/q),
+// and the last inverse stage's N^-1 and iw[1]*N^-1, balanced, with their
+// quotients by q.
+struct FpK {
+    const double2* fw;
+    const double2* iw;
+    double q, qinv, ninv, ninvq, iw1n, iw1nq;
+};
+
+__device__ __forceinline__ double fp_bal(uint64_t x, uint64_t q) {
+    return x > q / 2 ? -__ull2double_rn(q - x) : __ull2double_rn(x);
+}
+
+template <int N>
+__device__ __forceinline__ FpK fp_consts(const LimbTab& T) {
+    FpK F;
+    F.fw = reinterpret_cast<const double2*>(T.tw + 4 * N);
+    F.iw = reinterpret_cast<const double2*>(T.tw + 6 * N);
+    F.q = __ull2double_rn(T.q);
+    F.qinv = __drcp_rn(F.q);
+    F.ninv = fp_bal(T.ninv, T.q);
+    F.ninvq = __ddiv_rn(F.ninv, F.q);
+    F.iw1n = fp_bal(T.iw1n, T.q);
+    F.iw1nq = __ddiv_rn(F.iw1n, F.q);
+    return F;
+}
+
+// u64 residue (< 2^53) -> balanced FP64 value
+__device__ __forceinline__ double fp_in(uint64_t x, const FpK& F) {
+    return fp_reduce(__ull2double_rn(x), F.q, F.qinv);
+}
+
+// balanced FP64 value (|v| < q) -> canonical u64 residue
+__device__ __forceinline__ uint64_t fp_out(double v, const FpK& F) {
+    return __double2ull_rn(v < 0.0 ? __dadd_rn(v, F.q) : v);
+}
+
+template <int R, int S0, int r>
+__device__ __forceinline__ void fwd_stage_fp(double* x, int g, const double2* __restrict__ fw, double q) {
+    constexpr int half = 1 << (R - 1 - r);
+#pragma unroll
+    for (int gi = 0; gi < (1 << r); gi++) {
+        const double2 w = __ldg(fw + (1 << (S0 + r)) + (g << r) + gi);
+#pragma unroll
+        for (int kk = 0; kk < half; kk++) {
+            const int k = gi * 2 * half + kk;
+            const double X = x[k];
+            const double Tv = fp_mulmod(x[k + half], w.x, w.y, q);
+            x[k] = __dadd_rn(X, Tv);
+            x[k + half] = __dsub_rn(X, Tv);
+        }
+    }
+    if constexpr (r + 1 < R) fwd_stage_fp<R, S0, r + 1>(x, g, fw, q);
+}
+
+// K: the LimbTab (integer modes) or the FpK (FP64 mode) of the transform.
+template <int LOGN, int R, int S0, int M, int CL, class K>
+__device__ __forceinline__ void fwd_compute(NttV<M>* v, const K& T, int h, int tid) {
     constexpr int TLOG = LOGN - S0 - R;
     using G = Geo<LOGN, R, TLOG, CL>;
+    if constexpr (M == kModeFp) {
 #pragma unroll
-    for (int u = 0; u < G::SETS; u++)
-        fwd_stage<R, S0, 0, NC>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, fw, q, 4 * q);
+        for (int u = 0; u < G::SETS; u++)
+            fwd_stage_fp<R, S0, 0>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, T.fw, T.q);
+#pragma unroll
+        for (int k = 0; k < NttCfg<LOGN, CL>::E; k++) v[k] = fp_reduce(v[k], T.q, T.qinv);
+    } else {
+        const ulonglong2* fw = reinterpret_cast<const ulonglong2*>(T.tw);
+#pragma unroll
+        for (int u = 0; u < G::SETS; u++)
+            fwd_stage<R, S0, 0, M == kModeNC>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, fw, T.q, 4 * T.q);
+    }
 }
 
 // One inverse GS stage (span 2^(TLOG+r)) on values in [0, 4q); the stage of
@@ -237,13 +353,53 @@ __device__ __forceinline__ void inv_stage(uint64_t* x, int g, const ulonglong2* 
     if constexpr (r + 1 < R) inv_stage<LOGN, R, TLOG, r + 1, NC>(x, g, iw, T, q4);
 }
 
-template <int LOGN, int R, int TLOG, bool NC, int CL>
-__device__ __forceinline__ void inv_compute(uint64_t* v, const ulonglong2* __restrict__ iw, const LimbTab& T, int h,
-                                            int tid) {
-    using G = Geo<LOGN, R, TLOG, CL>;
+// FP64 inverse stage: sums of the pass's second and fourth stage (r = 1, 3)
+// are reduced, which keeps every product input below 3.5q (bounds above).
+template <int LOGN, int R, int TLOG, int r>
+__device__ __forceinline__ void inv_stage_fp(double* x, int g, const double2* __restrict__ iw, const FpK& T) {
+    constexpr int span = 1 << r;
+    constexpr int m = 1 << (LOGN - TLOG - r - 1);
+    constexpr bool last = (TLOG + r == LOGN - 1);
+    const double q = T.q;
 #pragma unroll
-    for (int u = 0; u < G::SETS; u++)
-        inv_stage<LOGN, R, TLOG, 0, NC>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, iw, T, 4 * T.q);
+    for (int gi = 0; gi < ((1 << R) >> (r + 1)); gi++) {
+        double2 w;
+        if constexpr (last) {
+            w.x = T.iw1n;
+            w.y = T.iw1nq;
+        } else {
+            w = __ldg(iw + m + (g << (R - r - 1)) + gi);
+        }
+#pragma unroll
+        for (int kk = 0; kk < span; kk++) {
+            const int k = gi * 2 * span + kk;
+            const double X = x[k], Y = x[k + span];
+            const double s = __dadd_rn(X, Y);
+            if constexpr (last) x[k] = fp_mulmod(s, T.ninv, T.ninvq, q);
+            else if constexpr (r & 1) x[k] = fp_reduce(s, q, T.qinv);
+            else x[k] = s;
+            x[k + span] = fp_mulmod(__dsub_rn(X, Y), w.x, w.y, q);
+        }
+    }
+    if constexpr (r + 1 < R) inv_stage_fp<LOGN, R, TLOG, r + 1>(x, g, iw, T);
+}
+
+template <int LOGN, int R, int TLOG, int M, int CL, class K>
+__device__ __forceinline__ void inv_compute(NttV<M>* v, const K& T, int h, int tid) {
+    using G = Geo<LOGN, R, TLOG, CL>;
+    if constexpr (M == kModeFp) {
+#pragma unroll
+        for (int u = 0; u < G::SETS; u++)
+            inv_stage_fp<LOGN, R, TLOG, 0>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, T.iw, T);
+#pragma unroll
+        for (int k = 0; k < NttCfg<LOGN, CL>::E; k++) v[k] = fp_reduce(v[k], T.q, T.qinv);
+    } else {
+        const ulonglong2* iw = reinterpret_cast<const ulonglong2*>(T.tw) + NttCfg<LOGN, CL>::N;
+#pragma unroll
+        for (int u = 0; u < G::SETS; u++)
+            inv_stage<LOGN, R, TLOG, 0, M == kModeNC>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, iw, T,
+                                                      4 * T.q);
+    }
 }
 
 // [0, 8q) -> [0, q)
@@ -259,12 +415,26 @@ __device__ __forceinline__ uint64_t canon4(uint64_t x, uint64_t q) {
     return x >= q ? x - q : x;
 }
 
+// A loaded residue as a value of mode M, and a final value as a canonical
+// residue (forward: from shared memory, [0, 8q) for the integer modes).
+template <int M, class K>
+__device__ __forceinline__ NttV<M> ntt_in(uint64_t x, const K& T) {
+    if constexpr (M == kModeFp) return fp_in(x, T);
+    else return x;
+}
+
+// The transform's constants for mode M: the table entry itself, or FpK.
+template <int LOGN, int M>
+__device__ __forceinline__ auto ntt_consts(const LimbTab& T) {
+    if constexpr (M == kModeFp) return fp_consts<(1 << LOGN)>(T);
+    else return T;
+}
+
 // Forward pass P (stages fwd_s0(P) ..) and the ones after it.  Pass 0's
 // values are already in v; every pass stores its results back to the
 // positions it read (its own sets), so one barrier between passes suffices.
-template <int LOGN, int P, bool NC, int CL>
-__device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulonglong2* fw, uint64_t q, int h,
-                                           int tid) {
+template <int LOGN, int P, int M, int CL, class K>
+__device__ __forceinline__ void fwd_passes(uint64_t* sm, NttV<M>* v, const K& T, int h, int tid) {
     using C = NttCfg<LOGN, CL>;
     constexpr int R = C::fwd_r(P), S0 = C::fwd_s0(P), TLOG = LOGN - S0 - R;
     if constexpr (P > 0) {
@@ -272,7 +442,7 @@ __device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulon
         else __syncthreads();
         smem_load<LOGN, R, TLOG, CL>(sm, v, h, tid);
     }
-    fwd_compute<LOGN, R, S0, NC, CL>(v, fw, q, h, tid);
+    fwd_compute<LOGN, R, S0, M, CL>(v, T, h, tid);
     if constexpr (C::CL == 2 && P == 0) {
         // the first pass's sets span both halves: element sigma + k*JS goes
         // to CTA k / (E/2).  The partner must be done reading its shared
@@ -283,11 +453,11 @@ __device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulon
         uint64_t* s0 = cluster_smem(sm, 0) + pad(sg);
         uint64_t* s1 = cluster_smem(sm, 1) + pad(sg);
 #pragma unroll
-        for (int k = 0; k < C::E; k++) (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))] = v[k];
+        for (int k = 0; k < C::E; k++) (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))] = vbits(v[k]);
     } else {
         smem_store<LOGN, R, TLOG, CL>(sm, v, h, tid);
     }
-    if constexpr (P + 1 < C::NPASS) fwd_passes<LOGN, P + 1, NC, CL>(sm, v, fw, q, h, tid);
+    if constexpr (P + 1 < C::NPASS) fwd_passes<LOGN, P + 1, M, CL>(sm, v, T, h, tid);
 }
 
 // Forward transform of one poly-limb.  ld(j) returns element j (< 8q, e.g.
@@ -299,40 +469,54 @@ __device__ __forceinline__ void fwd_passes(uint64_t* sm, uint64_t* v, const ulon
 // input is staged in shared memory uses ntt_forward_from_smem instead.
 // first(k, sigma) supplies element sigma + k*JS of the first-pass set
 // (k is a compile-time constant after unrolling).
-template <int LOGN, bool NC, int CL = ntt_default_cl(LOGN), class First, class St>
+template <int LOGN, int M, int CL = ntt_default_cl(LOGN), class First, class St>
 __device__ __forceinline__ void ntt_forward_core(uint64_t* sm, const LimbTab& T, First& first, St& st) {
     using C = NttCfg<LOGN, CL>;
     static_assert(LOGN >= 10 && LOGN <= 15, "NTT supports N in [1024, 32768]");
     static_assert(C::fwd_r(0) == C::RMAX, "the first pass takes RMAX stages");
     const int tid = threadIdx.x;
     const int h = ntt_rank<LOGN, CL>();
-    const ulonglong2* fw = reinterpret_cast<const ulonglong2*>(T.tw);
-    uint64_t v[C::E];
+    const auto K = ntt_consts<LOGN, M>(T);
+    NttV<M> v[C::E];
     // first pass: one set per thread, elements sigma + k*JS
     const int sg = h * C::NT + tid;
 #pragma unroll
-    for (int k = 0; k < C::E; k++) v[k] = first(k, sg);
-    fwd_passes<LOGN, 0, NC, CL>(sm, v, fw, T.q, h, tid);
+    for (int k = 0; k < C::E; k++) v[k] = ntt_in<M>(first(k, sg), K);
+    fwd_passes<LOGN, 0, M, CL>(sm, v, K, h, tid);
     __syncthreads();
     // own share, coalesced: j = h*H + tid + k*NT
 #pragma unroll
     for (int k = 0; k < C::E; k++) {
         const int jl = tid + k * C::NT;
-        st(h * C::H + jl, NC ? mod_u64(sm[pad(jl)], T.q, T.mu64) : canon8(sm[pad(jl)], T.q));
+        uint64_t y;
+        if constexpr (M == kModeFp) y = fp_out(vfrom<double>(sm[pad(jl)]), K);
+        else if constexpr (M == kModeNC) y = mod_u64(sm[pad(jl)], T.q, T.mu64);
+        else y = canon8(sm[pad(jl)], T.q);
+        st(h * C::H + jl, y);
     }
 }
 
-template <int LOGN, bool NC, int CL = ntt_default_cl(LOGN), class Ld, class St>
-__device__ __forceinline__ void ntt_forward_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
+// Forward transform of the loader's elements: FP64 for limbs with q < 2^50,
+// integer otherwise (a uniform branch per CTA).  The correction-free integer
+// variant measured no faster here: the forward integer butterfly is bound by
+// the IMAD pipe, not by the ALU instructions NC removes.
+// FPOK = false keeps a kernel integer-only (less code and fewer registers
+// where the FP64 mode does not pay).
+template <int LOGN, int CL = ntt_default_cl(LOGN), bool FPOK = true, class Ld, class St>
+__device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
     auto first = [&](int k, int sg) { return ld(sg + k * NttCfg<LOGN, CL>::JS); };
-    ntt_forward_core<LOGN, NC, CL>(sm, T, first, st);
+    if (FPOK && T.fp)
+        ntt_forward_core<LOGN, kModeFp, CL>(sm, T, first, st);
+    else
+        ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
 }
 
-// Forward transform of a poly-limb already staged in shared memory: each
-// CTA's share at its own padded local positions, complete (__syncthreads,
-// or cluster_sync for CL = 2) before the call.  The first pass reads it with
-// the half chosen at compile time, so no per-element address selection.
-template <int LOGN, int CL = ntt_default_cl(LOGN), class St>
+// Forward transform of a poly-limb already staged in shared memory (u64
+// residues): each CTA's share at its own padded local positions, complete
+// (__syncthreads, or cluster_sync for CL = 2) before the call.  The first
+// pass reads it with the half chosen at compile time, so no per-element
+// address selection.
+template <int LOGN, int CL = ntt_default_cl(LOGN), bool FPOK = true, class St>
 __device__ __forceinline__ void ntt_forward_from_smem(uint64_t* sm, const LimbTab& T, St st) {
     using C = NttCfg<LOGN, CL>;
     if constexpr (CL == 2) {
@@ -340,27 +524,24 @@ __device__ __forceinline__ void ntt_forward_from_smem(uint64_t* sm, const LimbTa
         const uint64_t* s0 = cluster_smem(sm, 0) + pad(sg0);
         const uint64_t* s1 = cluster_smem(sm, 1) + pad(sg0);
         auto first = [&](int k, int) { return (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))]; };
-        ntt_forward_core<LOGN, false, CL>(sm, T, first, st);
+        if (FPOK && T.fp)
+            ntt_forward_core<LOGN, kModeFp, CL>(sm, T, first, st);
+        else
+            ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
     } else {
         auto first = [&](int k, int sg) { return sm[pad(sg + k * C::JS)]; };
-        ntt_forward_core<LOGN, false, CL>(sm, T, first, st);
+        if (FPOK && T.fp)
+            ntt_forward_core<LOGN, kModeFp, CL>(sm, T, first, st);
+        else
+            ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
     }
-}
-
-// Forward transform.  The correction-free variant (NC) measured no faster
-// here: the forward butterfly is bound by the IMAD pipe, not by the ALU
-// instructions NC removes, so every limb uses the corrected butterflies.
-template <int LOGN, int CL = ntt_default_cl(LOGN), class Ld, class St>
-__device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
-    ntt_forward_impl<LOGN, false, CL>(sm, T, ld, st);
 }
 
 // Inverse pass P in GS order (spans 1 .. N/2) mirrors forward pass
 // NPASS-1-P.  Its values are in shared memory on entry; the last pass keeps
 // its results (elements tid + k*NT) in v.
-template <int LOGN, int P, bool NC, int CL>
-__device__ __forceinline__ void inv_passes(uint64_t* sm, uint64_t* v, const ulonglong2* iw, const LimbTab& T, int h,
-                                           int tid) {
+template <int LOGN, int P, int M, int CL, class K>
+__device__ __forceinline__ void inv_passes(uint64_t* sm, NttV<M>* v, const K& T, int h, int tid) {
     using C = NttCfg<LOGN, CL>;
     constexpr int FP = C::NPASS - 1 - P;
     constexpr int R = C::fwd_r(FP), TLOG = LOGN - C::fwd_s0(FP) - R;
@@ -374,56 +555,64 @@ __device__ __forceinline__ void inv_passes(uint64_t* sm, uint64_t* v, const ulon
         const uint64_t* s0 = cluster_smem(sm, 0) + pad(sg);
         const uint64_t* s1 = cluster_smem(sm, 1) + pad(sg);
 #pragma unroll
-        for (int k = 0; k < C::E; k++) v[k] = (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))];
+        for (int k = 0; k < C::E; k++)
+            v[k] = vfrom<NttV<M>>((k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))]);
         cluster_sync();
     } else {
         __syncthreads();
         smem_load<LOGN, R, TLOG, CL>(sm, v, h, tid);
     }
-    inv_compute<LOGN, R, TLOG, NC, CL>(v, iw, T, h, tid);
+    inv_compute<LOGN, R, TLOG, M, CL>(v, T, h, tid);
     if constexpr (P + 1 < C::NPASS) {
         smem_store<LOGN, R, TLOG, CL>(sm, v, h, tid);
-        inv_passes<LOGN, P + 1, NC, CL>(sm, v, iw, T, h, tid);
+        inv_passes<LOGN, P + 1, M, CL>(sm, v, T, h, tid);
     }
 }
 
 // Inverse transform (including x N^-1) of one poly-limb; ld(j) returns
-// element j (< 4q) for j = rank*H + tid + k*NT, st(j, v) receives canonical
-// output j for j = sigma + k*JS, sigma = rank*NT + tid.  A caller that reuses
-// `sm` afterwards must __syncthreads() first.
-// sink(k, sigma, x) receives canonical output sigma + k*JS.
-template <int LOGN, bool NC, int CL = ntt_default_cl(LOGN), class Ld, class Sink>
+// element j (< 4q) for j = rank*H + tid + k*NT.  A caller that reuses `sm`
+// afterwards must __syncthreads() first.  sink(k, sigma, x) receives
+// canonical output sigma + k*JS, sigma = rank*NT + tid.
+template <int LOGN, int M, int CL = ntt_default_cl(LOGN), class Ld, class Sink>
 __device__ __forceinline__ void ntt_inverse_core(uint64_t* sm, const LimbTab& T, Ld& ld, Sink& sink) {
     using C = NttCfg<LOGN, CL>;
     static_assert(LOGN >= 10 && LOGN <= 15, "NTT supports N in [1024, 32768]");
     const int tid = threadIdx.x;
     const int h = ntt_rank<LOGN, CL>();
-    const ulonglong2* iw = reinterpret_cast<const ulonglong2*>(T.tw) + C::N;
-    uint64_t v[C::E];
+    const auto K = ntt_consts<LOGN, M>(T);
+    NttV<M> v[C::E];
     // own share: j = h*H + tid + k*NT
 #pragma unroll
     for (int k = 0; k < C::E; k++) {
         const int jl = tid + k * C::NT;
-        sm[pad(jl)] = ld(h * C::H + jl);
+        sm[pad(jl)] = vbits(ntt_in<M>(ld(h * C::H + jl), K));
     }
-    inv_passes<LOGN, 0, NC, CL>(sm, v, iw, T, h, tid);
+    inv_passes<LOGN, 0, M, CL>(sm, v, K, h, tid);
     // last-pass set: elements sigma + k*JS (for CL = 1, sigma = tid)
     const int sg = h * C::NT + tid;
 #pragma unroll
-    for (int k = 0; k < C::E; k++) sink(k, sg, canon4(v[k], T.q));
+    for (int k = 0; k < C::E; k++) {
+        if constexpr (M == kModeFp) sink(k, sg, fp_out(v[k], K));
+        else sink(k, sg, canon4(v[k], T.q));
+    }
 }
 
-template <int LOGN, bool NC, int CL = ntt_default_cl(LOGN), class Ld, class St>
+// Inverse transform of mode NC (integer limbs: correction-free or not), or
+// FP64 for limbs with q < 2^50 whatever NC says (a uniform branch per CTA).
+template <int LOGN, int NC, int CL = ntt_default_cl(LOGN), bool FPOK = true, class Ld, class St>
 __device__ __forceinline__ void ntt_inverse_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
     auto sink = [&](int k, int sg, uint64_t x) { st(sg + k * NttCfg<LOGN, CL>::JS, x); };
-    ntt_inverse_core<LOGN, NC, CL>(sm, T, ld, sink);
+    if (FPOK && T.fp)
+        ntt_inverse_core<LOGN, kModeFp, CL>(sm, T, ld, sink);
+    else
+        ntt_inverse_core<LOGN, NC ? kModeNC : kModeInt, CL>(sm, T, ld, sink);
 }
 
 // Inverse transform whose canonical output is parked in shared memory: each
 // CTA's share at its own padded local positions (through DSMEM for CL = 2,
 // complete on return; for CL = 1 a thread's outputs are the positions
 // pad(tid + k*NT) it alone reads afterwards).
-template <int LOGN, bool NC, int CL = ntt_default_cl(LOGN), class Ld>
+template <int LOGN, int NC, int CL = ntt_default_cl(LOGN), bool FPOK = true, class Ld>
 __device__ __forceinline__ void ntt_inverse_to_smem(uint64_t* sm, const LimbTab& T, Ld& ld) {
     using C = NttCfg<LOGN, CL>;
     if constexpr (CL == 2) {
@@ -431,22 +620,28 @@ __device__ __forceinline__ void ntt_inverse_to_smem(uint64_t* sm, const LimbTab&
         uint64_t* s0 = cluster_smem(sm, 0) + pad(sg0);
         uint64_t* s1 = cluster_smem(sm, 1) + pad(sg0);
         auto sink = [&](int k, int, uint64_t x) { (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))] = x; };
-        ntt_inverse_core<LOGN, NC, CL>(sm, T, ld, sink);
+        if (FPOK && T.fp)
+            ntt_inverse_core<LOGN, kModeFp, CL>(sm, T, ld, sink);
+        else
+            ntt_inverse_core<LOGN, NC ? kModeNC : kModeInt, CL>(sm, T, ld, sink);
         cluster_sync();
     } else {
         auto sink = [&](int k, int sg, uint64_t x) { sm[pad(sg + k * C::JS)] = x; };
-        ntt_inverse_core<LOGN, NC, CL>(sm, T, ld, sink);
+        if (FPOK && T.fp)
+            ntt_inverse_core<LOGN, kModeFp, CL>(sm, T, ld, sink);
+        else
+            ntt_inverse_core<LOGN, NC ? kModeNC : kModeInt, CL>(sm, T, ld, sink);
     }
 }
 
-// Inverse transform, with the correction-free butterflies when
-// 4q * 2^LOGN * 2 fits 64 bits (a uniform branch per CTA).
-template <int LOGN, int CL = ntt_default_cl(LOGN), class Ld, class St>
+// Inverse transform: FP64 for q < 2^50 (when FPOK); otherwise integer,
+// correction-free when 4q * 2^LOGN * 2 fits 64 bits.
+template <int LOGN, int CL = ntt_default_cl(LOGN), bool FPOK = true, class Ld, class St>
 __device__ __forceinline__ void ntt_inverse_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
-    if (T.q < (1ULL << (61 - LOGN)))
-        ntt_inverse_impl<LOGN, true, CL>(sm, T, ld, st);
+    if (!(FPOK && T.fp) && T.q < (1ULL << (61 - LOGN)))
+        ntt_inverse_impl<LOGN, true, CL, FPOK>(sm, T, ld, st);
     else
-        ntt_inverse_impl<LOGN, false, CL>(sm, T, ld, st);
+        ntt_inverse_impl<LOGN, false, CL, FPOK>(sm, T, ld, st);
 }
 
 }  // namespace tsg

@@ -187,7 +187,7 @@ struct ts_ctx {
     std::vector<uint64_t> h_fw, h_iw;  // [L][n]
     std::vector<double> h_twist_re, h_twist_im, h_tw_re, h_tw_im;
     // device
-    uint64_t* d_tw = nullptr;  // [L][4][n]
+    uint64_t* d_tw = nullptr;  // [L][8][n]: integer (w, w') pairs, then FP64 (w, w/q) pairs, forward then inverse
     LimbTab* d_tabs = nullptr;
     double* d_fft = nullptr;   // [4][n]
     unsigned long long* d_stats = nullptr;
@@ -348,7 +348,7 @@ int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bit
     c->logn = __builtin_ctz(n);
     const int logn = c->logn;
     std::vector<LimbTab> tabs(L);
-    std::vector<uint64_t> tw((size_t)L * 4 * n);
+    std::vector<uint64_t> tw((size_t)L * 8 * n);
     c->h_fw.assign((size_t)L * n, 0);
     c->h_iw.assign((size_t)L * n, 0);
     for (uint32_t l = 0; l < L; l++) {
@@ -366,13 +366,21 @@ int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bit
             delete c;
             return fail(TS_ERR_ARG, "no primitive 2N-th root for q=%llu", (unsigned long long)q);
         }
-        // device layout per limb: (fw, fw') pairs, then (iw, iw') pairs
-        uint64_t* dst = tw.data() + (size_t)l * 4 * n;
+        // device layout per limb: (fw, fw') pairs, then (iw, iw') pairs; then
+        // the FP64 mode's (w, w/q) pairs with w balanced into (-q/2, q/2]
+        uint64_t* dst = tw.data() + (size_t)l * 8 * n;
+        const double qd = (double)q;
+        auto bal = [q](uint64_t w) { return w > q / 2 ? (double)(int64_t)(w - q) : (double)w; };
+        auto put = [](uint64_t* d, double x) { memcpy(d, &x, 8); };
         for (uint32_t i = 0; i < n; i++) {
             dst[2 * i] = fw[i];
             dst[2 * i + 1] = shoup(fw[i], q);
             dst[2 * (size_t)n + 2 * i] = iw[i];
             dst[2 * (size_t)n + 2 * i + 1] = shoup(iw[i], q);
+            put(dst + 4 * (size_t)n + 2 * i, bal(fw[i]));
+            put(dst + 4 * (size_t)n + 2 * i + 1, bal(fw[i]) / qd);
+            put(dst + 6 * (size_t)n + 2 * i, bal(iw[i]));
+            put(dst + 6 * (size_t)n + 2 * i + 1, bal(iw[i]) / qd);
         }
         LimbTab& T = tabs[l];
         T.q = q;
@@ -384,6 +392,7 @@ int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bit
         T.bk = 64 - __builtin_clzll(q);
         T.bmu = (uint64_t)(((u128)1 << (2 * T.bk)) / q);
         T.thresh = (uint64_t)(((u128)1 << 64) % q);  // (u64::MAX - q + 1) % q, rng.rs:126
+        T.fp = q < (1ULL << 50) ? 1 : 0;
     }
     c->h_twist_re.assign(n, 0.0);
     c->h_twist_im.assign(n, 0.0);
@@ -430,7 +439,7 @@ int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bit
             rc = fail(TS_ERR_OOM, "table allocation failed");
             break;
         }
-        for (uint32_t l = 0; l < L; l++) tabs[l].tw = c->d_tw + (size_t)l * 4 * n;
+        for (uint32_t l = 0; l < L; l++) tabs[l].tw = c->d_tw + (size_t)l * 8 * n;
         cudaMemcpy(c->d_tw, tw.data(), tw.size() * 8, cudaMemcpyHostToDevice);
         cudaMemcpy(c->d_tabs, tabs.data(), L * sizeof(LimbTab), cudaMemcpyHostToDevice);
         cudaMemcpy(c->d_fft, c->h_twist_re.data(), n * 8, cudaMemcpyHostToDevice);
@@ -558,7 +567,7 @@ int encrypt_core(ts_ctx* c, const SlotSrc& src, size_t count, const uint64_t* d_
                 if (room >= 4) {
                     const long long limb = (long long)n * 8;
                     pl.r[pl.n++] = L2Range{c->d_fft, nullptr, 0, 0, 1, 1, 0, 4 * limb};
-                    pl.r[pl.n++] = L2Range{c->d_tw, nullptr, 0, 0, 1, 1, 0, 4 * (long long)c->L * limb};
+                    pl.r[pl.n++] = L2Range{c->d_tw, nullptr, 0, 0, 1, 1, 0, 8 * (long long)c->L * limb};
                     if (!d_skof) {  // one key for the whole batch
                         pl.r[pl.n++] = L2Range{d_sk, nullptr, 0, 0, 1, 1, 0, (long long)c->L * limb};
                         pl.r[pl.n++] = L2Range{d_sks, nullptr, 0, 0, 1, 1, 0, (long long)c->L * limb};

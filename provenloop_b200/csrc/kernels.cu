@@ -246,31 +246,35 @@ constexpr size_t ntt_smem_bytes() {
 // ======================================================================
 // Plain batched NTT / INTT (ntt.rs:79-141)
 // ======================================================================
-template <int LOGN, bool INV>
-__global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
+// MINB CTAs per SM: 2 for the CTA-pair form below N = 32768 (half a
+// poly-limb each, 64 registers per thread), so one CTA's loads and stores
+// overlap the other's butterflies.
+template <int LOGN, bool INV, int CLX = ntt_default_cl(LOGN), int MINB = 1>
+__global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
     k_ntt(uint64_t* __restrict__ data, const LimbTab* __restrict__ tabs, int lmod, int l0) {
     extern __shared__ __align__(16) uint64_t sm[];
-    const long long p = blockIdx.x / NttCfg<LOGN>::CL;
+    const long long p = blockIdx.x / CLX;
     const LimbTab T = tabs[l0 + (int)(p % lmod)];
     uint64_t* a = data + (p << LOGN);
     auto ld = [&](int j) { return a[j]; };
     auto st = [&](int j, uint64_t x) { a[j] = x; };
     if (INV)
-        ntt_inverse_block<LOGN>(sm, T, ld, st);
+        ntt_inverse_block<LOGN, CLX>(sm, T, ld, st);
     else
-        ntt_forward_block<LOGN>(sm, T, ld, st);
+        ntt_forward_block<LOGN, CLX>(sm, T, ld, st);
 }
 
 cudaError_t launch_ntt(const DevCtx& c, uint64_t* data, long long P, int lmod, int l0, bool inverse, cudaStream_t s) {
     if (P <= 0) return cudaSuccess;
     TSG_LOGN_SWITCH(c.logn, {
-        constexpr size_t smem = ntt_smem_bytes<LG>();
-        constexpr int CL = NttCfg<LG>::CL;
-        auto kern = inverse ? k_ntt<LG, true> : k_ntt<LG, false>;
+        constexpr int CL = LG >= 13 ? 2 : NttCfg<LG>::CL;
+        constexpr int MINB = (CL == 2 && LG < 15) ? 2 : 1;
+        constexpr size_t smem = (size_t)NttCfg<LG, CL>::SMEM_WORDS * 8;
+        auto kern = inverse ? k_ntt<LG, true, CL, MINB> : k_ntt<LG, false, CL, MINB>;
         cudaError_t e = ensure_smem(kern, smem);
         if (e != cudaSuccess) return e;
         KScope ks(inverse ? "ntt_inverse" : "ntt_forward", s);
-        return launch_cl(CL, kern, dim3((unsigned)(P * CL)), NttCfg<LG>::NT, smem, s, data, c.tabs, lmod, l0);
+        return launch_cl(CL, kern, dim3((unsigned)(P * CL)), NttCfg<LG, CL>::NT, smem, s, data, c.tabs, lmod, l0);
     });
     return cudaGetLastError();
 }

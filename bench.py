@@ -314,8 +314,9 @@ def run_ours(args):
     torch.cuda.synchronize(dev)
     _lib.profile_enable(False)
     kern = {}
-    for name in ("encode", "encode_a", "encode_b", "enc_a", "enc_u", "plan", "gauss_fix", "enc_a_fix", "enc_u_fix",
-                 "decrypt_limb", "decode_a", "decode_b", "dec_fused", "gather_inter", "bmat"):
+    for name in ("prefetch_l2", "gauss_gen", "encode", "encode_a", "encode_b", "enc_a", "enc_u", "enc_x",
+                 "enc_combine", "plan", "gauss_fix", "enc_a_fix", "enc_u_fix", "decrypt_limb", "crt_seg", "decode_a",
+                 "decode_b", "dec_fused", "gather_inter", "bmat", "warm_decrypt_limb", "warm_crt_seg"):
         ms, n = _lib.profile_read(name)
         if n:
             kern[name] = (ms, n)

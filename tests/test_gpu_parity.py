@@ -402,3 +402,49 @@ def test_dp_noise(T, ctx16, oracle):
     assert np.abs(out[0] - (clipped[0] + noise)).max() < 1e-9
     big = add_dp_noise(ctx16, np.zeros((1, 200000 // 100)), sigma, seeds=[1])
     assert abs(big.std() - sigma) < 0.3
+
+
+# NTT-friendly primes on either side of 2^50, the bound of the FP64 butterfly
+# mode (below: exact FP64 products; above: 64-bit integer Shoup products)
+FP_EDGE = {8192: [1125899906826241, 1125899906990081], 16384: [1125899904679937, 1125899908022273],
+           32768: [1125899904679937, 1125899908022273]}
+
+
+@pytest.mark.parametrize("n", [8192, 16384, 32768])
+def test_ntt_fp64_mode_edges_bit_exact(T, oracle, n):
+    """Both transform modes at the largest values they admit: inputs of all
+    q - 1, alternating 0 / q - 1, and uniform residues, on the primes just
+    below and just above 2^50; forward and inverse bit-exact against the
+    oracle (ntt.rs:79-141)."""
+    from provenloop_b200._lib import lib, check
+    qs = FP_EDGE[n]
+    assert qs[0] < (1 << 50) < qs[1]
+    ctx = T.CkksContext.from_moduli(n, qs)
+    rng = np.random.default_rng(50 + n)
+    polys = []
+    for kind in range(3):
+        rows = []
+        for q in qs:
+            if kind == 0:
+                rows.append(np.full(n, q - 1, np.uint64))
+            elif kind == 1:
+                rows.append(np.where(np.arange(n) % 2 == 0, 0, q - 1).astype(np.uint64))
+            else:
+                rows.append(rng.integers(0, q, size=n, dtype=np.uint64))
+        polys.append(np.stack(rows))
+    x = np.stack(polys)
+    d = _dev(x)
+    check(lib().ts_ntt_forward(ctx.handle, d.data_ptr(), 3, 2, 0))
+    ctx.synchronize()
+    fwd = _host(d).reshape(x.shape)
+    for p in range(3):
+        for l, q in enumerate(qs):
+            assert np.array_equal(fwd[p, l], oracle.ntt_forward(x[p, l], n, q)), (p, l)
+    # inverse of the extreme inputs themselves (not a round trip)
+    d2 = _dev(x)
+    check(lib().ts_ntt_inverse(ctx.handle, d2.data_ptr(), 3, 2, 0))
+    ctx.synchronize()
+    inv = _host(d2).reshape(x.shape)
+    for p in range(3):
+        for l, q in enumerate(qs):
+            assert np.array_equal(inv[p, l], oracle.ntt_inverse(x[p, l], n, q)), (p, l)

@@ -234,8 +234,8 @@ cudaError_t launch_cl(int cl, void (*kern)(KArgs...), dim3 grid, unsigned block,
 // the throughput instantiations; no for the CTA-pair variants below
 // N = 32768, which serve small batches, where the second code path's
 // instruction fetches cost more than its faster butterflies save.
-template <int LOGN, int CL>
-constexpr bool kPairFp = CL == ntt_default_cl(LOGN);
+template <int LOGN, int CL, int MINB = 1>
+constexpr bool kPairFp = CL == ntt_default_cl(LOGN) || MINB == 2;
 
 // Shared-memory bytes of one NTT CTA (its padded share of a poly-limb).
 template <int LOGN>
@@ -765,8 +765,8 @@ constexpr size_t kEncPlanWinBytes = (2 * kEncPlanRound + 16) * 4;
 // (speculative, no rejection): limb l's candidate i at words 2*l*N + 2i, low
 // word first; the Gaussian block follows at 2*L*N.  In list mode the CTAs
 // walk the flagged streams only, using their exact plans.
-template <int LOGN, int CLX = ntt_default_cl(LOGN)>
-__global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, 1)
+template <int LOGN, int CLX = ntt_default_cl(LOGN), int MINB = 1>
+__global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
     k_enc_a(uint64_t* __restrict__ ct, const uint64_t* __restrict__ seeds, const LimbTab* __restrict__ tabs, int L,
             int nvec, uint32_t* flags, const StreamPlan* __restrict__ plans, int plan_mode) {
     extern __shared__ __align__(16) uint64_t sm[];
@@ -831,13 +831,13 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, 1)
         }
         if constexpr (C::CL == 2) cluster_sync();  // the transform reads both shares
         else __syncthreads();
-        ntt_forward_from_smem<LOGN, CLX, kPairFp<LOGN, CLX>>(sm, T, [&](int j, uint64_t x) { c1[j] = x; });
+        ntt_forward_from_smem<LOGN, CLX, kPairFp<LOGN, CLX, MINB>>(sm, T, [&](int j, uint64_t x) { c1[j] = x; });
         __syncthreads();
     }
 }
 
-template <int LOGN, int CLX = ntt_default_cl(LOGN)>
-__global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, 1)
+template <int LOGN, int CLX = ntt_default_cl(LOGN), int MINB = 1>
+__global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
     k_enc_u(uint64_t* __restrict__ ct, const int64_t* __restrict__ m, const int8_t* __restrict__ e,
             const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
             const LimbTab* __restrict__ tabs, int L,
@@ -858,7 +858,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, 1)
         const int64_t* mv = m + ((size_t)v << LOGN);
         const int8_t* ev = e + ((size_t)v << LOGN);
         if (sub && threadIdx.x == 0) prefetch_l2(c1 + h0, (unsigned)C::H * 8u);  // this CTA's share, read by the epilogue
-        ntt_forward_block<LOGN, CLX, kPairFp<LOGN, CLX>>(
+        ntt_forward_block<LOGN, CLX, kPairFp<LOGN, CLX, MINB>>(
             sm, T,
             [&](int j) {
                 // |e| < q: the reference's residue of a negative e is q + e
@@ -905,6 +905,29 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
     TSG_LOGN_SWITCH(c.logn, {
         constexpr size_t smem = ntt_smem_bytes<LG>();
         constexpr int CL = NttCfg<LG>::CL;
+        // (LP: the pair form exists from N = 8192; other sizes never take it)
+        constexpr int LP = (LG == 13 || LG == 14) ? LG : 14;
+        if (LG == 13 || LG == 14) {
+            // speculative pass over every stream: CTA pairs, two CTAs per SM
+            // (as the plain NTT), so one CTA's loads overlap the other's
+            // butterflies
+            if (!plan_mode) {
+                constexpr size_t smem2 = (size_t)NttCfg<LP, 2>::SMEM_WORDS * 8;
+                cudaError_t er = ensure_smem(k_enc_a<LP, 2, 2>, smem2);
+                if (er != cudaSuccess) return er;
+                er = ensure_smem(k_enc_u<LP, 2, 2>, smem2);
+                if (er != cudaSuccess) return er;
+                {
+                    KScope ks("enc_a", s);
+                    er = launch_cl(2, k_enc_a<LP, 2, 2>, dim3(c.L * 2, nvec), NttCfg<LP, 2>::NT, smem2, s, ct, seeds,
+                                   c.tabs, c.L, nvec, flags, plans, 0);
+                    if (er != cudaSuccess) return er;
+                }
+                KScope ks("enc_u", s);
+                return launch_cl(2, k_enc_u<LP, 2, 2>, dim3(c.L * 2, nvec), NttCfg<LP, 2>::NT, smem2, s, ct, m, e, sk,
+                                 sks, sk_of, c.tabs, c.L, nvec, (const uint32_t*)flags, 0, 1);
+            }
+        }
         const size_t smem_a = plan_mode ? smem + kEncPlanWinBytes : smem;
         cudaError_t er = ensure_smem(k_enc_a<LG>, smem + kEncPlanWinBytes);
         if (er != cudaSuccess) return er;

@@ -567,7 +567,10 @@ int encrypt_core(ts_ctx* c, const SlotSrc& src, size_t count, const uint64_t* d_
                 if (room >= 4) {
                     const long long limb = (long long)n * 8;
                     pl.r[pl.n++] = L2Range{c->d_fft, nullptr, 0, 0, 1, 1, 0, 4 * limb};
-                    pl.r[pl.n++] = L2Range{c->d_tw, nullptr, 0, 0, 1, 1, 0, 8 * (long long)c->L * limb};
+                    // the small-batch kernels below N = 32768 are integer-only:
+                    // their half of each limb's tables
+                    pl.r[pl.n++] = c->logn >= 15 ? L2Range{c->d_tw, nullptr, 0, 0, 1, 1, 0, 8 * (long long)c->L * limb}
+                                                 : L2Range{c->d_tw, nullptr, 0, 0, 1, (int)c->L, 8 * limb, 4 * limb};
                     if (!d_skof) {  // one key for the whole batch
                         pl.r[pl.n++] = L2Range{d_sk, nullptr, 0, 0, 1, 1, 0, (long long)c->L * limb};
                         pl.r[pl.n++] = L2Range{d_sks, nullptr, 0, 0, 1, 1, 0, (long long)c->L * limb};

@@ -1655,6 +1655,79 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     }
 }
 
+// The same decrypt for N = 8192 and 16384 on a cluster of four CTAs per
+// (delta, batch) vector, two CTAs per SM: ranks 0-1 run the limb-0 INTT as a
+// CTA pair, ranks 2-3 the limb-1 INTT (each CTA half a poly-limb; FP64
+// butterflies for a limb below 2^50), both parked in shared memory.  Then
+// CTA (l, h) takes the l-th half of half h's positions: limb 0 from rank h,
+// limb 1 from rank 2 + h, through DSMEM, into the CRT, / Delta^2 and the
+// segment functionals; rank 0 adds the four CTAs' partials in rank order.
+// No limb-0 round trip through memory, and one CTA's loads overlap the
+// other's butterflies on each SM.
+template <int LOGN>
+__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
+    k_dec_quad(const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs, const uint64_t* __restrict__ sk,
+               const uint64_t* __restrict__ sks, const int* __restrict__ sk_of, const uint64_t* __restrict__ pt,
+               const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel, int per_ct,
+               const LimbTab* __restrict__ tabs, int L, CrtConst K, double inv_scale, const double* __restrict__ W,
+               int cols, double* __restrict__ seg_out) {
+    extern __shared__ __align__(16) uint64_t sm[];
+    using C = NttCfg<LOGN, 2>;
+    constexpr int N = C::N, NT = C::NT, H = C::H;
+    __shared__ double red[NT / 32][kMaxSegCols];
+    const int tid = threadIdx.x;
+    const int rank = cluster_rank(), limb = rank >> 1, h = rank & 1;
+    const int v = blockIdx.x >> 2;
+    const int ci = v / per_ct;
+    const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
+    const size_t key = (size_t)(sk_of ? sk_of[ci] : 0) * L;
+    {
+        const LimbTab T = tabs[limb];
+        const uint64_t* c0 = cts + (size_t)ci * ct_stride + ((size_t)limb << LOGN);
+        const uint64_t* c1 = cts + (size_t)ci * ct_stride + ((size_t)(ct_limbs + limb) << LOGN);
+        const uint64_t* s = sk + ((key + limb) << LOGN);
+        const uint64_t* sp = sks + ((key + limb) << LOGN);
+        const uint64_t* p = pt + (((size_t)pv * L + limb) << LOGN);
+        const uint64_t* pp = pts + (((size_t)pv * L + limb) << LOGN);
+        // p*(c0 + c1*s): c0 + c1*s < 5q, the product lies in [0, 4q)
+        auto ld = [&](int j) { return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q); };
+        ntt_inverse_to_smem<LOGN, false, 2>(sm, T, ld);  // ends with a cluster barrier
+    }
+    const uint64_t* m0 = cluster_smem(sm, h);
+    const uint64_t* m1 = cluster_smem(sm, 2 + h);
+    double acc[kMaxSegCols];
+#pragma unroll
+    for (int c = 0; c < kMaxSegCols; c++) acc[c] = 0.0;
+    constexpr int Q = H / 2;  // positions per CTA
+#pragma unroll 4
+    for (int jq = tid; jq < Q; jq += NT) {
+        const int jl = limb * Q + jq;
+        const int j = h * H + jl;
+        const double coeff = __dmul_rn(crt_coeff(m0[pad(jl)], m1[pad(jl)], K), inv_scale);
+#pragma unroll
+        for (int c = 0; c < kMaxSegCols; c++)
+            if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
+    }
+    const int lane = tid & 31, wid = tid >> 5;
+#pragma unroll
+    for (int c = 0; c < kMaxSegCols; c++) {
+        double a = acc[c];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) red[wid][c] = a;
+    }
+    cluster_sync();  // every CTA done reading the parked limbs; partials written
+    if (rank == 0 && tid < cols) {
+        double a = 0.0;
+        for (int r = 0; r < 4; r++) {
+            const double* rr = cooperative_groups::this_cluster().map_shared_rank(&red[0][0], r);
+            for (int w = 0; w < NT / 32; w++) a += rr[w * kMaxSegCols + tid];
+        }
+        seg_out[(size_t)v * cols + tid] = a;
+    }
+    cluster_sync();  // keep the partials alive until rank 0 has read them
+}
+
 cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_stride, int ct_limbs,
                              const uint64_t* sk, const uint64_t* sks, const int* sk_of, const uint64_t* pt,
                              const uint64_t* pts, const int* pt_sel, int per_ct,
@@ -1667,6 +1740,18 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
     // spilled 648 bytes and ran 15% slower)
     const bool nc0 = c.q0 < (1ULL << (61 - c.logn)), nc1 = c.q1 < (1ULL << (61 - c.logn));
     TSG_LOGN_SWITCH(c.logn, {
+        // N = 8192, 16384: four-CTA clusters (LQ: other sizes never take it)
+        constexpr int LQ = (LG == 13 || LG == 14) ? LG : 14;
+        if (LG == 13 || LG == 14) {
+            constexpr size_t smemq = (size_t)NttCfg<LQ, 2>::SMEM_WORDS * 8;
+            cudaError_t er = ensure_smem(k_dec_quad<LQ>, smemq);
+            if (er != cudaSuccess) return er;
+            KScope ks("dec_fused", s);
+            k_dec_quad<LQ><<<dim3((unsigned)nvec * 4), NttCfg<LQ, 2>::NT, smemq, s>>>(
+                cts, ct_stride, ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L, c.crt, inv_scale, W,
+                seg_cols, seg_out);
+            return cudaGetLastError();
+        }
         constexpr size_t smem = ntt_smem_bytes<LG>();
         constexpr int CL = NttCfg<LG>::CL;
         // one CTA per SM (the padded share fills most of shared memory); M0

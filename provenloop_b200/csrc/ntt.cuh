@@ -158,6 +158,9 @@ __device__ __forceinline__ void cluster_sync() { cooperative_groups::this_cluste
 __device__ __forceinline__ uint64_t* cluster_smem(uint64_t* sm, int rank) {
     return cooperative_groups::this_cluster().map_shared_rank(sm, rank);
 }
+// A transform pair is cluster ranks (2i, 2i + 1): a cluster may hold several
+// pairs (one per limb), which then take the same barriers in step.
+__device__ __forceinline__ int pair_base() { return cluster_rank() & ~1; }
 
 // Padded local offset of element k*JS of a cross-half set, k < E/2.  A
 // set base sigma < JS has no bits in common with k*JS (a multiple of JS), so
@@ -171,7 +174,7 @@ __host__ __device__ constexpr int xoff(int k) {
 // Rank of this CTA within its transform (0 unless CL = 2).
 template <int LOGN, int CL = ntt_default_cl(LOGN)>
 __device__ __forceinline__ int ntt_rank() {
-    if constexpr (CL == 2) return cluster_rank();
+    if constexpr (CL == 2) return cluster_rank() & 1;
     return 0;
 }
 
@@ -450,8 +453,8 @@ __device__ __forceinline__ void fwd_passes(uint64_t* sm, NttV<M>* v, const K& T,
         static_assert((1 << R) == C::E, "the cross-half pass holds a whole set per thread");
         cluster_sync();
         const int sg = Geo<LOGN, R, TLOG, CL>::sigma(h, tid, 0);
-        uint64_t* s0 = cluster_smem(sm, 0) + pad(sg);
-        uint64_t* s1 = cluster_smem(sm, 1) + pad(sg);
+        uint64_t* s0 = cluster_smem(sm, pair_base()) + pad(sg);
+        uint64_t* s1 = cluster_smem(sm, pair_base() + 1) + pad(sg);
 #pragma unroll
         for (int k = 0; k < C::E; k++) (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))] = vbits(v[k]);
     } else {
@@ -521,8 +524,8 @@ __device__ __forceinline__ void ntt_forward_from_smem(uint64_t* sm, const LimbTa
     using C = NttCfg<LOGN, CL>;
     if constexpr (CL == 2) {
         const int sg0 = ntt_rank<LOGN, CL>() * C::NT + threadIdx.x;
-        const uint64_t* s0 = cluster_smem(sm, 0) + pad(sg0);
-        const uint64_t* s1 = cluster_smem(sm, 1) + pad(sg0);
+        const uint64_t* s0 = cluster_smem(sm, pair_base()) + pad(sg0);
+        const uint64_t* s1 = cluster_smem(sm, pair_base() + 1) + pad(sg0);
         auto first = [&](int k, int) { return (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))]; };
         if (FPOK && T.fp)
             ntt_forward_core<LOGN, kModeFp, CL>(sm, T, first, st);
@@ -552,8 +555,8 @@ __device__ __forceinline__ void inv_passes(uint64_t* sm, NttV<M>* v, const K& T,
         static_assert((1 << R) == C::E, "the cross-half pass holds a whole set per thread");
         cluster_sync();
         const int sg = Geo<LOGN, R, TLOG, CL>::sigma(h, tid, 0);
-        const uint64_t* s0 = cluster_smem(sm, 0) + pad(sg);
-        const uint64_t* s1 = cluster_smem(sm, 1) + pad(sg);
+        const uint64_t* s0 = cluster_smem(sm, pair_base()) + pad(sg);
+        const uint64_t* s1 = cluster_smem(sm, pair_base() + 1) + pad(sg);
 #pragma unroll
         for (int k = 0; k < C::E; k++)
             v[k] = vfrom<NttV<M>>((k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))]);
@@ -617,8 +620,8 @@ __device__ __forceinline__ void ntt_inverse_to_smem(uint64_t* sm, const LimbTab&
     using C = NttCfg<LOGN, CL>;
     if constexpr (CL == 2) {
         const int sg0 = ntt_rank<LOGN, CL>() * C::NT + threadIdx.x;
-        uint64_t* s0 = cluster_smem(sm, 0) + pad(sg0);
-        uint64_t* s1 = cluster_smem(sm, 1) + pad(sg0);
+        uint64_t* s0 = cluster_smem(sm, pair_base()) + pad(sg0);
+        uint64_t* s1 = cluster_smem(sm, pair_base() + 1) + pad(sg0);
         auto sink = [&](int k, int, uint64_t x) { (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))] = x; };
         if (FPOK && T.fp)
             ntt_inverse_core<LOGN, kModeFp, CL>(sm, T, ld, sink);

@@ -211,13 +211,17 @@ __device__ __forceinline__ void fwd_stage(uint64_t* x, int g, const ulonglong2* 
 // are integers held exactly in doubles, balanced around 0; twiddles are
 // balanced too (|w| <= q/2) and stored with wq = fl(w / q).
 //
-// fp_mulmod(y, w, wq): b = rint(fl(y * wq)), T = y*w - b*q with y*w = h + l
-// split exactly by an FMA (h = fl(y*w), l = fma(y, w, -h)).  For |y| <= 2^52
-// and q < 2^50: |fl(y*wq) - y*w/q| <= |y| * 2^-53, so |T| <= q(1/2 + |y|2^-53)
-// <= q; h - b*q is an integer below 2^53 in magnitude, hence fma(-b, q, h)
-// and the final + l are exact.  T is congruent to y*w mod q, so every
-// butterfly is exact modular arithmetic, and the canonical outputs equal the
-// integer path's bit for bit.
+// fp_mulmod(y, w, wq): b = the integer nearest y*wq, T = y*w - b*q with
+// y*w = h + l split exactly by an FMA (h = fl(y*w), l = fma(y, w, -h)).
+// b comes from the round-to-integer constant R = 1.5 * 2^52: for |t| < 2^51,
+// fl(t + R) lies in [2^52, 2^53), where the spacing of doubles is 1, so
+// fl(fma(y, wq, R)) - R is y*wq rounded once to the nearest integer (two
+// full-rate FP64 operations; no separate round-to-integer instruction).
+// For |y| <= 2^52 and q < 2^50: |y*wq - y*w/q| <= |y| * 2^-54, so
+// |T| <= q(1/2 + |y|2^-54) <= q; h - b*q is an integer below 2^53 in
+// magnitude, hence fma(-b, q, h) and the final + l are exact.  T is
+// congruent to y*w mod q, so every butterfly is exact modular arithmetic,
+// and the canonical outputs equal the integer path's bit for bit.
 //
 // Bounds (B = largest |value|, q < 2^50 so q * 2^-53 < 1/8):
 //   forward CT: B' = B + q(1/2 + B 2^-53).  From B = q/2 at the start of a
@@ -228,16 +232,24 @@ __device__ __forceinline__ void fwd_stage(uint64_t* x, int g, const ulonglong2* 
 //     |y| <= 3.5q.
 // Every pass ends with a reduction to |v| <= q/2 (plus a rounding sliver),
 // so each pass starts from the same bound.
+constexpr double kFpRound = 6755399441055744.0;  // 1.5 * 2^52
+
+// nearest integer to x*y (ties to even) for |x*y| < 2^51, one rounding
+__device__ __forceinline__ double fp_round_mul(double x, double y) {
+    return __dsub_rn(__fma_rn(x, y, kFpRound), kFpRound);
+}
+
 __device__ __forceinline__ double fp_mulmod(double y, double w, double wq, double q) {
     const double h = __dmul_rn(y, w);
     const double l = __fma_rn(y, w, -h);
-    const double b = rint(__dmul_rn(y, wq));
+    const double b = fp_round_mul(y, wq);
     return __dadd_rn(__fma_rn(-b, q, h), l);
 }
 
-// v - q*rint(v/q): |result| <= q/2 + a sliver, exact (an integer < 2^53)
+// v - q*round(v/q): |result| <= q/2 + a sliver, exact (an integer < 2^53);
+// an NTT prime exceeds 2N >= 2^13, so |v/q| < 2^40, far inside 2^51
 __device__ __forceinline__ double fp_reduce(double v, double q, double qinv) {
-    return __fma_rn(-rint(__dmul_rn(v, qinv)), q, v);
+    return __fma_rn(-fp_round_mul(v, qinv), q, v);
 }
 
 // Per-transform FP64 constants, derived from the limb's table entry: the

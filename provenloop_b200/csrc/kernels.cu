@@ -1656,12 +1656,13 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
 }
 
 // The same decrypt for N = 8192 and 16384 on a cluster of four CTAs per
-// (delta, batch) vector, two CTAs per SM: ranks 0-1 run the limb-0 INTT as a
-// CTA pair, ranks 2-3 the limb-1 INTT (each CTA half a poly-limb; FP64
-// butterflies for a limb below 2^50), both parked in shared memory.  Then
-// CTA (l, h) takes the l-th half of half h's positions: limb 0 from rank h,
-// limb 1 from rank 2 + h, through DSMEM, into the CRT, / Delta^2 and the
-// segment functionals; rank 0 adds the four CTAs' partials in rank order.
+// (delta, batch) vector, two CTAs per SM: one pair of ranks (0-1 in even
+// clusters, 2-3 in odd ones) runs the limb-0 INTT, the other pair the limb-1
+// INTT (each CTA half a poly-limb; FP64 butterflies for a limb below 2^50),
+// both parked in shared memory.  Then CTA (l, h) takes the l-th half of half
+// h's positions, reading both limbs through DSMEM, into the CRT, / Delta^2
+// and the segment functionals; rank 0 adds the four CTAs' partials in
+// (limb, half) order.
 // No limb-0 round trip through memory, and one CTA's loads overlap the
 // other's butterflies on each SM.
 template <int LOGN>
@@ -1676,8 +1677,14 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT,
     constexpr int N = C::N, NT = C::NT, H = C::H;
     __shared__ double red[NT / 32][kMaxSegCols];
     const int tid = threadIdx.x;
-    const int rank = cluster_rank(), limb = rank >> 1, h = rank & 1;
     const int v = blockIdx.x >> 2;
+    // The scheduler puts the four CTAs of a cluster on four SMs and refills a
+    // finished cluster's slots with the next cluster in the same rank order,
+    // so with fixed roles an SM would host limb-0 CTAs (IMAD butterflies)
+    // only, or limb-1 CTAs (FP64 butterflies) only.  Odd clusters swap which
+    // pair takes limb 0, which mixes the two pipes' work on an SM.
+    const int swap = v & 1;
+    const int rank = cluster_rank(), limb = (rank >> 1) ^ swap, h = rank & 1;
     const int ci = v / per_ct;
     const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
     const size_t key = (size_t)(sk_of ? sk_of[ci] : 0) * L;
@@ -1693,8 +1700,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT,
         auto ld = [&](int j) { return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q); };
         ntt_inverse_to_smem<LOGN, false, 2>(sm, T, ld);  // ends with a cluster barrier
     }
-    const uint64_t* m0 = cluster_smem(sm, h);
-    const uint64_t* m1 = cluster_smem(sm, 2 + h);
+    const uint64_t* m0 = cluster_smem(sm, (swap << 1) + h);
+    const uint64_t* m1 = cluster_smem(sm, ((swap ^ 1) << 1) + h);
     double acc[kMaxSegCols];
 #pragma unroll
     for (int c = 0; c < kMaxSegCols; c++) acc[c] = 0.0;
@@ -1719,7 +1726,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT,
     cluster_sync();  // every CTA done reading the parked limbs; partials written
     if (rank == 0 && tid < cols) {
         double a = 0.0;
-        for (int r = 0; r < 4; r++) {
+        for (int role = 0; role < 4; role++) {  // (limb, half) order, whichever rank took it
+            const int r = ((((role >> 1) ^ swap) << 1) | (role & 1));
             const double* rr = cooperative_groups::this_cluster().map_shared_rank(&red[0][0], r);
             for (int w = 0; w < NT / 32; w++) a += rr[w * kMaxSegCols + tid];
         }

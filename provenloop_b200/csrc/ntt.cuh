@@ -63,7 +63,7 @@ struct LimbTab {
     uint64_t bmu;          // Barrett floor(2^(2k) / q)
     uint64_t thresh;       // 2^64 mod q: range_u64 rejection threshold (rng.rs:126)
     int bk;                // bitlen(q)
-    int fp;                // q < 2^50: the transforms run in FP64 (below); tables at tw + 4n
+    int fp;                // q < 2^50: the transforms run in FP64 (below); tables at tw + 4n; 2: q < 2^44, lazy
 };
 
 // Padded shared-memory index of element j.
@@ -118,9 +118,10 @@ struct Geo {
 
 // Values of a transform: u64 residues (integer modes) or FP64 integers
 // (FP64 mode); shared memory holds their 64-bit patterns either way.
-constexpr int kModeInt = 0, kModeNC = 1, kModeFp = 2;
+constexpr int kModeInt = 0, kModeNC = 1, kModeFp = 2, kModeFpLazy = 3;
+__host__ __device__ constexpr bool is_fp(int m) { return m == kModeFp || m == kModeFpLazy; }
 template <int M>
-using NttV = typename std::conditional<M == kModeFp, double, uint64_t>::type;
+using NttV = typename std::conditional<is_fp(M), double, uint64_t>::type;
 __device__ __forceinline__ uint64_t vbits(uint64_t x) { return x; }
 __device__ __forceinline__ uint64_t vbits(double x) { return (uint64_t)__double_as_longlong(x); }
 template <class V>
@@ -232,6 +233,15 @@ __device__ __forceinline__ void fwd_stage(uint64_t* x, int g, const ulonglong2* 
 //     |y| <= 3.5q.
 // Every pass ends with a reduction to |v| <= q/2 (plus a rounding sliver),
 // so each pass starts from the same bound.
+// Lazy mode (kModeFpLazy, q < 2^44): the forward transform reduces after its
+// last pass only, and the inverse only at the end of each pass.  Forward:
+// each of at most 15 stages adds at most q(1/2 + |y|2^-54) <= 0.52q, so
+// values stay below 8.5q.  Inverse: sums double within a pass of at most
+// five stages, so they stay below 16q.  Products then see |y| <= 16q, so
+// |y*wq| <= 8q < 2^51 (the rounding constant's range) and
+// |y|q2^-54 <= q2^-6; every value stays far below 2^53, and the products
+// keep |T| <= 0.52q.  Removing the reductions saves three FP64 operations
+// per element and pass (forward) or per sum of two stages (inverse).
 constexpr double kFpRound = 6755399441055744.0;  // 1.5 * 2^52
 
 // nearest integer to x*y (ties to even) for |x*y| < 2^51, one rounding
@@ -313,12 +323,15 @@ template <int LOGN, int R, int S0, int M, int CL, class K>
 __device__ __forceinline__ void fwd_compute(NttV<M>* v, const K& T, int h, int tid) {
     constexpr int TLOG = LOGN - S0 - R;
     using G = Geo<LOGN, R, TLOG, CL>;
-    if constexpr (M == kModeFp) {
+    if constexpr (is_fp(M)) {
 #pragma unroll
         for (int u = 0; u < G::SETS; u++)
             fwd_stage_fp<R, S0, 0>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, T.fw, T.q);
+        // the lazy mode reduces after the last pass only
+        if constexpr (M == kModeFp || S0 + R == LOGN) {
 #pragma unroll
-        for (int k = 0; k < NttCfg<LOGN, CL>::E; k++) v[k] = fp_reduce(v[k], T.q, T.qinv);
+            for (int k = 0; k < NttCfg<LOGN, CL>::E; k++) v[k] = fp_reduce(v[k], T.q, T.qinv);
+        }
     } else {
         const ulonglong2* fw = reinterpret_cast<const ulonglong2*>(T.tw);
 #pragma unroll
@@ -370,7 +383,7 @@ __device__ __forceinline__ void inv_stage(uint64_t* x, int g, const ulonglong2* 
 
 // FP64 inverse stage: sums of the pass's second and fourth stage (r = 1, 3)
 // are reduced, which keeps every product input below 3.5q (bounds above).
-template <int LOGN, int R, int TLOG, int r>
+template <int LOGN, int R, int TLOG, int r, bool LAZY>
 __device__ __forceinline__ void inv_stage_fp(double* x, int g, const double2* __restrict__ iw, const FpK& T) {
     constexpr int span = 1 << r;
     constexpr int m = 1 << (LOGN - TLOG - r - 1);
@@ -391,21 +404,21 @@ __device__ __forceinline__ void inv_stage_fp(double* x, int g, const double2* __
             const double X = x[k], Y = x[k + span];
             const double s = __dadd_rn(X, Y);
             if constexpr (last) x[k] = fp_mulmod(s, T.ninv, T.ninvq, q);
-            else if constexpr (r & 1) x[k] = fp_reduce(s, q, T.qinv);
+            else if constexpr ((r & 1) && !LAZY) x[k] = fp_reduce(s, q, T.qinv);
             else x[k] = s;
             x[k + span] = fp_mulmod(__dsub_rn(X, Y), w.x, w.y, q);
         }
     }
-    if constexpr (r + 1 < R) inv_stage_fp<LOGN, R, TLOG, r + 1>(x, g, iw, T);
+    if constexpr (r + 1 < R) inv_stage_fp<LOGN, R, TLOG, r + 1, LAZY>(x, g, iw, T);
 }
 
 template <int LOGN, int R, int TLOG, int M, int CL, class K>
 __device__ __forceinline__ void inv_compute(NttV<M>* v, const K& T, int h, int tid) {
     using G = Geo<LOGN, R, TLOG, CL>;
-    if constexpr (M == kModeFp) {
+    if constexpr (is_fp(M)) {
 #pragma unroll
         for (int u = 0; u < G::SETS; u++)
-            inv_stage_fp<LOGN, R, TLOG, 0>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, T.iw, T);
+            inv_stage_fp<LOGN, R, TLOG, 0, M == kModeFpLazy>(v + u * (1 << R), G::sigma(h, tid, u) >> TLOG, T.iw, T);
 #pragma unroll
         for (int k = 0; k < NttCfg<LOGN, CL>::E; k++) v[k] = fp_reduce(v[k], T.q, T.qinv);
     } else {
@@ -434,14 +447,14 @@ __device__ __forceinline__ uint64_t canon4(uint64_t x, uint64_t q) {
 // residue (forward: from shared memory, [0, 8q) for the integer modes).
 template <int M, class K>
 __device__ __forceinline__ NttV<M> ntt_in(uint64_t x, const K& T) {
-    if constexpr (M == kModeFp) return fp_in(x, T);
+    if constexpr (is_fp(M)) return fp_in(x, T);
     else return x;
 }
 
 // The transform's constants for mode M: the table entry itself, or FpK.
 template <int LOGN, int M>
 __device__ __forceinline__ auto ntt_consts(const LimbTab& T) {
-    if constexpr (M == kModeFp) return fp_consts<(1 << LOGN)>(T);
+    if constexpr (is_fp(M)) return fp_consts<(1 << LOGN)>(T);
     else return T;
 }
 
@@ -504,11 +517,21 @@ __device__ __forceinline__ void ntt_forward_core(uint64_t* sm, const LimbTab& T,
     for (int k = 0; k < C::E; k++) {
         const int jl = tid + k * C::NT;
         uint64_t y;
-        if constexpr (M == kModeFp) y = fp_out(vfrom<double>(sm[pad(jl)]), K);
+        if constexpr (is_fp(M)) y = fp_out(vfrom<double>(sm[pad(jl)]), K);
         else if constexpr (M == kModeNC) y = mod_u64(sm[pad(jl)], T.q, T.mu64);
         else y = canon8(sm[pad(jl)], T.q);
         st(h * C::H + jl, y);
     }
+}
+
+// FP64 forward transform: the lazy mode for limbs the table marks (fp == 2,
+// q < 2^44), else the reducing one (a uniform branch per CTA).
+template <int LOGN, int CL, class First, class St>
+__device__ __forceinline__ void ntt_forward_fp(uint64_t* sm, const LimbTab& T, First& first, St& st) {
+    if (T.fp == 2)
+        ntt_forward_core<LOGN, kModeFpLazy, CL>(sm, T, first, st);
+    else
+        ntt_forward_core<LOGN, kModeFp, CL>(sm, T, first, st);
 }
 
 // Forward transform of the loader's elements: FP64 for limbs with q < 2^50,
@@ -521,7 +544,7 @@ template <int LOGN, int CL = ntt_default_cl(LOGN), bool FPOK = true, class Ld, c
 __device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
     auto first = [&](int k, int sg) { return ld(sg + k * NttCfg<LOGN, CL>::JS); };
     if (FPOK && T.fp)
-        ntt_forward_core<LOGN, kModeFp, CL>(sm, T, first, st);
+        ntt_forward_fp<LOGN, CL>(sm, T, first, st);
     else
         ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
 }
@@ -540,13 +563,13 @@ __device__ __forceinline__ void ntt_forward_from_smem(uint64_t* sm, const LimbTa
         const uint64_t* s1 = cluster_smem(sm, pair_base() + 1) + pad(sg0);
         auto first = [&](int k, int) { return (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))]; };
         if (FPOK && T.fp)
-            ntt_forward_core<LOGN, kModeFp, CL>(sm, T, first, st);
+            ntt_forward_fp<LOGN, CL>(sm, T, first, st);
         else
             ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
     } else {
         auto first = [&](int k, int sg) { return sm[pad(sg + k * C::JS)]; };
         if (FPOK && T.fp)
-            ntt_forward_core<LOGN, kModeFp, CL>(sm, T, first, st);
+            ntt_forward_fp<LOGN, CL>(sm, T, first, st);
         else
             ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
     }
@@ -607,9 +630,18 @@ __device__ __forceinline__ void ntt_inverse_core(uint64_t* sm, const LimbTab& T,
     const int sg = h * C::NT + tid;
 #pragma unroll
     for (int k = 0; k < C::E; k++) {
-        if constexpr (M == kModeFp) sink(k, sg, fp_out(v[k], K));
+        if constexpr (is_fp(M)) sink(k, sg, fp_out(v[k], K));
         else sink(k, sg, canon4(v[k], T.q));
     }
+}
+
+// FP64 inverse transform, lazy or reducing as for the forward one.
+template <int LOGN, int CL, class Ld, class Sink>
+__device__ __forceinline__ void ntt_inverse_fp(uint64_t* sm, const LimbTab& T, Ld& ld, Sink& sink) {
+    if (T.fp == 2)
+        ntt_inverse_core<LOGN, kModeFpLazy, CL>(sm, T, ld, sink);
+    else
+        ntt_inverse_core<LOGN, kModeFp, CL>(sm, T, ld, sink);
 }
 
 // Inverse transform of mode NC (integer limbs: correction-free or not), or
@@ -618,7 +650,7 @@ template <int LOGN, int NC, int CL = ntt_default_cl(LOGN), bool FPOK = true, cla
 __device__ __forceinline__ void ntt_inverse_impl(uint64_t* sm, const LimbTab& T, Ld& ld, St& st) {
     auto sink = [&](int k, int sg, uint64_t x) { st(sg + k * NttCfg<LOGN, CL>::JS, x); };
     if (FPOK && T.fp)
-        ntt_inverse_core<LOGN, kModeFp, CL>(sm, T, ld, sink);
+        ntt_inverse_fp<LOGN, CL>(sm, T, ld, sink);
     else
         ntt_inverse_core<LOGN, NC ? kModeNC : kModeInt, CL>(sm, T, ld, sink);
 }
@@ -636,14 +668,14 @@ __device__ __forceinline__ void ntt_inverse_to_smem(uint64_t* sm, const LimbTab&
         uint64_t* s1 = cluster_smem(sm, pair_base() + 1) + pad(sg0);
         auto sink = [&](int k, int, uint64_t x) { (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))] = x; };
         if (FPOK && T.fp)
-            ntt_inverse_core<LOGN, kModeFp, CL>(sm, T, ld, sink);
+            ntt_inverse_fp<LOGN, CL>(sm, T, ld, sink);
         else
             ntt_inverse_core<LOGN, NC ? kModeNC : kModeInt, CL>(sm, T, ld, sink);
         cluster_sync();
     } else {
         auto sink = [&](int k, int sg, uint64_t x) { sm[pad(sg + k * C::JS)] = x; };
         if (FPOK && T.fp)
-            ntt_inverse_core<LOGN, kModeFp, CL>(sm, T, ld, sink);
+            ntt_inverse_fp<LOGN, CL>(sm, T, ld, sink);
         else
             ntt_inverse_core<LOGN, NC ? kModeNC : kModeInt, CL>(sm, T, ld, sink);
     }

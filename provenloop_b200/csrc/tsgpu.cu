@@ -392,7 +392,7 @@ int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bit
         T.bk = 64 - __builtin_clzll(q);
         T.bmu = (uint64_t)(((u128)1 << (2 * T.bk)) / q);
         T.thresh = (uint64_t)(((u128)1 << 64) % q);  // (u64::MAX - q + 1) % q, rng.rs:126
-        T.fp = q < (1ULL << 50) ? 1 : 0;
+        T.fp = q < (1ULL << 44) ? 2 : q < (1ULL << 50) ? 1 : 0;  // 2: the lazy FP64 mode
     }
     c->h_twist_re.assign(n, 0.0);
     c->h_twist_im.assign(n, 0.0);

@@ -1665,7 +1665,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
 // (limb, half) order.
 // No limb-0 round trip through memory, and one CTA's loads overlap the
 // other's butterflies on each SM.
-template <int LOGN>
+template <int LOGN, int MAXC>
 __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
     k_dec_quad(const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs, const uint64_t* __restrict__ sk,
                const uint64_t* __restrict__ sks, const int* __restrict__ sk_of, const uint64_t* __restrict__ pt,
@@ -1702,9 +1702,9 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT,
     }
     const uint64_t* m0 = cluster_smem(sm, (swap << 1) + h);
     const uint64_t* m1 = cluster_smem(sm, ((swap ^ 1) << 1) + h);
-    double acc[kMaxSegCols];
+    double acc[MAXC];  // MAXC >= cols: 5 covers N = 16384 at d >= 1366
 #pragma unroll
-    for (int c = 0; c < kMaxSegCols; c++) acc[c] = 0.0;
+    for (int c = 0; c < MAXC; c++) acc[c] = 0.0;
     constexpr int Q = H / 2;  // positions per CTA
 #pragma unroll 4
     for (int jq = tid; jq < Q; jq += NT) {
@@ -1712,12 +1712,12 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT,
         const int j = h * H + jl;
         const double coeff = __dmul_rn(crt_coeff(m0[pad(jl)], m1[pad(jl)], K), inv_scale);
 #pragma unroll
-        for (int c = 0; c < kMaxSegCols; c++)
+        for (int c = 0; c < MAXC; c++)
             if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
     }
     const int lane = tid & 31, wid = tid >> 5;
 #pragma unroll
-    for (int c = 0; c < kMaxSegCols; c++) {
+    for (int c = 0; c < MAXC; c++) {
         double a = acc[c];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
@@ -1752,10 +1752,12 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
         constexpr int LQ = (LG == 13 || LG == 14) ? LG : 14;
         if (LG == 13 || LG == 14) {
             constexpr size_t smemq = (size_t)NttCfg<LQ, 2>::SMEM_WORDS * 8;
-            cudaError_t er = ensure_smem(k_dec_quad<LQ>, smemq);
+            // accumulators for at most 5 segment columns where that suffices
+            auto kq = seg_cols <= 5 ? k_dec_quad<LQ, 5> : k_dec_quad<LQ, kMaxSegCols>;
+            cudaError_t er = ensure_smem(kq, smemq);
             if (er != cudaSuccess) return er;
             KScope ks("dec_fused", s);
-            k_dec_quad<LQ><<<dim3((unsigned)nvec * 4), NttCfg<LQ, 2>::NT, smemq, s>>>(
+            kq<<<dim3((unsigned)nvec * 4), NttCfg<LQ, 2>::NT, smemq, s>>>(
                 cts, ct_stride, ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L, c.crt, inv_scale, W,
                 seg_cols, seg_out);
             return cudaGetLastError();

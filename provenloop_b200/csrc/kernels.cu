@@ -1706,7 +1706,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT,
 #pragma unroll
     for (int c = 0; c < MAXC; c++) acc[c] = 0.0;
     constexpr int Q = H / 2;  // positions per CTA
-#pragma unroll 4
+#pragma unroll 2  // (4 spilled more at 64 registers)
     for (int jq = tid; jq < Q; jq += NT) {
         const int jl = limb * Q + jq;
         const int j = h * H + jl;

@@ -165,9 +165,12 @@ int ts_decrypt(ts_ctx* ctx, const ts_ct* ct, const ts_sk* sk, const int32_t* sk_
  * At N = 16384 that fits 4 ciphertexts after ct x pt (CRT, 2 limbs) or 5
  * fresh ones per call; larger requests fail with TS_ERR_ARG.  The work is
  * queued on the context's stream and the call returns without waiting.
- * The first call on a device resolves the array's address
- * (cudaGetSymbolAddress), so make that first call before any stream
- * capture.  Calls share the array: calls that overlap on the GPU race. */
+ * ts_ctx_create resolves the array's address on its device
+ * (cudaGetSymbolAddress), which also loads the array under CUDA's lazy
+ * module loading: create the context at start-up, before the host reserves
+ * the rest of the device.  If that early resolve failed, the first call on
+ * the device retries it, so make that first call before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race. */
 int ts_decrypt_noalloc(ts_ctx* ctx, const ts_ct* ct, const ts_sk* sk, double* out_dev);
 
 /* ct_pt_mul(ct, plaintext) -- lib.rs:178-195 / __mul__ lib.rs:336-356 /

@@ -10,7 +10,14 @@
 // fixed, file-scope device array instead of from an allocator.
 //
 // The array (kScratchBytes = 2 MiB) is part of the library image: every GPU
-// that loads libtsgpu.so holds it until the process exits.  All calls share
+// that loads this code holds it until the process exits.  Under CUDA's lazy
+// module loading (the default from CUDA 12.2) a module is loaded, and its
+// __device__ arrays allocated, on first use; ts_ctx_create therefore
+// resolves the array's address on the context's device (noalloc_prepare),
+// so the 2 MiB are taken when the context is made at start-up, not at the
+// first decrypt.  If that early resolve fails (the device was already full),
+// context creation still succeeds and the first ts_decrypt_noalloc call on
+// that device retries it.  All calls share
 // it and it keeps the last call's contents; nothing in it has to start at
 // zero, because each call writes every byte it later reads.  Calls that
 // overlap on the GPU (two streams, or two contexts on one device) race on
@@ -32,7 +39,32 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 std::mutex g_sym_mu;
 void* g_sym_addr[64] = {};  // device address of g_noalloc_scratch, per device
 
+// Device address of the array on `device`, which must be current; resolved
+// once per device and cached.
+cudaError_t scratch_address(int device, void** out) {
+    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(g_sym_mu);
+    if (!g_sym_addr[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        g_sym_addr[device] = p;
+    }
+    *out = g_sym_addr[device];
+    return cudaSuccess;
+}
+
 }  // namespace
+
+namespace tsg_host {
+// Called by context creation with `device` current: loads the array on that
+// device.  A failure is not fatal there (the error is cleared and the first
+// ts_decrypt_noalloc call on the device tries again).
+void noalloc_prepare(int device) {
+    void* p = nullptr;
+    if (scratch_address(device, &p) != cudaSuccess) cudaGetLastError();
+}
+}  // namespace tsg_host
 
 // Accessors implemented in tsgpu.cu (the opaque structs live there).
 namespace tsg_host {
@@ -55,11 +87,14 @@ extern "C" int ts_decrypt_noalloc(ts_ctx* ctx, const ts_ct* ct, const ts_sk* sk,
     std::mutex* mu = nullptr;
     const ts_ctx *ct_owner = nullptr, *sk_owner = nullptr;
     const uint64_t *d_ct = nullptr, *d_sk = nullptr, *d_sks = nullptr;
-    noalloc_ctx(ctx, &device, &dc, &stream, &n, &slots, &mu);
-    noalloc_ct(ct, &ct_owner, &count, &limbs, &scale, &d_ct);
-    noalloc_sk(sk, &sk_owner, &kcount, &d_sk, &d_sks);
+    int rc = noalloc_ctx(ctx, &device, &dc, &stream, &n, &slots, &mu);
+    if (rc == TS_OK) rc = noalloc_ct(ct, &ct_owner, &count, &limbs, &scale, &d_ct);
+    if (rc == TS_OK) rc = noalloc_sk(sk, &sk_owner, &kcount, &d_sk, &d_sks);
+    if (rc != TS_OK) return noalloc_fail(rc, "ts_decrypt_noalloc: could not read the context, ciphertext or key");
     if (ct_owner != ctx || sk_owner != ctx)
         return noalloc_fail(TS_ERR_ARG, "ts_decrypt_noalloc: objects belong to another context");
+    if (kcount < 1 || !d_sk || !d_ct || count < 1)
+        return noalloc_fail(TS_ERR_ARG, "ts_decrypt_noalloc: empty key set or ciphertext");
     if (reinterpret_cast<uintptr_t>(out_dev) % 8)
         return noalloc_fail(TS_ERR_ARG, "ts_decrypt_noalloc: out_dev must be 8-byte aligned");
     // same CRT rule as ts_decrypt (ciphertext.rs:351)
@@ -78,20 +113,12 @@ extern "C" int ts_decrypt_noalloc(ts_ctx* ctx, const ts_ct* ct, const ts_sk* sk,
     std::lock_guard<std::mutex> lk(*mu);
     cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) return noalloc_fail(TS_ERR_CUDA, cudaGetErrorString(e));
+    // the array's device address on this device (resolved by context
+    // creation; resolved here, with the device current, if that failed)
+    if (device < 0 || device >= 64) return noalloc_fail(TS_ERR_ARG, "ts_decrypt_noalloc: device id >= 64");
     void* base = nullptr;
-    {
-        // first call on a device: resolve the array's device address (with
-        // that device current); later calls reuse it
-        std::lock_guard<std::mutex> g(g_sym_mu);
-        if (device < 0 || device >= 64) return noalloc_fail(TS_ERR_ARG, "ts_decrypt_noalloc: device id >= 64");
-        if (!g_sym_addr[device]) {
-            void* p = nullptr;
-            e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-            if (e != cudaSuccess) return noalloc_fail(TS_ERR_CUDA, cudaGetErrorString(e));
-            g_sym_addr[device] = p;
-        }
-        base = g_sym_addr[device];
-    }
+    e = scratch_address(device, &base);
+    if (e != cudaSuccess) return noalloc_fail(TS_ERR_CUDA, cudaGetErrorString(e));
     uint64_t* M = static_cast<uint64_t*>(base);
     double* fft = reinterpret_cast<double*>(static_cast<char*>(base) + m_bytes);
     e = launch_decrypt_limbs(*dc, M, nl, d_ct, (long long)2 * limbs * n, (int)limbs, d_sk, d_sks, nullptr, nullptr, nullptr, 1,

@@ -169,6 +169,10 @@ static void fft_tables(uint32_t n, double* twist_re, double* twist_im, double* t
     }
 }
 
+namespace tsg_host {
+void noalloc_prepare(int device);  // noalloc.cu
+}
+
 // =====================================================================
 // objects
 // =====================================================================
@@ -449,6 +453,9 @@ int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bit
         cudaMemset(c->d_stats, 0, STAT_COUNT * sizeof(unsigned long long));
         e = cudaDeviceSynchronize();
         if (e != cudaSuccess) { rc = fail(TS_ERR_CUDA, "table upload: %s", cudaGetErrorString(e)); break; }
+        // load ts_decrypt_noalloc's fixed array on this device now (lazy
+        // module loading would otherwise allocate it at its first call)
+        tsg_host::noalloc_prepare(device);
     } while (0);
     if (rc != TS_OK) {
         ts_ctx_destroy(c);

@@ -1,9 +1,9 @@
 """Sharding of independent users across ranks (one process per GPU).
 
 Users -- each a hidden state with its own encryption stream and, optionally,
-its own secret key -- have no data dependence on each other
-(SURVEY-level fact of the reference: _he_lora_delta treats every token
-independently, inference_engine.py:1197-1405).  So ranks take disjoint
+its own secret key -- have no data dependence on each other (the reference's
+_he_lora_delta treats every token independently,
+demonstrator/server/inference_engine.py:1197-1405).  So ranks take disjoint
 blocks of users and run the whole pipeline locally; the only exchange is
 gathering the decrypted deltas to rank 0, one collective per step.
 """

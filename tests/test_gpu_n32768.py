@@ -164,3 +164,35 @@ def test_lora_delta_c4_chain(T, oracle):
         assert np.abs(inter[i] - oi).max() < 1e-8, i
     plain = (A.astype(np.float64) @ H.T).T @ B.astype(np.float64).T
     assert np.abs(delta - plain).max() < 1e-4
+
+
+def test_lora_delta_c4_full_call(T, oracle):
+    """The C4 benchmark call itself: custom(32768, [60,40,40,40,60]), 256
+    users with their own keys (seed 3 + user) x 56 rank-32 adapters = 14336
+    deltas in one ts_lora_delta_batch call (seven 2048-delta passes).  Rows
+    of the first, a middle and the last user against the oracle; every row
+    against float64 B (A h)."""
+    from provenloop_b200.backend import ZeroMoaiLora
+    users, adapters, r, d = 256, 56, 32, 1536
+    ctx = T.CkksContext.custom(N, C4_BITS)
+    o = oracle.Ctx(N, oracle.params_custom(N, C4_BITS))
+    rng = np.random.default_rng(3)
+    A = (rng.standard_normal((adapters, r, d)) * 0.02).astype(np.float32)
+    B = (rng.standard_normal((adapters, d, r)) * 0.02).astype(np.float32)
+    n = users * adapters
+    H = np.random.default_rng(3000).standard_normal((n, d))
+    adapter = np.tile(np.arange(adapters, dtype=np.int32), users)
+    user = np.repeat(np.arange(users, dtype=np.int32), adapters)
+    seeds = (np.arange(n, dtype=np.uint64) + 5_000_000).astype(np.uint64)
+    lora = ZeroMoaiLora(ctx, A, B)
+    delta, inter = lora.delta(ctx.keygen_batch([3 + u for u in range(users)]), H, seeds, expert=adapter,
+                              sk_index=user)
+    for u, a in ((0, 0), (0, 55), (127, 17), (128, 30), (255, 0), (255, 55)):
+        i = u * adapters + a
+        od, oi = o.lora_delta(o.keygen(3 + u), H[i], A[a], B[a], enc_seed=int(seeds[i]))
+        assert np.abs(delta[i] - od).max() < 1e-4, (u, a)
+        assert np.abs(inter[i] - oi).max() < 1e-8, (u, a)
+    for a in range(adapters):
+        rows = adapter == a
+        plain = (H[rows] @ A[a].astype(np.float64).T) @ B[a].astype(np.float64).T
+        assert np.abs(delta[rows] - plain).max() < 1e-4, a

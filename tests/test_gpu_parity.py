@@ -358,6 +358,55 @@ def test_lora_delta_more_vectors_than_sms(T, ctx16, octx16):
         assert np.abs(inter[i] - oi).max() < 1e-8, i
 
 
+def test_lora_delta_two_chunks_c1(T, ctx16, octx16):
+    """The benchmarked shape and beyond: C1 with 2100 hidden states in one
+    call, so the library's 2048-delta passes run twice (a full pass as the
+    bench times it, then a ragged one).  Rows from both passes, including
+    the first and last of each, against the oracle; every row against
+    float64 B (A h) (inference_engine.py:1244-1392)."""
+    from provenloop_b200.backend import ZeroMoaiLora
+    rng = np.random.default_rng(0)
+    A = (rng.standard_normal((16, 1536)) * 0.02).astype(np.float32)
+    B = (rng.standard_normal((1536, 16)) * 0.02).astype(np.float32)
+    n = 2100
+    H = np.random.default_rng(77).standard_normal((n, 1536)).astype(np.float32).astype(np.float64)
+    seeds = np.arange(90_000, 90_000 + n, dtype=np.uint64)
+    lora = ZeroMoaiLora(ctx16, A, B)
+    delta, inter = lora.delta(ctx16.keygen(0), H, seeds)
+    osk = octx16.keygen(0)
+    pc = octx16.lora_pack(A)
+    for i in (0, 1, 1023, 2046, 2047, 2048, 2049, 2099):
+        od, oi = octx16.lora_delta(osk, H[i], A, B, enc_seed=int(seeds[i]), pt_cache=pc)
+        assert np.abs(delta[i] - od).max() < 1e-4, i
+        assert np.abs(inter[i] - oi).max() < 1e-8, i
+    plain = (H @ A.astype(np.float64).T) @ B.astype(np.float64).T
+    assert np.abs(delta - plain).max() < 1e-4
+
+
+def test_lora_delta_eight_columns_fused(T, ctx16, octx16):
+    """d = 1024 at N = 16384: 8 segment columns per plaintext, which takes
+    the fused four-CTA decrypt sized for up to 10 columns (the benchmark's
+    d = 1536 uses the 5-column form), in the batched regime (80 states x 2
+    plaintext batches)."""
+    from provenloop_b200.backend import ZeroMoaiLora
+    rng = np.random.default_rng(14)
+    r, d, n = 16, 1024, 80
+    A = (rng.standard_normal((r, d)) * 0.02).astype(np.float32)
+    B = (rng.standard_normal((d, r)) * 0.02).astype(np.float32)
+    H = rng.standard_normal((n, d))
+    seeds = list(range(800, 800 + n))
+    lora = ZeroMoaiLora(ctx16, A, B)
+    assert (lora.cols, lora.batches) == (8, 2)
+    delta, inter = lora.delta(ctx16.keygen(5), H, seeds)
+    osk = octx16.keygen(5)
+    for i in (0, 1, 39, 78, 79):
+        od, oi = octx16.lora_delta(osk, H[i], A, B, enc_seed=seeds[i])
+        assert np.abs(delta[i] - od).max() < 1e-4, i
+        assert np.abs(inter[i] - oi).max() < 1e-8, i
+    plain = (H @ A.astype(np.float64).T) @ B.astype(np.float64).T
+    assert np.abs(delta - plain).max() < 1e-4
+
+
 def test_lora_delta_ragged_rank_and_small_d(T, ctx16, octx16):
     from provenloop_b200.backend import ZeroMoaiLora
     rng = np.random.default_rng(10)

@@ -18,8 +18,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libtsgpu.so")
-SOURCES = ["kernels.cu", "tsgpu.cu", "noalloc.cu"]
-HEADERS = ["common.cuh", "ntt.cuh", "fft.cuh", "kernels.cuh"]
+SOURCES = ["kernels.cu", "k_ntt.cu", "k_encode.cu", "k_encrypt.cu", "k_decrypt.cu", "tsgpu.cu", "noalloc.cu"]
+HEADERS = ["common.cuh", "ntt.cuh", "fft.cuh", "kernels.cuh", "launch.cuh"]
 
 
 def nvcc_path() -> str:
@@ -55,9 +55,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
     nvcc = nvcc_path()
     objs = []
     procs = []
-    # the sources compile in parallel (not --split-compile: its partitioning
-    # of the kernel file measured 10-20 % slower, run-to-run unstable code for
-    # the fused decrypt kernel)
+    # the sources compile in parallel, each kernel whole within its file (not
+    # --split-compile: its partitioning of a kernel file measured 10-20 %
+    # slower, run-to-run unstable code for the fused decrypt kernel)
     for s in SOURCES:
         obj = os.path.join(CSRC, s.replace(".cu", ".o"))
         cmd = [nvcc, "-c", os.path.join(CSRC, s), "-o", obj] + flags(verbose)

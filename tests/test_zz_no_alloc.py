@@ -35,12 +35,14 @@ def _device_memory_state():
 
 def _reset_pool_high_watermark():
     try:
+        from cuda.bindings import driver as dr
         from cuda.bindings import runtime as rt
     except ImportError:
         return
     err, pool = rt.cudaDeviceGetDefaultMemPool(0)
     assert err == rt.cudaError_t.cudaSuccess
-    (err,) = rt.cudaMemPoolSetAttribute(pool, rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemHigh, rt.cuuint64_t(0))
+    # the high watermark can only be reset, by writing zero
+    (err,) = rt.cudaMemPoolSetAttribute(pool, rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemHigh, dr.cuuint64_t(0))
     assert err == rt.cudaError_t.cudaSuccess
 
 

@@ -150,6 +150,25 @@ int ts_ct_import(ts_ctx* ctx, const uint64_t* c0, const uint64_t* c1, uint32_t n
 /* Ciphertext `index` of a batch as its own object (device copy). */
 int ts_ct_select(ts_ctx* ctx, const ts_ct* ct, uint32_t index, ts_ct** out);
 
+/* Wire format (tensafe-he-core serialize.rs:14-93; no PyO3 method): an
+ * RnsPoly is limb-major little-endian u64, a ciphertext [scale f64 LE | c0 |
+ * c1], a public key [b | a].
+ * ts_ct_to_bytes -- serialize.rs:71-77 ct_to_bytes, for every ciphertext of
+ * the object, blobs back to back (count * (8 + 2 * num_limbs * n * 8) bytes;
+ * TS_ERR_ARG if out_len is smaller).  *written (may be NULL) gets the size. */
+int ts_ct_to_bytes(const ts_ct* ct, uint8_t* out, size_t out_len, size_t* written);
+/* serialize.rs:80-93 ct_from_bytes(bytes, n, num_limbs): len must be a
+ * positive multiple of 8 + 2 * num_limbs * n * 8 (TS_ERR_ARG otherwise, the
+ * reference's assert_eq!); several blobs give one object of as many
+ * ciphertexts, which must share their scale.  Words above q_l are refused
+ * (TS_ERR_ARG), where the reference would accept and compute on them. */
+int ts_ct_from_bytes(ts_ctx* ctx, const uint8_t* bytes, size_t len, uint32_t num_limbs, ts_ct** out);
+/* serialize.rs:48-52 pk_to_bytes: 2 * L * n * 8 bytes. */
+int ts_pk_to_bytes(const ts_pk* pk, uint8_t* out, size_t out_len, size_t* written);
+/* serialize.rs:55-67 pk_from_bytes(bytes, n, L): len must be 2 * L * n * 8;
+ * words above q_l are refused. */
+int ts_pk_from_bytes(ts_ctx* ctx, const uint8_t* bytes, size_t len, ts_pk** out);
+
 /* decrypt(ct, sk) -- lib.rs:167-175, ciphertext.rs:327-400: writes
  * count * num_slots doubles (row i = ciphertext i).  sk_index as above. */
 int ts_decrypt(ts_ctx* ctx, const ts_ct* ct, const ts_sk* sk, const int32_t* sk_index, double* out,

@@ -91,6 +91,12 @@ def lib():
                 "or_rescale": (C.c_int, [C.c_void_p, U64P, U64P, C.c_uint32, U64P, U64P]),
                 "or_u128_to_f64": (C.c_double, [C.c_uint64, C.c_uint64]),
                 "or_find_reject_seed": (C.c_uint64, [U64P, C.c_uint32, C.c_size_t, C.c_uint64, C.c_uint64, C.c_int]),
+                "or_rns_poly_to_bytes": (None, [U64P, C.c_size_t, C.c_uint32, C.c_char_p]),
+                "or_rns_poly_from_bytes": (C.c_int, [C.c_char_p, C.c_size_t, C.c_size_t, C.c_uint32, U64P]),
+                "or_pk_to_bytes": (None, [U64P, U64P, C.c_size_t, C.c_uint32, C.c_char_p]),
+                "or_pk_from_bytes": (C.c_int, [C.c_char_p, C.c_size_t, C.c_size_t, C.c_uint32, U64P, U64P]),
+                "or_ct_to_bytes": (None, [C.c_double, U64P, U64P, C.c_size_t, C.c_uint32, C.c_char_p]),
+                "or_ct_from_bytes": (C.c_int, [C.c_char_p, C.c_size_t, C.c_size_t, C.c_uint32, F64P, U64P, U64P]),
                 "or_lora_delta": (C.c_int, [C.c_void_p, U64P, F64P, C.c_uint32, F32P, F32P, C.c_uint32,
                                             C.c_uint64, C.c_int, F64P, F64P]),
                 "or_lora_pack": (C.c_int, [C.c_void_p, F32P, C.c_uint32, C.c_uint32, U64P]),
@@ -221,6 +227,59 @@ def find_reject_seed(moduli, n, start, count, kind):
     return None if s == 0xFFFFFFFFFFFFFFFF else s
 
 
+# ---------------------------------------------------------------- wire format
+def rns_poly_to_bytes(poly) -> bytes:
+    """serialize.rs:14-23: limb-major, u64 little-endian."""
+    p = _u64(poly)
+    L, n = p.shape
+    out = C.create_string_buffer(L * n * 8)
+    lib().or_rns_poly_to_bytes(_p(p, U64P), n, L, out)
+    return out.raw
+
+
+def rns_poly_from_bytes(blob: bytes, n: int, L: int):
+    out = np.zeros((L, n), np.uint64)
+    if lib().or_rns_poly_from_bytes(blob, len(blob), n, L, _p(out, U64P)):
+        raise ValueError(f"Expected {L * n * 8} bytes for RnsPoly(n={n}, L={L}), got {len(blob)}")
+    return out
+
+
+def pk_to_bytes(b, a) -> bytes:
+    """serialize.rs:48-52: [b | a]."""
+    b, a = _u64(b), _u64(a)
+    L, n = b.shape
+    out = C.create_string_buffer(2 * L * n * 8)
+    lib().or_pk_to_bytes(_p(b, U64P), _p(a, U64P), n, L, out)
+    return out.raw
+
+
+def pk_from_bytes(blob: bytes, n: int, L: int):
+    b = np.zeros((L, n), np.uint64)
+    a = np.zeros((L, n), np.uint64)
+    if lib().or_pk_from_bytes(blob, len(blob), n, L, _p(b, U64P), _p(a, U64P)):
+        raise ValueError(f"Expected {2 * L * n * 8} bytes for PublicKey, got {len(blob)}")
+    return b, a
+
+
+def ct_to_bytes(scale: float, c0, c1) -> bytes:
+    """serialize.rs:71-77: [scale f64 LE | c0 | c1]."""
+    c0, c1 = _u64(c0), _u64(c1)
+    L, n = c0.shape
+    out = C.create_string_buffer(8 + 2 * L * n * 8)
+    lib().or_ct_to_bytes(float(scale), _p(c0, U64P), _p(c1, U64P), n, L, out)
+    return out.raw
+
+
+def ct_from_bytes(blob: bytes, n: int, L: int):
+    """serialize.rs:80-93; returns (scale, c0, c1)."""
+    c0 = np.zeros((L, n), np.uint64)
+    c1 = np.zeros((L, n), np.uint64)
+    sc = C.c_double()
+    if lib().or_ct_from_bytes(blob, len(blob), n, L, C.byref(sc), _p(c0, U64P), _p(c1, U64P)):
+        raise ValueError(f"Expected {8 + 2 * L * n * 8} bytes for Ciphertext, got {len(blob)}")
+    return sc.value, c0, c1
+
+
 def u128_to_f64(v: int) -> float:
     return float(lib().or_u128_to_f64((v >> 64) & 0xFFFFFFFFFFFFFFFF, v & 0xFFFFFFFFFFFFFFFF))
 
@@ -294,14 +353,14 @@ class Ctx:
         return re, im
 
     # keys / ciphertexts (polys returned as [L, n] uint64)
-    def keygen(self, seed: int):
-        r = Rng(seed)
+    def keygen(self, seed: int = None, rng: Rng = None):
+        r = rng if rng is not None else Rng(seed)
         sk = np.zeros(self.L * self.n, np.uint64)
         lib().or_keygen(self._h, r.ref, _p(sk, U64P))
         return sk.reshape(self.L, self.n)
 
-    def keygen_public(self, sk, seed: int):
-        r = Rng(seed)
+    def keygen_public(self, sk, seed: int = None, rng: Rng = None):
+        r = rng if rng is not None else Rng(seed)
         sk = _u64(sk)
         b = np.zeros(self.L * self.n, np.uint64)
         a = np.zeros(self.L * self.n, np.uint64)

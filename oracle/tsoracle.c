@@ -973,6 +973,70 @@ int or_rescale(const or_ctx *c, const uint64_t *c0, const uint64_t *c1,
 }
 
 /* ======================================================================== */
+/* Wire format: serialize.rs:14-93                                           */
+/* ======================================================================== */
+
+/* u64::to_le_bytes / from_le_bytes, independent of the host's byte order. */
+static void le_put(uint8_t *o, uint64_t x) {
+    for (int b = 0; b < 8; b++) o[b] = (uint8_t)(x >> (8 * b));
+}
+
+static uint64_t le_get(const uint8_t *o) {
+    uint64_t x = 0;
+    for (int b = 0; b < 8; b++) x |= (uint64_t)o[b] << (8 * b);
+    return x;
+}
+
+/* serialize.rs:14-23 */
+void or_rns_poly_to_bytes(const uint64_t *poly, size_t n, uint32_t L, uint8_t *out) {
+    for (uint32_t l = 0; l < L; l++)
+        for (size_t i = 0; i < n; i++) le_put(out + ((size_t)l * n + i) * 8, poly[(size_t)l * n + i]);
+}
+
+/* serialize.rs:26-44 */
+int or_rns_poly_from_bytes(const uint8_t *bytes, size_t len, size_t n, uint32_t L, uint64_t *poly) {
+    if (len != (size_t)L * n * 8) return -1;
+    size_t off = 0;
+    for (uint32_t l = 0; l < L; l++)
+        for (size_t i = 0; i < n; i++, off += 8) poly[(size_t)l * n + i] = le_get(bytes + off);
+    return 0;
+}
+
+/* serialize.rs:48-52 */
+void or_pk_to_bytes(const uint64_t *b, const uint64_t *a, size_t n, uint32_t L, uint8_t *out) {
+    or_rns_poly_to_bytes(b, n, L, out);
+    or_rns_poly_to_bytes(a, n, L, out + (size_t)L * n * 8);
+}
+
+/* serialize.rs:55-67 */
+int or_pk_from_bytes(const uint8_t *bytes, size_t len, size_t n, uint32_t L, uint64_t *b, uint64_t *a) {
+    const size_t poly = (size_t)L * n * 8;
+    if (len != 2 * poly) return -1;
+    if (or_rns_poly_from_bytes(bytes, poly, n, L, b)) return -1;
+    return or_rns_poly_from_bytes(bytes + poly, poly, n, L, a);
+}
+
+/* serialize.rs:71-77 */
+void or_ct_to_bytes(double scale, const uint64_t *c0, const uint64_t *c1, size_t n, uint32_t L, uint8_t *out) {
+    uint64_t sb;
+    memcpy(&sb, &scale, 8); /* f64::to_le_bytes: the IEEE bits, little-endian */
+    le_put(out, sb);
+    or_rns_poly_to_bytes(c0, n, L, out + 8);
+    or_rns_poly_to_bytes(c1, n, L, out + 8 + (size_t)L * n * 8);
+}
+
+/* serialize.rs:80-93 */
+int or_ct_from_bytes(const uint8_t *bytes, size_t len, size_t n, uint32_t L, double *scale, uint64_t *c0,
+                     uint64_t *c1) {
+    const size_t poly = (size_t)L * n * 8;
+    if (len != 8 + 2 * poly) return -1;
+    const uint64_t sb = le_get(bytes);
+    memcpy(scale, &sb, 8);
+    if (or_rns_poly_from_bytes(bytes + 8, poly, n, L, c0)) return -1;
+    return or_rns_poly_from_bytes(bytes + 8 + poly, poly, n, L, c1);
+}
+
+/* ======================================================================== */
 /* ZeRo-MOAI delta: inference_engine.py:1244-1392                           */
 /* ======================================================================== */
 

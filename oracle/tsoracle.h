@@ -151,6 +151,19 @@ void or_ct_sub(const or_ctx *c, const uint64_t *a0, const uint64_t *a1,
 int or_rescale(const or_ctx *c, const uint64_t *c0, const uint64_t *c1,
                uint32_t num_limbs, uint64_t *o0, uint64_t *o1);
 
+/* ---- wire format (serialize.rs:14-93) ----------------------------------- */
+/* RnsPoly: limb-major, every u64 little-endian (L*n*8 bytes). */
+void or_rns_poly_to_bytes(const uint64_t *poly, size_t n, uint32_t L, uint8_t *out);
+/* -1 unless len == L*n*8 (the reference's assert_eq!). */
+int or_rns_poly_from_bytes(const uint8_t *bytes, size_t len, size_t n, uint32_t L, uint64_t *poly);
+/* PublicKey: [b | a] (2*L*n*8 bytes). */
+void or_pk_to_bytes(const uint64_t *b, const uint64_t *a, size_t n, uint32_t L, uint8_t *out);
+int or_pk_from_bytes(const uint8_t *bytes, size_t len, size_t n, uint32_t L, uint64_t *b, uint64_t *a);
+/* Ciphertext: [scale f64 LE | c0 | c1] (8 + 2*L*n*8 bytes). */
+void or_ct_to_bytes(double scale, const uint64_t *c0, const uint64_t *c1, size_t n, uint32_t L, uint8_t *out);
+int or_ct_from_bytes(const uint8_t *bytes, size_t len, size_t n, uint32_t L, double *scale, uint64_t *c0,
+                     uint64_t *c1);
+
 /* u128 -> f64, round-to-nearest-even (Rust `as f64`). */
 double or_u128_to_f64(uint64_t hi, uint64_t lo);
 

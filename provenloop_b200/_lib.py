@@ -72,6 +72,10 @@ SIGNATURES = {
     "ts_ct_export": (cint, [vp, u32, P(u64), P(u64)]),
     "ts_ct_import": (cint, [vp, P(u64), P(u64), u32, f64, pvp]),
     "ts_ct_select": (cint, [vp, vp, u32, pvp]),
+    "ts_ct_to_bytes": (cint, [vp, C.c_char_p, sz, P(sz)]),
+    "ts_ct_from_bytes": (cint, [vp, C.c_char_p, sz, u32, pvp]),
+    "ts_pk_to_bytes": (cint, [vp, C.c_char_p, sz, P(sz)]),
+    "ts_pk_from_bytes": (cint, [vp, C.c_char_p, sz, pvp]),
     "ts_decrypt": (cint, [vp, vp, vp, P(i32), vp, cint]),
     "ts_decrypt_noalloc": (cint, [vp, vp, vp, vp]),
     "ts_ct_pt_mul": (cint, [vp, vp, P(f64), sz, pvp]),

@@ -168,6 +168,29 @@ __device__ __forceinline__ int gaussian_round(uint64_t u1w, uint64_t u2w, double
     return (int)round(v);
 }
 
+// The encryption's error sample round(3.19 * z) (sampling.rs:10, :51-58;
+// rng.rs:152-157) with the transcendental work in float32 first.  CUDA's
+// logf (at most 1 ulp), cosf (at most 2 ulp) and sqrtf (correctly rounded),
+// with the rounding of u1, u2, 2*pi and 3.19 to float and of the products,
+// put the float value v within 4.4e-5 of the exact 3.19 * z whenever
+// |3.19 * z| >= 0.4, and below 0.402 in magnitude otherwise.  So when |v|
+// lies more than kGaussGuard (5.7x that bound) from a half-integer, round(v)
+// is the rounding of the reference's f64 value; the rest (about one sample
+// in 2000) take the f64 evaluation, gaussian_round, with its near-tie count.
+constexpr float kGaussGuard = 2.5e-4f;
+
+__device__ __forceinline__ int gaussian_round_e(uint64_t u1w, uint64_t u2w, bool* near_tie) {
+    const float u1 = __double2float_rn(u64_to_unit(u1w));
+    const float u2 = __double2float_rn(u64_to_unit(u2w));
+    const float v = __fmul_rn(__fmul_rn(sqrtf(__fmul_rn(-2.0f, logf(u1))), cosf(__fmul_rn(6.2831855f, u2))), 3.19f);
+    const float a = fabsf(v);
+    if (fabsf(a - floorf(a) - 0.5f) > kGaussGuard) {
+        *near_tie = false;
+        return (int)roundf(v);
+    }
+    return gaussian_round(u1w, u2w, 3.19, near_tie);
+}
+
 // ----------------------------------------------------------------- L2 prefetch
 // Asks the TMA unit to pull [p, p + bytes) into L2 (p 16-byte aligned, bytes
 // a multiple of 16); a hint that neither blocks nor touches shared memory.

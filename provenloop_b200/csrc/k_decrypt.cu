@@ -102,6 +102,40 @@ __device__ __forceinline__ double crt_coeff(uint64_t m0, uint64_t m1, const CrtC
     return neg ? -mag : mag;
 }
 
+// The same CRT for the segment functionals, on the FP64 pipe (K.q1d != 0,
+// i.e. q1 < 2^50).  k = (m1 - m0) q0^-1 mod q1 is formed exactly (fp_mulmod
+// is an exact modular product below 2^50), and so is the centring decision:
+// Q = q0 q1 is odd, so mu = m0 + k q0 > Q/2 exactly when k > (q1 - 1)/2, or
+// k = (q1 - 1)/2 and m0 > q0/2.  The centred value m0 + k' q0 (k' = k, or
+// k - q1) is then formed with three roundings, within 2^9 + ulp/2 of the
+// exact value, where crt_coeff rounds the 128-bit value once: the
+// functionals sum thousands of terms of magnitude ~2^80 in f64 anyway (an
+// absolute error of 2^-71 per term after / Delta^2).
+__device__ __forceinline__ double crt_coeff_fp(uint64_t m0, uint64_t m1, const CrtConst& K) {
+    // exact u64 -> double for values below 2^52: the bits of 2^52 + x, minus 2^52
+    const double R52 = 4503599627370496.0;
+    const double h = __dsub_rn(__longlong_as_double((long long)(0x4330000000000000ULL | (m0 >> 30))), R52);
+    const double l = __dsub_rn(__longlong_as_double((long long)(0x4330000000000000ULL | (m0 & 0x3fffffffULL))), R52);
+    const double m1d = __dsub_rn(__longlong_as_double((long long)(0x4330000000000000ULL | m1)), R52);
+    // m0 = h 2^30 + l = h (2^30 mod q1) + l (mod q1); |t| <= q1
+    const double t = fp_mulmod(h, K.r30, K.r30q, K.q1d);
+    const double x = __dsub_rn(__dsub_rn(m1d, t), l);  // = m1 - m0 (mod q1); |x| < 2 q1 + 2^30, exact
+    double k = fp_mulmod(x, K.q0invd, K.q0invq, K.q1d);  // |k| <= q1
+    k = k < 0.0 ? __dadd_rn(k, K.q1d) : k;
+    k = k >= K.q1d ? __dsub_rn(k, K.q1d) : k;  // [0, q1)
+    const bool neg = k > K.t_half || (k == K.t_half && m0 > K.q0_half);
+    const double kc = neg ? __dsub_rn(k, K.q1d) : k;
+    // m0 + kc (q0_hi + q0_lo): |kc q0_lo| < 2^48, m0 rounded once to 53 bits
+    return __fma_rn(kc, K.q0_hi, __fma_rn(kc, K.q0_lo, __fma_rn(h, 1073741824.0, l)));
+}
+
+// The coefficient for the functionals: the FP64 form where the moduli allow.
+template <bool FPC>
+__device__ __forceinline__ double crt_seg_coeff(uint64_t m0, uint64_t m1, const CrtConst& K) {
+    if constexpr (FPC) return crt_coeff_fp(m0, m1, K);
+    else return crt_coeff(m0, m1, K);
+}
+
 template <int LOGN>
 __global__ void __launch_bounds__(1024, 1)
     k_decode_a(const uint64_t* __restrict__ M, int nl, int crt, double scale, CrtConst K, uint64_t q0, FftTab T,
@@ -295,7 +329,9 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
                 for (int kk = 0; kk < G; kk++) {
                     const int jl = tid + (k0 + kk) * NT;
                     const int j = h * C::H + jl;
-                    const double coeff = __dmul_rn(crt_coeff(m0r[kk], sm[pad(jl)], K), inv_scale);
+                    const double coeff = __dmul_rn(K.q1d != 0.0 ? crt_coeff_fp(m0r[kk], sm[pad(jl)], K)
+                                                                  : crt_coeff(m0r[kk], sm[pad(jl)], K),
+                                                   inv_scale);
 #pragma unroll
                     for (int c = 0; c < kMaxSegCols; c++)
                         if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
@@ -347,7 +383,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
 // (limb, half) order.
 // No limb-0 round trip through memory, and one CTA's loads overlap the
 // other's butterflies on each SM.
-template <int LOGN, int MAXC>
+template <int LOGN, int MAXC, bool FPC>
 __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
     k_dec_quad(const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs, const uint64_t* __restrict__ sk,
                const uint64_t* __restrict__ sks, const int* __restrict__ sk_of, const uint64_t* __restrict__ pt,
@@ -392,7 +428,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT,
     for (int jq = tid; jq < Q; jq += NT) {
         const int jl = limb * Q + jq;
         const int j = h * H + jl;
-        const double coeff = __dmul_rn(crt_coeff(m0[pad(jl)], m1[pad(jl)], K), inv_scale);
+        const double coeff = __dmul_rn(crt_seg_coeff<FPC>(m0[pad(jl)], m1[pad(jl)], K), inv_scale);
 #pragma unroll
         for (int c = 0; c < MAXC; c++)
             if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
@@ -435,7 +471,9 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
         if (LG == 13 || LG == 14) {
             constexpr size_t smemq = (size_t)NttCfg<LQ, 2>::SMEM_WORDS * 8;
             // accumulators for at most 5 segment columns where that suffices
-            auto kq = seg_cols <= 5 ? k_dec_quad<LQ, 5> : k_dec_quad<LQ, kMaxSegCols>;
+            const bool fpc = c.crt.q1d != 0.0;
+            auto kq = seg_cols <= 5 ? (fpc ? k_dec_quad<LQ, 5, true> : k_dec_quad<LQ, 5, false>)
+                                    : (fpc ? k_dec_quad<LQ, kMaxSegCols, true> : k_dec_quad<LQ, kMaxSegCols, false>);
             cudaError_t er = ensure_smem(kq, smemq);
             if (er != cudaSuccess) return er;
             KScope ks("dec_fused", s);
@@ -469,6 +507,7 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
 // 8x the SMs instead of running one block per vector.
 constexpr int kCrtCl = 8;
 
+template <bool FPC>
 __global__ void __launch_bounds__(256)
     k_crt_seg(const uint64_t* __restrict__ M, int logn, CrtConst K, double inv_scale, const double* __restrict__ W,
               int cols, double* __restrict__ seg_out) {
@@ -481,7 +520,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int c = 0; c < kMaxSegCols; c++) acc[c] = 0.0;
     for (int j = j0 + tid; j < j0 + slice; j += blockDim.x) {
-        const double coeff = __dmul_rn(crt_coeff(m0[j], m1[j], K), inv_scale);
+        const double coeff = __dmul_rn(crt_seg_coeff<FPC>(m0[j], m1[j], K), inv_scale);
 #pragma unroll
         for (int c = 0; c < kMaxSegCols; c++)
             if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * n + j), acc[c]);
@@ -517,8 +556,8 @@ cudaError_t launch_crt_seg(const DevCtx& c, const uint64_t* M, int nvec, double 
     if (nvec <= 0) return cudaSuccess;
     if (seg_cols < 1 || seg_cols > kMaxSegCols || c.L < 2 || (c.n % kCrtCl) != 0) return cudaErrorInvalidValue;
     KScope ks(scope, s);
-    return launch_cl(kCrtCl, k_crt_seg, dim3((unsigned)(nvec * kCrtCl)), 256, 0, s, M, c.logn, c.crt, inv_scale, W,
-                     seg_cols, seg_out);
+    return launch_cl(kCrtCl, c.crt.q1d != 0.0 ? k_crt_seg<true> : k_crt_seg<false>, dim3((unsigned)(nvec * kCrtCl)),
+                     256, 0, s, M, c.logn, c.crt, inv_scale, W, seg_cols, seg_out);
 }
 
 

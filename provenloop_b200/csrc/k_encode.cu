@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(1024, 1)
                     bool tie;
                     const uint64_t u1 = (uint64_t)w[4 * cc] | ((uint64_t)w[4 * cc + 1] << 32);
                     const uint64_t u2 = (uint64_t)w[4 * cc + 2] | ((uint64_t)w[4 * cc + 3] << 32);
-                    e[(size_t)v * N + j] = (int8_t)gaussian_round(u1, u2, 3.19, &tie);
+                    e[(size_t)v * N + j] = (int8_t)gaussian_round_e(u1, u2, &tie);
                     ties += tie ? 1 : 0;
                 }
             }
@@ -229,17 +229,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(enc1::NT, 1)
             chacha_block(seed, (uint32_t)((gauss_off >> 4) + (uint64_t)b), w);
             char4 o;
             bool tie;
-            o.x = (signed char)gaussian_round((uint64_t)w[0] | ((uint64_t)w[1] << 32),
-                                              (uint64_t)w[2] | ((uint64_t)w[3] << 32), 3.19, &tie);
+            o.x = (signed char)gaussian_round_e((uint64_t)w[0] | ((uint64_t)w[1] << 32),
+                                              (uint64_t)w[2] | ((uint64_t)w[3] << 32), &tie);
             ties += tie;
-            o.y = (signed char)gaussian_round((uint64_t)w[4] | ((uint64_t)w[5] << 32),
-                                              (uint64_t)w[6] | ((uint64_t)w[7] << 32), 3.19, &tie);
+            o.y = (signed char)gaussian_round_e((uint64_t)w[4] | ((uint64_t)w[5] << 32),
+                                              (uint64_t)w[6] | ((uint64_t)w[7] << 32), &tie);
             ties += tie;
-            o.z = (signed char)gaussian_round((uint64_t)w[8] | ((uint64_t)w[9] << 32),
-                                              (uint64_t)w[10] | ((uint64_t)w[11] << 32), 3.19, &tie);
+            o.z = (signed char)gaussian_round_e((uint64_t)w[8] | ((uint64_t)w[9] << 32),
+                                              (uint64_t)w[10] | ((uint64_t)w[11] << 32), &tie);
             ties += tie;
-            o.w = (signed char)gaussian_round((uint64_t)w[12] | ((uint64_t)w[13] << 32),
-                                              (uint64_t)w[14] | ((uint64_t)w[15] << 32), 3.19, &tie);
+            o.w = (signed char)gaussian_round_e((uint64_t)w[12] | ((uint64_t)w[13] << 32),
+                                              (uint64_t)w[14] | ((uint64_t)w[15] << 32), &tie);
             ties += tie;
             reinterpret_cast<char4*>(e + (size_t)v * N)[b] = o;
         }

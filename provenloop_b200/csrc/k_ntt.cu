@@ -170,17 +170,17 @@ __global__ void k_gauss_gen(int8_t* __restrict__ e, const uint64_t* __restrict__
         chacha_block(seeds[v], (uint32_t)((off >> 4) + (uint64_t)b), w);
         char4 o;
         bool tie;
-        o.x = (signed char)gaussian_round((uint64_t)w[0] | ((uint64_t)w[1] << 32),
-                                          (uint64_t)w[2] | ((uint64_t)w[3] << 32), 3.19, &tie);
+        o.x = (signed char)gaussian_round_e((uint64_t)w[0] | ((uint64_t)w[1] << 32),
+                                          (uint64_t)w[2] | ((uint64_t)w[3] << 32), &tie);
         ties += tie;
-        o.y = (signed char)gaussian_round((uint64_t)w[4] | ((uint64_t)w[5] << 32),
-                                          (uint64_t)w[6] | ((uint64_t)w[7] << 32), 3.19, &tie);
+        o.y = (signed char)gaussian_round_e((uint64_t)w[4] | ((uint64_t)w[5] << 32),
+                                          (uint64_t)w[6] | ((uint64_t)w[7] << 32), &tie);
         ties += tie;
-        o.z = (signed char)gaussian_round((uint64_t)w[8] | ((uint64_t)w[9] << 32),
-                                          (uint64_t)w[10] | ((uint64_t)w[11] << 32), 3.19, &tie);
+        o.z = (signed char)gaussian_round_e((uint64_t)w[8] | ((uint64_t)w[9] << 32),
+                                          (uint64_t)w[10] | ((uint64_t)w[11] << 32), &tie);
         ties += tie;
-        o.w = (signed char)gaussian_round((uint64_t)w[12] | ((uint64_t)w[13] << 32),
-                                          (uint64_t)w[14] | ((uint64_t)w[15] << 32), 3.19, &tie);
+        o.w = (signed char)gaussian_round_e((uint64_t)w[12] | ((uint64_t)w[13] << 32),
+                                          (uint64_t)w[14] | ((uint64_t)w[15] << 32), &tie);
         ties += tie;
         reinterpret_cast<char4*>(e + (size_t)v * N)[b] = o;
     }

@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(512)
                 const uint64_t u1 = (uint64_t)win[o] | ((uint64_t)win[o + 1] << 32);
                 const uint64_t u2 = (uint64_t)win[o + 2] | ((uint64_t)win[o + 3] << 32);
                 bool tie;
-                e[(size_t)v * N + j0 + jj] = (int8_t)gaussian_round(u1, u2, 3.19, &tie);
+                e[(size_t)v * N + j0 + jj] = (int8_t)gaussian_round_e(u1, u2, &tie);
                 ties += tie;
             }
         }

@@ -47,6 +47,11 @@ struct CrtConst {
     int pad;
     uint64_t Q_lo, Q_hi;  // q0*q1
     uint64_t H_lo, H_hi;  // (q0*q1)/2
+    // FP64 form of the same CRT for the segment functionals (crt_coeff_fp):
+    // q1, (2^30 mod q1) and (q0^-1 mod q1) balanced with their quotients by
+    // q1, (q1 - 1)/2, q0 = q0_hi + q0_lo (q0_hi = fl(q0)), floor(q0 / 2)
+    double q1d, r30, r30q, q0invd, q0invq, t_half, q0_hi, q0_lo;
+    uint64_t q0_half;
 };
 
 struct DevCtx {

@@ -420,6 +420,18 @@ int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bit
         K.Q_hi = (uint64_t)(Q >> 64);
         K.H_lo = (uint64_t)H;
         K.H_hi = (uint64_t)(H >> 64);
+        if (q1 < (1ULL << 50)) {  // the FP64 form needs exact products mod q1
+            auto bal = [q1](uint64_t w) { return w > q1 / 2 ? -(double)(q1 - w) : (double)w; };
+            K.q1d = (double)q1;
+            K.r30 = bal((1ULL << 30) % q1);
+            K.r30q = K.r30 / K.q1d;
+            K.q0invd = bal(K.q0inv);
+            K.q0invq = K.q0invd / K.q1d;
+            K.t_half = (double)((q1 - 1) / 2);
+            K.q0_hi = (double)q0;
+            K.q0_lo = (double)(int64_t)(q0 - (uint64_t)K.q0_hi);  // |q0 - fl(q0)| <= 2^7
+            K.q0_half = q0 / 2;
+        }
     } else {
         K.q0 = c->q[0];
     }
@@ -1061,6 +1073,133 @@ int ts_ct_select(ts_ctx* c, const ts_ct* ct, uint32_t index, ts_ct** out) {
     const size_t words = (size_t)2 * ct->limbs * c->n;
     CU(cudaMemcpyAsync(o->d, ct->d + index * words, words * 8, cudaMemcpyDeviceToDevice, c->stream));
     *out = ctx_adopt(o);
+    return TS_OK;
+}
+
+// ------------------------------------------------------------------ wire format
+// serialize.rs:14-93: an RnsPoly is limb-major little-endian u64; a
+// ciphertext is [scale f64 LE | c0 | c1], a public key [b | a].  The device
+// layout of a ciphertext object, [count][2][limbs][n], is already the wire
+// layout of c0 | c1 (and a key's [2][L][n] that of b | a), so each direction
+// is one copy; a batch of ciphertexts is their blobs back to back (one
+// strided copy).
+static_assert(__BYTE_ORDER__ == __ORDER_LITTLE_ENDIAN__, "the wire format and the device are little-endian");
+
+// Every u64 of `polys` polynomials of `limbs` limbs at p (unaligned bytes)
+// must be at most q_l: canonical residues, or q itself, which the
+// reference's encode can emit (its negative branch when q divides a
+// coefficient).  Larger words would break the kernels' lazy-reduction
+// bounds, so they are refused instead of being reduced silently.
+static int check_wire_residues(const ts_ctx* c, const uint8_t* p, size_t polys, uint32_t limbs, const char* what) {
+    for (size_t k = 0; k < polys; k++)
+        for (uint32_t l = 0; l < limbs; l++) {
+            const uint64_t q = c->q[l];
+            const uint8_t* w = p + ((k * limbs + l) * (size_t)c->n) * 8;
+            for (uint32_t i = 0; i < c->n; i++) {
+                uint64_t x;
+                memcpy(&x, w + (size_t)i * 8, 8);
+                if (x > q)
+                    return fail(TS_ERR_ARG, "%s: word %u of limb %u is %llu, not a residue mod %llu", what, i, l,
+                                (unsigned long long)x, (unsigned long long)q);
+            }
+        }
+    return TS_OK;
+}
+
+int ts_ct_to_bytes(const ts_ct* ct, uint8_t* out, size_t out_len, size_t* written) {
+    if (!ct || !out) return fail(TS_ERR_ARG, "bad ct_to_bytes arguments");
+    ts_ctx* c = ct->ctx;
+    const size_t body = (size_t)2 * ct->limbs * c->n * 8, blob = 8 + body, total = blob * ct->count;
+    if (out_len < total) return fail(TS_ERR_ARG, "ct_to_bytes: %zu bytes needed, the buffer holds %zu", total, out_len);
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    for (uint32_t i = 0; i < ct->count; i++) memcpy(out + (size_t)i * blob, &ct->scale, 8);
+    if (ct->count == 1)
+        CU(cudaMemcpyAsync(out + 8, ct->d, body, cudaMemcpyDeviceToHost, c->stream));
+    else
+        CU(cudaMemcpy2DAsync(out + 8, blob, ct->d, body, body, ct->count, cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    if (written) *written = total;
+    return TS_OK;
+}
+
+int ts_ct_from_bytes(ts_ctx* c, const uint8_t* bytes, size_t len, uint32_t num_limbs, ts_ct** out) {
+    if (!c || !bytes || !out) return fail(TS_ERR_ARG, "bad ct_from_bytes arguments");
+    if (num_limbs == 0 || num_limbs > c->L)
+        return fail(TS_ERR_ARG, "ct_from_bytes: num_limbs %u out of range [1, %u]", num_limbs, c->L);
+    const size_t body = (size_t)2 * num_limbs * c->n * 8, blob = 8 + body;
+    if (len == 0 || len % blob != 0)
+        return fail(TS_ERR_ARG, "Expected a multiple of %zu bytes for Ciphertext(n=%u, L=%u), got %zu", blob, c->n,
+                    num_limbs, len);
+    const size_t count = len / blob;
+    if (count > UINT32_MAX) return fail(TS_ERR_ARG, "ct_from_bytes: too many ciphertexts");
+    double scale = 0.0;
+    memcpy(&scale, bytes, 8);
+    for (size_t i = 0; i < count; i++) {
+        if (memcmp(bytes + i * blob, bytes, 8) != 0)
+            return fail(TS_ERR_ARG, "ct_from_bytes: ciphertext %zu has another scale than ciphertext 0", i);
+        int rc = check_wire_residues(c, bytes + i * blob + 8, 2, num_limbs, "ct_from_bytes");
+        if (rc) return rc;
+    }
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    ts_ct* ct = nullptr;
+    rc = new_ct(c, (uint32_t)count, num_limbs, scale, &ct);
+    if (rc) return rc;
+    cudaError_t e = count == 1 ? cudaMemcpyAsync(ct->d, bytes + 8, body, cudaMemcpyHostToDevice, c->stream)
+                               : cudaMemcpy2DAsync(ct->d, body, bytes + 8, blob, body, count, cudaMemcpyHostToDevice,
+                                                   c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) {
+        cudaFreeAsync(ct->d, c->stream);
+        delete ct;
+        return fail(TS_ERR_CUDA, "ct_from_bytes: %s", cudaGetErrorString(e));
+    }
+    *out = ctx_adopt(ct);
+    return TS_OK;
+}
+
+int ts_pk_to_bytes(const ts_pk* pk, uint8_t* out, size_t out_len, size_t* written) {
+    if (!pk || !out) return fail(TS_ERR_ARG, "bad pk_to_bytes arguments");
+    ts_ctx* c = pk->ctx;
+    const size_t total = (size_t)2 * c->L * c->n * 8;
+    if (out_len < total) return fail(TS_ERR_ARG, "pk_to_bytes: %zu bytes needed, the buffer holds %zu", total, out_len);
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    CU(cudaMemcpyAsync(out, pk->d, total, cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    if (written) *written = total;
+    return TS_OK;
+}
+
+int ts_pk_from_bytes(ts_ctx* c, const uint8_t* bytes, size_t len, ts_pk** out) {
+    if (!c || !bytes || !out) return fail(TS_ERR_ARG, "bad pk_from_bytes arguments");
+    const size_t words = (size_t)c->L * c->n;
+    if (len != 2 * words * 8) return fail(TS_ERR_ARG, "Expected %zu bytes for PublicKey, got %zu", 2 * words * 8, len);
+    int rc = check_wire_residues(c, bytes, 2, c->L, "pk_from_bytes");
+    if (rc) return rc;
+    Lock lk(c);
+    rc = set_device(c);
+    if (rc) return rc;
+    ts_pk* pk = new ts_pk{c, nullptr};
+    rc = dev_alloc(c, (void**)&pk->d, 4 * words * 8);
+    if (rc) {
+        delete pk;
+        return rc;
+    }
+    cudaError_t e = cudaMemcpyAsync(pk->d, bytes, 2 * words * 8, cudaMemcpyHostToDevice, c->stream);
+    // Shoup companions of b and a, as keygen_public makes them
+    if (e == cudaSuccess) e = launch_shoup_companion(c->dc, pk->d + 2 * words, pk->d, 2LL * c->L, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) {
+        cudaFreeAsync(pk->d, c->stream);
+        delete pk;
+        return fail(TS_ERR_CUDA, "pk_from_bytes: %s", cudaGetErrorString(e));
+    }
+    *out = ctx_adopt(pk);
     return TS_OK;
 }
 

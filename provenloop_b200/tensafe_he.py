@@ -112,6 +112,13 @@ class TenSafePublicKey:
         check(lib().ts_pk_export(self.handle, ptr(b, C.c_uint64), ptr(a, C.c_uint64)), "ts_pk_export")
         return b.reshape(self._ctx._L, self._ctx._n), a.reshape(self._ctx._L, self._ctx._n)
 
+    def to_bytes(self) -> bytes:
+        """serialize.rs:48-52 pk_to_bytes: [b | a], limb-major u64 LE."""
+        size = 2 * self._ctx._L * self._ctx._n * 8
+        buf = C.create_string_buffer(size)
+        check(lib().ts_pk_to_bytes(self.handle, buf, size, None), "ts_pk_to_bytes")
+        return buf.raw
+
 
 class TenSafeCiphertext:
     """CKKS ciphertext with operator overloading (lib.rs:309-395)."""
@@ -157,9 +164,15 @@ class TenSafeCiphertext:
         return c0.reshape(nl, n), c1.reshape(nl, n)
 
     def to_bytes(self) -> bytes:
-        """serialize.rs:71-77 layout: [scale f64 LE | c0 | c1], u64 LE."""
-        c0, c1 = self.export()
-        return struct.pack("<d", self.scale) + c0.astype("<u8").tobytes() + c1.astype("<u8").tobytes()
+        """serialize.rs:71-77 ct_to_bytes: [scale f64 LE | c0 | c1], limb-major
+        u64 LE (ts_ct_to_bytes).  A batch gives its ciphertexts' blobs back to
+        back."""
+        count, nl, _ = self._info()
+        size = count * (8 + 2 * nl * self._ctx._n * 8)
+        buf = C.create_string_buffer(size)
+        written = C.c_size_t()
+        check(lib().ts_ct_to_bytes(self.handle, buf, size, C.byref(written)), "ts_ct_to_bytes")
+        return buf.raw[: written.value]
 
 
 class CkksContext:
@@ -369,16 +382,27 @@ class CkksContext:
                                  C.byref(h)), "ts_ct_import")
         return TenSafeCiphertext(self, h)
 
-    def ciphertext_from_bytes(self, blob: bytes) -> TenSafeCiphertext:
-        """serialize.rs:80-93 (length checked like the reference's assert)."""
-        words = len(blob) - 8
-        per = self._n * 8
-        if words < 0 or words % (2 * per) != 0:
-            raise ValueError(f"Expected 8 + 2*L*{per} bytes for Ciphertext, got {len(blob)}")
-        nl = words // (2 * per)
-        scale = struct.unpack("<d", blob[:8])[0]
-        body = np.frombuffer(blob[8:], dtype="<u8").reshape(2, nl, self._n)
-        return self.import_ciphertext(body[0], body[1], scale)
+    def ciphertext_from_bytes(self, blob: bytes, num_limbs: int = None) -> TenSafeCiphertext:
+        """serialize.rs:80-93 ct_from_bytes (ts_ct_from_bytes); the length is
+        checked like the reference's assert_eq!.  num_limbs defaults to what
+        the length of one blob implies (the reference passes it explicitly)."""
+        blob = bytes(blob)
+        if num_limbs is None:
+            words = len(blob) - 8
+            per = 2 * self._n * 8
+            if words <= 0 or words % per != 0:
+                raise ValueError(f"Expected 8 + 2*L*{self._n * 8} bytes for Ciphertext, got {len(blob)}")
+            num_limbs = words // per
+        h = C.c_void_p()
+        check(lib().ts_ct_from_bytes(self.handle, blob, len(blob), int(num_limbs), C.byref(h)), "ts_ct_from_bytes")
+        return TenSafeCiphertext(self, h)
+
+    def public_key_from_bytes(self, blob: bytes) -> "TenSafePublicKey":
+        """serialize.rs:55-67 pk_from_bytes (ts_pk_from_bytes)."""
+        blob = bytes(blob)
+        h = C.c_void_p()
+        check(lib().ts_pk_from_bytes(self.handle, blob, len(blob), C.byref(h)), "ts_pk_from_bytes")
+        return TenSafePublicKey(self, h)
 
     # -------------------------------------------------------------- info
     @staticmethod

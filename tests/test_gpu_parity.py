@@ -290,17 +290,82 @@ def test_ct_add_sub_and_scale_mismatch(T, ctx16, octx16):
         (ca * b) + cb
 
 
-def test_serialize_roundtrip(T, ctx16):
-    sk = ctx16.keygen(42)
+def test_serialize_bytes_match_oracle(T, ctx16, octx16, oracle):
+    """serialize.rs:71-93 through the C ABI: the bytes of a GPU ciphertext
+    equal the oracle's ct_to_bytes of the same (bit-exact) ciphertext, for a
+    fresh one, a batch (blobs back to back), a ct x pt product (scale 2^80)
+    and a rescaled one (3 limbs); bytes from the oracle load back and
+    decrypt (the reference's KAT tolerance, serialize.rs:139-144)."""
+    sk, osk = ctx16.keygen(42), octx16.keygen(42)
     z = np.arange(10, dtype=np.float64)
     ct = ctx16.encrypt(z, sk, seed=42)
+    o0, o1, osc = octx16.encrypt(z, osk, seed=42)
+    want = oracle.ct_to_bytes(osc, o0, o1)
     blob = ct.to_bytes()
-    assert len(blob) == 8 + 2 * 4 * 16384 * 8
-    ct2 = ctx16.ciphertext_from_bytes(blob)
-    assert ct2.to_bytes() == blob
+    assert len(blob) == 8 + 2 * 4 * 16384 * 8 and blob == want
+    ct2 = ctx16.ciphertext_from_bytes(want)
+    assert ct2.to_bytes() == want
     assert np.abs(ctx16.decrypt(ct2, sk)[:10] - z).max() < 1e-4
+    # a batch: each ciphertext's blob, back to back
+    X = np.random.default_rng(31).standard_normal((3, 700))
+    cts = ctx16.encrypt_batch(X, sk, seeds=[5, 6, 7])
+    want3 = b""
+    for i in range(3):
+        e0, e1, esc = octx16.encrypt(X[i], osk, seed=5 + i)
+        want3 += oracle.ct_to_bytes(esc, e0, e1)
+    assert cts.to_bytes() == want3
+    back = ctx16.ciphertext_from_bytes(want3)
+    assert back._info()[0] == 3 and back.to_bytes() == want3
+    # ct x pt (scale Delta^2) and its rescale (3 limbs)
+    pt = np.random.default_rng(32).standard_normal(8192)
+    prod = ct * pt
+    p0, p1 = octx16.ct_pt_mul(o0, o1, pt)
+    assert prod.to_bytes() == oracle.ct_to_bytes(prod.scale, p0, p1)
+    r = ctx16.rescale(prod)
+    r0, r1 = octx16.rescale(p0, p1)
+    rb = r.to_bytes()
+    assert rb == oracle.ct_to_bytes(r.scale, r0, r1) and len(rb) == 8 + 2 * 3 * 16384 * 8
+    assert ctx16.ciphertext_from_bytes(rb, num_limbs=3).to_bytes() == rb
+    # the reference's length assert, a word above q, mixed scales
     with pytest.raises(ValueError):
-        ctx16.ciphertext_from_bytes(blob[:-8])
+        ctx16.ciphertext_from_bytes(want[:-8])
+    with pytest.raises(ValueError):
+        ctx16.ciphertext_from_bytes(want, num_limbs=3)
+    bad = bytearray(want)
+    bad[8:16] = (ctx16.moduli[0] + 1).to_bytes(8, "little")
+    with pytest.raises(ValueError, match="residue"):
+        ctx16.ciphertext_from_bytes(bytes(bad))
+    ok_q = bytearray(want)
+    ok_q[8:16] = ctx16.moduli[0].to_bytes(8, "little")       # q itself: a word the reference's encode can emit
+    ctx16.ciphertext_from_bytes(bytes(ok_q))
+    mixed = want + bytes(prod.to_bytes()[:8]) + want[8:]
+    with pytest.raises(ValueError, match="scale"):
+        ctx16.ciphertext_from_bytes(mixed)
+
+
+def test_pk_serialize_matches_oracle(T, ctx16, octx16, oracle):
+    """serialize.rs:48-67 through the C ABI: pk bytes equal the oracle's
+    pk_to_bytes of the same key; a key loaded from the oracle's bytes
+    encrypts bit-identically to the original (Shoup companions rebuilt)."""
+    sk, osk = ctx16.keygen(42), octx16.keygen(42)
+    pk = ctx16.keygen_public(sk, seed=43)
+    ob, oa = octx16.keygen_public(osk, 43)
+    want = oracle.pk_to_bytes(ob, oa)
+    assert pk.to_bytes() == want
+    pk2 = ctx16.public_key_from_bytes(want)
+    assert pk2.to_bytes() == want
+    z = np.random.default_rng(33).standard_normal(3000)
+    a = ctx16.encrypt_pk(z, pk, seed=44).to_bytes()
+    b = ctx16.encrypt_pk(z, pk2, seed=44).to_bytes()
+    assert a == b
+    o0, o1, osc = octx16.encrypt_pk(z, ob, oa, 44)
+    assert a == oracle.ct_to_bytes(osc, o0, o1)
+    with pytest.raises(ValueError):
+        ctx16.public_key_from_bytes(want[:-1])
+    bad = bytearray(want)
+    bad[-8:] = (2 ** 64 - 1).to_bytes(8, "little")
+    with pytest.raises(ValueError, match="residue"):
+        ctx16.public_key_from_bytes(bytes(bad))
 
 
 # ------------------------------------------------------------------ ZeRo-MOAI delta

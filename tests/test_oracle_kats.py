@@ -351,6 +351,56 @@ def test_serialize_roundtrip(ctx8k):
     assert np.abs(ctx.decrypt(body[0], body[1], sc2, sk)[:10] - z).max() < 1e-4
 
 
+def test_serialize_layout_golden(oracle):
+    """serialize.rs:8-93 by hand on a tiny case (N = 4, L = 2): limb-major
+    little-endian u64 words; a ciphertext is [scale f64 LE | c0 | c1], a
+    public key [b | a]."""
+    poly = np.array([[1, 2, 0x0102030405060708, 2 ** 64 - 1], [7, 0, 2 ** 63, 0x00ff]], np.uint64)
+    want = bytes.fromhex(
+        "0100000000000000" "0200000000000000" "0807060504030201" "ffffffffffffffff"
+        "0700000000000000" "0000000000000000" "0000000000000080" "ff00000000000000")
+    assert oracle.rns_poly_to_bytes(poly) == want
+    assert np.array_equal(oracle.rns_poly_from_bytes(want, 4, 2), poly)
+    other = poly[::-1].copy()
+    assert oracle.pk_to_bytes(poly, other) == want + oracle.rns_poly_to_bytes(other)
+    ct = oracle.ct_to_bytes(2.0 ** 80, poly, other)
+    assert ct[:8] == bytes.fromhex("000000000000f044")      # 2^80 as f64, little-endian
+    assert ct[8:] == want + oracle.rns_poly_to_bytes(other)
+    sc, c0, c1 = oracle.ct_from_bytes(ct, 4, 2)
+    assert sc == 2.0 ** 80 and np.array_equal(c0, poly) and np.array_equal(c1, other)
+    b, a = oracle.pk_from_bytes(want + want, 4, 2)
+    assert np.array_equal(b, poly) and np.array_equal(a, poly)
+    with pytest.raises(ValueError):                           # the reference's assert_eq! on the length
+        oracle.ct_from_bytes(ct[:-1], 4, 2)
+    with pytest.raises(ValueError):
+        oracle.pk_from_bytes(want, 4, 2)
+    with pytest.raises(ValueError):
+        oracle.rns_poly_from_bytes(want + b"\0", 4, 2)
+
+
+def test_serialize_reference_kats(oracle):
+    """serialize.rs:102-145: keys and the ciphertext drawn from ONE stream
+    (TenSafeRng::from_seed(42): keygen, then keygen_public / encrypt of
+    0..9); bytes round-trip exactly and the deserialized ciphertext decrypts
+    within 1e-4."""
+    ctx = oracle.Ctx(8192)
+    r = oracle.Rng(42)
+    sk = ctx.keygen(rng=r)
+    b, a = ctx.keygen_public(sk, rng=r)
+    blob = oracle.pk_to_bytes(b, a)
+    assert len(blob) == 2 * ctx.L * ctx.n * 8
+    b2, a2 = oracle.pk_from_bytes(blob, ctx.n, ctx.L)
+    assert np.array_equal(b, b2) and np.array_equal(a, a2)
+    r = oracle.Rng(42)
+    sk = ctx.keygen(rng=r)
+    z = np.arange(10, dtype=np.float64)
+    c0, c1, sc = ctx.encrypt(z, sk, rng=r)
+    blob = oracle.ct_to_bytes(sc, c0, c1)
+    sc2, d0, d1 = oracle.ct_from_bytes(blob, ctx.n, ctx.L)
+    assert sc2 == sc and np.array_equal(d0, c0) and np.array_equal(d1, c1)
+    assert np.abs(ctx.decrypt(d0, d1, sc2, sk)[:10] - z).max() < 1e-4
+
+
 def test_keygen_ternary_mapping(oracle):
     # ciphertext.rs:77-103: draw r -> sample_ternary(q=3) -> {0:2,1:0,2:1}
     # -> limb match {0:q-1,1:0,2:1}; so r=0 -> +1, r=1 -> -1, r=2 -> 0.

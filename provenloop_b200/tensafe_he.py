@@ -388,11 +388,12 @@ class CkksContext:
         the length of one blob implies (the reference passes it explicitly)."""
         blob = bytes(blob)
         if num_limbs is None:
-            words = len(blob) - 8
-            per = 2 * self._n * 8
-            if words <= 0 or words % per != 0:
+            # the largest limb count whose blob size divides the length (one
+            # blob, or several back to back)
+            fits = [nl for nl in range(self._L, 0, -1) if len(blob) % (8 + 2 * nl * self._n * 8) == 0]
+            if not blob or not fits:
                 raise ValueError(f"Expected 8 + 2*L*{self._n * 8} bytes for Ciphertext, got {len(blob)}")
-            num_limbs = words // per
+            num_limbs = fits[0]
         h = C.c_void_p()
         check(lib().ts_ct_from_bytes(self.handle, blob, len(blob), int(num_limbs), C.byref(h)), "ts_ct_from_bytes")
         return TenSafeCiphertext(self, h)

@@ -333,7 +333,6 @@ def run_reference(args):
 # 8 bytes per poly-limb):
 #   enc_a         per (ct, limb):        write c1 (8N)
 #   enc_u         per (ct, limb):        read m (8N) + e (N) + s (8N) + c1 (8N), write c0 (8N) = 33N
-#   enc_fused     per (ct, limb):        read m (8N) + e (N) + s (8N), write c1 (8N) + c0 (8N) = 33N
 #   decrypt_limb  per (ct, batch, limb): read c0, c1 (16N) + s (8N) + NTT(pt) (8N), write M (8N) = 40N
 #   decode_a      per (ct, batch):       read M (2 x 8N), write 16N = 32N
 #   decode_b      per (ct, batch):       read 16N
@@ -350,7 +349,6 @@ def kernel_bytes_per_delta(name: str, L: int = 4, nb: int = 4) -> float:
     table = {
         "enc_a": 8 * n * L,
         "enc_u": 33 * n * L,
-        "enc_fused": 33 * n * L,
         "decrypt_limb": 40 * n * nb * 2,
         "decode_a": 32 * n * nb,
         "decode_b": 16 * n * nb,
@@ -362,7 +360,7 @@ def kernel_bytes_per_delta(name: str, L: int = 4, nb: int = 4) -> float:
     return float(table.get(name, 0))
 
 
-KERNEL_NAMES = ("prefetch_l2", "gauss_gen", "encode", "encode_a", "encode_b", "enc_a", "enc_u", "enc_x", "enc_fused",
+KERNEL_NAMES = ("prefetch_l2", "gauss_gen", "encode", "encode_a", "encode_b", "enc_a", "enc_u", "enc_x",
                 "enc_combine", "plan", "gauss_fix", "enc_a_fix", "enc_u_fix", "decrypt_limb", "crt_seg", "decode_a",
                 "decode_b", "dec_fused", "gather_inter", "bmat", "warm_decrypt_limb", "warm_crt_seg")
 

@@ -225,6 +225,14 @@ int ts_hadamard(ts_ctx* ctx, uint64_t* out_dev, const uint64_t* a_dev, const uin
 int ts_lora_load(ts_ctx* ctx, const float* lora_a, const float* lora_b, uint32_t experts, uint32_t r, uint32_t d,
                  ts_lora** out);
 int ts_lora_destroy(ts_lora* lora);
+/* Hot swap of expert `expert` -- swap_adapter, inference_engine.py:879-959
+ * (the NTT(plaintext) cache rebuild of :1037-1074): lora_a [r][d] and
+ * lora_b [d][r] f32 (host; the adapter's r and d) replace the expert's
+ * packed plaintexts and B in place, so pointers a captured CUDA graph holds
+ * stay valid.  Ordered on the context's stream and complete on return: work
+ * queued on that stream before the call uses the old adapter, work after it
+ * the new one.  Do not swap while another stream's work reads the adapter. */
+int ts_lora_set_expert(ts_ctx* ctx, ts_lora* lora, uint32_t expert, const float* lora_a, const float* lora_b);
 int ts_lora_info(const ts_lora* lora, uint32_t* experts, uint32_t* r, uint32_t* d, uint32_t* cols,
                  uint32_t* batches);
 /* Encrypted LoRA deltas for n hidden states h [n][d] (f64): per state,

@@ -90,6 +90,7 @@ SIGNATURES = {
     "ts_hadamard": (cint, [vp, vp, vp, vp, sz, u32, cint]),
     "ts_lora_load": (cint, [vp, P(C.c_float), P(C.c_float), u32, u32, u32, pvp]),
     "ts_lora_destroy": (cint, [vp]),
+    "ts_lora_set_expert": (cint, [vp, vp, u32, P(C.c_float), P(C.c_float)]),
     "ts_lora_info": (cint, [vp, P(u32), P(u32), P(u32), P(u32), P(u32)]),
     "ts_lora_delta_batch": (cint, [vp, vp, vp, vp, u32, P(i32), P(i32), P(u64), vp, vp, cint]),
     "ts_dp_noise": (cint, [vp, vp, u32, u32, f64, f64, P(u64), cint]),

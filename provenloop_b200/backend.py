@@ -113,6 +113,18 @@ class ZeroMoaiLora:
     def handle(self):
         return self._hd._h
 
+    def set_expert(self, expert: int, lora_a, lora_b):
+        """Hot-swap one expert's adapter in place (swap_adapter,
+        inference_engine.py:879-959): A [r, d], B [d, r] with this object's r
+        and d.  Device pointers stay the same, so a captured decode-step graph
+        uses the new adapter on its next replay."""
+        A = np.ascontiguousarray(np.asarray(lora_a, dtype=np.float32))
+        B = np.ascontiguousarray(np.asarray(lora_b, dtype=np.float32))
+        if A.shape != (self.r, self.d) or B.shape != (self.d, self.r):
+            raise ValueError(f"expected A {(self.r, self.d)} and B {(self.d, self.r)}, got {A.shape} and {B.shape}")
+        check(lib().ts_lora_set_expert(self._ctx.handle, self.handle, int(expert), ptr(A, C.c_float),
+                                       ptr(B, C.c_float)), "ts_lora_set_expert")
+
     def delta(self, sk, h, seeds, expert=None, sk_index=None, out=None, out_inter=None, want_inter=True):
         """Encrypted deltas for hidden states h [n, d] (host arrays).
 

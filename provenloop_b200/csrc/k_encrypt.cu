@@ -136,72 +136,6 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
     }
 }
 
-// Both transforms of one (ciphertext, limb) on a cluster of four CTAs, two
-// per SM (N = 8192, 16384; the speculative pass over every stream): one CTA
-// pair draws a and transforms it, c1 = NTT(a), the other transforms m + e,
-// and the two run in step through the same barriers.  The second pair then
-// forms c0 = NTT(m + e) - c1*s with c1 read from the first pair's shared
-// memory, so c1 is written once and never read back.  Odd clusters swap the
-// pairs' roles: the four CTAs of a cluster land on four SMs, so an SM then
-// hosts both kinds of CTA (the a pair's ChaCha20 on the ALU pipe beside the
-// other pair's loads).
-template <int LOGN>
-__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
-    k_enc_quad(uint64_t* __restrict__ ct, const int64_t* __restrict__ m, const int8_t* __restrict__ e,
-               const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
-               const uint64_t* __restrict__ seeds, const LimbTab* __restrict__ tabs, int L, int nvec,
-               uint32_t* flags) {
-    extern __shared__ __align__(16) uint64_t sm[];
-    using C = NttCfg<LOGN, 2>;
-    constexpr int N = C::N, NT = C::NT, H = C::H;
-    const int limb = blockIdx.x >> 2, v = blockIdx.y, tid = threadIdx.x;
-    const int rank = cluster_rank(), role = (rank >> 1) ^ ((limb + v) & 1);
-    const int h0 = (rank & 1) * H;  // first element of this CTA's share
-    const LimbTab T = tabs[limb];
-    uint64_t* c0 = ct + (((size_t)v * 2 * L + limb) << LOGN);
-    uint64_t* c1 = ct + (((size_t)v * 2 * L + L + limb) << LOGN);
-    if (role == 0) {
-        // a = range_u64(q) draws (sampling.rs:62-64), limb l's candidate i at
-        // words 2lN + 2i; this CTA's share, 8 candidates per ChaCha block
-        const uint64_t seed = seeds[v];
-        const uint32_t blk0 = (uint32_t)limb * (N / 8);
-        bool rej = false;
-        for (int b = h0 / 8 + tid; b < (h0 + H) / 8; b += NT) {
-            uint32_t w[16];
-            chacha_block(seed, blk0 + (uint32_t)b, w);
-#pragma unroll
-            for (int c = 0; c < 8; c++) {
-                const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
-                rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
-                sm[pad(8 * b + c - h0)] = mod_u64(u, T.q, T.mu64);
-            }
-        }
-        if (rej) flag_stream(flags, nvec, v);
-    }
-    cluster_sync();  // the a pair's shares are staged (the other pair takes the barrier too)
-    if (role == 0) {
-        ntt_forward_from_smem<LOGN, 2, true, true>(sm, T, [&](int j, uint64_t y, uint64_t) { c1[j] = y; });
-    } else {
-        const size_t so = ((size_t)(sk_of ? sk_of[v] : 0) * L + limb) << LOGN;
-        const uint64_t* s = sk + so;
-        const uint64_t* sp = sks + so;
-        const int64_t* mv = m + ((size_t)v << LOGN);
-        const int8_t* ev = e + ((size_t)v << LOGN);
-        ntt_forward_block<LOGN, 2, true, true>(
-            sm, T,
-            [&](int j) {
-                // |e| < q: the reference's residue of a negative e is q + e
-                const int ej = ev[j];
-                return add_mod(signed_residue(mv[j], T.q, T.mu64), ej >= 0 ? (uint64_t)ej : T.q + ej, T.q);
-            },
-            [&](int j, uint64_t x, uint64_t a) {
-                // x - a*s with the product in [0, 4q): x + 4q - as lies in [1, 5q)
-                c0[j] = canon8(x + 4 * T.q - mul_shoup4(a, s[j], sp[j], T.q), T.q);
-            },
-            true);
-    }
-}
-
 // c0 -= c1*s over every limb of nvec ciphertexts, c0 holding NTT(m + e)
 // (the second half of k_enc_u when the two transforms ran concurrently).
 __global__ void k_enc_combine(uint64_t* __restrict__ ct, const uint64_t* __restrict__ sk,
@@ -236,14 +170,20 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
             // (as the plain NTT), so one CTA's loads overlap the other's
             // butterflies
             if (!plan_mode) {
-                // both transforms of a (ct, limb) on one four-CTA cluster
                 constexpr size_t smem2 = (size_t)NttCfg<LP, 2>::SMEM_WORDS * 8;
-                cudaError_t er = ensure_smem(k_enc_quad<LP>, smem2);
+                cudaError_t er = ensure_smem(k_enc_a<LP, 2, 2>, smem2);
                 if (er != cudaSuccess) return er;
-                KScope ks("enc_fused", s);
-                k_enc_quad<LP><<<dim3(c.L * 4, nvec), NttCfg<LP, 2>::NT, smem2, s>>>(ct, m, e, sk, sks, sk_of, seeds,
-                                                                                    c.tabs, c.L, nvec, flags);
-                return cudaGetLastError();
+                er = ensure_smem(k_enc_u<LP, 2, 2>, smem2);
+                if (er != cudaSuccess) return er;
+                {
+                    KScope ks("enc_a", s);
+                    er = launch_cl(2, k_enc_a<LP, 2, 2>, dim3(c.L * 2, nvec), NttCfg<LP, 2>::NT, smem2, s, ct, seeds,
+                                   c.tabs, c.L, nvec, flags, plans, 0);
+                    if (er != cudaSuccess) return er;
+                }
+                KScope ks("enc_u", s);
+                return launch_cl(2, k_enc_u<LP, 2, 2>, dim3(c.L * 2, nvec), NttCfg<LP, 2>::NT, smem2, s, ct, m, e, sk,
+                                 sks, sk_of, c.tabs, c.L, nvec, (const uint32_t*)flags, 0, 1);
             }
         }
         const size_t smem_a = plan_mode ? smem + kEncPlanWinBytes : smem;

@@ -497,28 +497,11 @@ __device__ __forceinline__ void fwd_passes(uint64_t* sm, NttV<M>* v, const K& T,
 // input is staged in shared memory uses ntt_forward_from_smem instead.
 // first(k, sigma) supplies element sigma + k*JS of the first-pass set
 // (k is a compile-time constant after unrolling).
-// A finished forward value in shared memory as a canonical residue.
-template <int M, class K>
-__device__ __forceinline__ uint64_t fwd_out(uint64_t raw, const K& Kc, const LimbTab& T) {
-    if constexpr (is_fp(M)) return fp_out(vfrom<double>(raw), Kc);
-    else if constexpr (M == kModeNC) return mod_u64(raw, T.q, T.mu64);
-    else return canon8(raw, T.q);
-}
-
-// PAIRED: two transforms of the same limb on the two CTA pairs of a
-// four-CTA cluster (ranks 0-1 and 2-3), run in step through the same
-// barriers.  After the last pass a cluster barrier makes both pairs' results
-// visible, st(j, y, y_other) also receives output j of the other pair (read
-// through distributed shared memory when `other` is set, else 0), and a
-// final cluster barrier keeps every CTA's shared memory alive until the
-// other pair has read it.
-template <int LOGN, int M, int CL = ntt_default_cl(LOGN), bool PAIRED = false, class First, class St>
-__device__ __forceinline__ void ntt_forward_core(uint64_t* sm, const LimbTab& T, First& first, St& st,
-                                                 bool other = false) {
+template <int LOGN, int M, int CL = ntt_default_cl(LOGN), class First, class St>
+__device__ __forceinline__ void ntt_forward_core(uint64_t* sm, const LimbTab& T, First& first, St& st) {
     using C = NttCfg<LOGN, CL>;
     static_assert(LOGN >= 10 && LOGN <= 15, "NTT supports N in [1024, 32768]");
     static_assert(C::fwd_r(0) == C::RMAX, "the first pass takes RMAX stages");
-    static_assert(!PAIRED || CL == 2, "paired transforms run on CTA pairs");
     const int tid = threadIdx.x;
     const int h = ntt_rank<LOGN, CL>();
     const auto K = ntt_consts<LOGN, M>(T);
@@ -528,37 +511,27 @@ __device__ __forceinline__ void ntt_forward_core(uint64_t* sm, const LimbTab& T,
 #pragma unroll
     for (int k = 0; k < C::E; k++) v[k] = ntt_in<M>(first(k, sg), K);
     fwd_passes<LOGN, 0, M, CL>(sm, v, K, h, tid);
-    if constexpr (PAIRED) {
-        cluster_sync();  // both pairs' last passes are in shared memory
-        const uint64_t* osm = cluster_smem(sm, cluster_rank() ^ 2);  // same half, other pair
+    __syncthreads();
+    // own share, coalesced: j = h*H + tid + k*NT
 #pragma unroll
-        for (int k = 0; k < C::E; k++) {
-            const int jl = tid + k * C::NT;
-            const uint64_t y = fwd_out<M>(sm[pad(jl)], K, T);
-            const uint64_t yo = other ? fwd_out<M>(osm[pad(jl)], K, T) : 0;
-            st(h * C::H + jl, y, yo);
-        }
-        cluster_sync();  // the other pair has read this CTA's results
-    } else {
-        __syncthreads();
-        // own share, coalesced: j = h*H + tid + k*NT
-#pragma unroll
-        for (int k = 0; k < C::E; k++) {
-            const int jl = tid + k * C::NT;
-            st(h * C::H + jl, fwd_out<M>(sm[pad(jl)], K, T));
-        }
+    for (int k = 0; k < C::E; k++) {
+        const int jl = tid + k * C::NT;
+        uint64_t y;
+        if constexpr (is_fp(M)) y = fp_out(vfrom<double>(sm[pad(jl)]), K);
+        else if constexpr (M == kModeNC) y = mod_u64(sm[pad(jl)], T.q, T.mu64);
+        else y = canon8(sm[pad(jl)], T.q);
+        st(h * C::H + jl, y);
     }
 }
 
 // FP64 forward transform: the lazy mode for limbs the table marks (fp == 2,
 // q < 2^44), else the reducing one (a uniform branch per CTA).
-template <int LOGN, int CL, bool PAIRED = false, class First, class St>
-__device__ __forceinline__ void ntt_forward_fp(uint64_t* sm, const LimbTab& T, First& first, St& st,
-                                               bool other = false) {
+template <int LOGN, int CL, class First, class St>
+__device__ __forceinline__ void ntt_forward_fp(uint64_t* sm, const LimbTab& T, First& first, St& st) {
     if (T.fp == 2)
-        ntt_forward_core<LOGN, kModeFpLazy, CL, PAIRED>(sm, T, first, st, other);
+        ntt_forward_core<LOGN, kModeFpLazy, CL>(sm, T, first, st);
     else
-        ntt_forward_core<LOGN, kModeFp, CL, PAIRED>(sm, T, first, st, other);
+        ntt_forward_core<LOGN, kModeFp, CL>(sm, T, first, st);
 }
 
 // Forward transform of the loader's elements: FP64 for limbs with q < 2^50,
@@ -567,13 +540,13 @@ __device__ __forceinline__ void ntt_forward_fp(uint64_t* sm, const LimbTab& T, F
 // the IMAD pipe, not by the ALU instructions NC removes.
 // FPOK = false keeps a kernel integer-only (less code and fewer registers
 // where the FP64 mode does not pay).
-template <int LOGN, int CL = ntt_default_cl(LOGN), bool FPOK = true, bool PAIRED = false, class Ld, class St>
-__device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T, Ld ld, St st, bool other = false) {
+template <int LOGN, int CL = ntt_default_cl(LOGN), bool FPOK = true, class Ld, class St>
+__device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T, Ld ld, St st) {
     auto first = [&](int k, int sg) { return ld(sg + k * NttCfg<LOGN, CL>::JS); };
     if (FPOK && T.fp)
-        ntt_forward_fp<LOGN, CL, PAIRED>(sm, T, first, st, other);
+        ntt_forward_fp<LOGN, CL>(sm, T, first, st);
     else
-        ntt_forward_core<LOGN, kModeInt, CL, PAIRED>(sm, T, first, st, other);
+        ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
 }
 
 // Forward transform of a poly-limb already staged in shared memory (u64
@@ -581,8 +554,8 @@ __device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T
 // (__syncthreads, or cluster_sync for CL = 2) before the call.  The first
 // pass reads it with the half chosen at compile time, so no per-element
 // address selection.
-template <int LOGN, int CL = ntt_default_cl(LOGN), bool FPOK = true, bool PAIRED = false, class St>
-__device__ __forceinline__ void ntt_forward_from_smem(uint64_t* sm, const LimbTab& T, St st, bool other = false) {
+template <int LOGN, int CL = ntt_default_cl(LOGN), bool FPOK = true, class St>
+__device__ __forceinline__ void ntt_forward_from_smem(uint64_t* sm, const LimbTab& T, St st) {
     using C = NttCfg<LOGN, CL>;
     if constexpr (CL == 2) {
         const int sg0 = ntt_rank<LOGN, CL>() * C::NT + threadIdx.x;
@@ -590,11 +563,10 @@ __device__ __forceinline__ void ntt_forward_from_smem(uint64_t* sm, const LimbTa
         const uint64_t* s1 = cluster_smem(sm, pair_base() + 1) + pad(sg0);
         auto first = [&](int k, int) { return (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))]; };
         if (FPOK && T.fp)
-            ntt_forward_fp<LOGN, CL, PAIRED>(sm, T, first, st, other);
+            ntt_forward_fp<LOGN, CL>(sm, T, first, st);
         else
-            ntt_forward_core<LOGN, kModeInt, CL, PAIRED>(sm, T, first, st, other);
+            ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
     } else {
-        static_assert(!PAIRED, "paired transforms run on CTA pairs");
         auto first = [&](int k, int sg) { return sm[pad(sg + k * C::JS)]; };
         if (FPOK && T.fp)
             ntt_forward_fp<LOGN, CL>(sm, T, first, st);

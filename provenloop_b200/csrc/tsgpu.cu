@@ -609,7 +609,11 @@ int encrypt_core(ts_ctx* c, const SlotSrc& src, size_t count, const uint64_t* d_
             CU(cudaStreamWaitEvent(c->stream, c->ev_join, 0));
             CU(launch_enc_combine(c->dc, ct, d_sk, d_sks, skof, (int)nv, c->stream));
         } else {
-            CU(launch_encode(c->dc, s, (int)nv, w.m, w.e, seeds, 2ULL * c->L * n, w.f, c->stream));
+            // the Gaussian error (words 2LN.. of each stream) in its own
+            // kernel: ChaCha20 and Box-Muller at full occupancy, where the
+            // encode's FFT holds one CTA per SM
+            CU(launch_encode(c->dc, s, (int)nv, w.m, nullptr, seeds, 0, w.f, c->stream));
+            CU(launch_gauss_gen(c->dc, w.e, seeds, (int)nv, 2ULL * c->L * n, c->stream));
             CU(launch_encrypt_limbs(c->dc, ct, w.m, w.e, d_sk, d_sks, skof, seeds, (int)nv, w.fl, w.pl, false,
                                     c->stream));
         }
@@ -1442,6 +1446,20 @@ int ts_hadamard(ts_ctx* c, uint64_t* out, const uint64_t* a, const uint64_t* b, 
 }
 
 // ------------------------------------------------------------------ ZeRo-MOAI
+// Packed plaintext rows of one adapter (inference_engine.py:1060-1068): row
+// b holds A's rows b*cols .. b*cols + cols - 1, row i of them at slots
+// i*d .. i*d + d - 1; out [nb][slots] must be zero on entry.
+static void pack_lora_rows(const float* A, uint32_t r, uint32_t d, uint32_t cols, uint32_t nb, uint32_t slots,
+                           double* out) {
+    for (uint32_t b = 0; b < nb; b++) {
+        double* row = out + (size_t)b * slots;
+        for (uint32_t i = 0; i < cols && b * cols + i < r; i++) {
+            const float* a_row = A + ((size_t)b * cols + i) * d;
+            for (uint32_t j = 0; j < d; j++) row[(size_t)i * d + j] = (double)a_row[j];
+        }
+    }
+}
+
 int ts_lora_load(ts_ctx* c, const float* A, const float* B, uint32_t experts, uint32_t r, uint32_t d, ts_lora** out) {
     if (!c || !A || !B || !out || experts == 0 || r == 0 || d == 0) return fail(TS_ERR_ARG, "bad lora_load arguments");
     if (d > c->slots) return fail(TS_ERR_ARG, "d_model %u exceeds slot count %u", d, c->slots);
@@ -1450,16 +1468,9 @@ int ts_lora_load(ts_ctx* c, const float* A, const float* B, uint32_t experts, ui
     if (rc) return rc;
     const uint32_t cols = c->slots / d > 0 ? c->slots / d : 1;  // inference_engine.py:1057
     const uint32_t nb = (r + cols - 1) / cols;                 // :1058
-    // packed plaintext rows (inference_engine.py:1060-1068)
     std::vector<double> packed((size_t)experts * nb * c->slots, 0.0);
     for (uint32_t e = 0; e < experts; e++)
-        for (uint32_t b = 0; b < nb; b++) {
-            double* row = packed.data() + ((size_t)e * nb + b) * c->slots;
-            for (uint32_t i = 0; i < cols && b * cols + i < r; i++) {
-                const float* a_row = A + ((size_t)e * r + b * cols + i) * d;
-                for (uint32_t j = 0; j < d; j++) row[(size_t)i * d + j] = (double)a_row[j];
-            }
-        }
+        pack_lora_rows(A + (size_t)e * r * d, r, d, cols, nb, c->slots, packed.data() + (size_t)e * nb * c->slots);
     ts_lora* lo = new ts_lora{c, experts, r, d, cols, nb, nullptr, nullptr, nullptr};
     double* d_in = nullptr;
     // Segment functionals of the decode (encoding.rs:295-315): slot k of a
@@ -1510,6 +1521,43 @@ int ts_lora_load(ts_ctx* c, const float* A, const float* B, uint32_t experts, ui
     }
     *out = ctx_adopt(lo);
     return TS_OK;
+}
+
+// Hot swap of one expert (inference_engine.py:879-959 swap_adapter, with the
+// NTT(plaintext) cache of :1037-1074): the expert's cached plaintexts, their
+// Shoup companions and its B are rebuilt in place, so device pointers held
+// elsewhere (a captured decode-step graph) stay valid.  The rebuild is
+// ordered on the context's stream and complete when the call returns; work
+// enqueued on that stream before the call sees the old adapter, work after
+// it the new one.
+int ts_lora_set_expert(ts_ctx* c, ts_lora* lo, uint32_t expert, const float* A, const float* B) {
+    if (!c || !lo || !A || !B) return fail(TS_ERR_ARG, "bad lora_set_expert arguments");
+    if (lo->ctx != c) return fail(TS_ERR_ARG, "adapter belongs to another context");
+    if (expert >= lo->experts) return fail(TS_ERR_ARG, "expert %u out of range (%u experts)", expert, lo->experts);
+    Lock lk(c);
+    int rc = set_device(c);
+    if (rc) return rc;
+    const uint32_t nb = lo->batches, r = lo->r, d = lo->d;
+    std::vector<double> packed((size_t)nb * c->slots, 0.0);
+    pack_lora_rows(A, r, d, lo->cols, nb, c->slots, packed.data());
+    const size_t pt_words = (size_t)lo->experts * nb * c->L * c->n;
+    const size_t off = (size_t)expert * nb * c->L * c->n;
+    double* d_in = nullptr;
+    rc = dev_alloc(c, (void**)&d_in, packed.size() * 8);
+    if (!rc) rc = h2d_small(c, d_in, packed.data(), packed.size());
+    if (!rc) rc = h2d_small(c, lo->d_b + (size_t)expert * d * r, B, (size_t)d * r);
+    if (!rc) rc = encode_ntt_core(c, d_in, nb, c->slots, c->slots, lo->d_pt + off);
+    if (!rc) {
+        cudaError_t e = launch_shoup_companion(c->dc, lo->d_pt + pt_words + off, lo->d_pt + off,
+                                               (long long)nb * c->L, c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "lora_set_expert: %s", cudaGetErrorString(e));
+    }
+    if (d_in) cudaFreeAsync(d_in, c->stream);
+    if (!rc) {
+        cudaError_t e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess) rc = fail(TS_ERR_CUDA, "lora_set_expert: %s", cudaGetErrorString(e));
+    }
+    return rc;
 }
 
 int ts_lora_destroy(ts_lora* lo) {

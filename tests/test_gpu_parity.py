@@ -562,3 +562,64 @@ def test_ntt_fp64_mode_edges_bit_exact(T, oracle, n):
     for p in range(3):
         for l, q in enumerate(qs):
             assert np.array_equal(inv[p, l], oracle.ntt_inverse(x[p, l], n, q)), (p, l)
+
+
+def test_lora_set_expert_between_graph_replays(T, oracle):
+    """Adapter hot swap (inference_engine.py:879-959): a captured CUDA graph
+    of ts_lora_delta_batch (device seeds and expert indexes) is replayed,
+    expert 1 is replaced in place, and the next replay of the same graph
+    gives expert 1's rows from the new adapter (against the oracle) while
+    the other experts' rows are unchanged."""
+    import torch
+    from provenloop_b200 import _lib
+    from provenloop_b200.backend import ZeroMoaiLora, lora_delta_graphable
+    ctx = T.CkksContext(16384)
+    octx = oracle.Ctx(16384)
+    rng = np.random.default_rng(61)
+    E, r, d, n = 3, 16, 1536, 6
+    A = (rng.standard_normal((E, r, d)) * 0.02).astype(np.float32)
+    B = (rng.standard_normal((E, d, r)) * 0.02).astype(np.float32)
+    A2 = (rng.standard_normal((r, d)) * 0.02).astype(np.float32)
+    B2 = (rng.standard_normal((d, r)) * 0.02).astype(np.float32)
+    H = rng.standard_normal((n, d))
+    seeds = np.arange(4000, 4000 + n, dtype=np.uint64)
+    expert = np.array([0, 1, 2, 1, 0, 1], dtype=np.int32)
+    sk = ctx.keygen(3)
+    lora = ZeroMoaiLora(ctx, A, B)
+    stream = torch.cuda.Stream()
+    _lib.check(_lib.lib().ts_ctx_set_stream(ctx.handle, stream.cuda_stream), "set_stream")
+    h = torch.from_numpy(H).cuda()
+    out = torch.empty_like(h)
+    sd = torch.from_numpy(seeds.view(np.int64)).cuda()
+    ex = torch.from_numpy(expert).cuda()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        lora_delta_graphable(lora, sk, h, sd, out, expert_dev=ex)  # sizes the scratch
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            lora_delta_graphable(lora, sk, h, sd, out, expert_dev=ex)
+    g.replay()
+    torch.cuda.synchronize()
+    before = out.cpu().numpy()
+    osk = octx.keygen(3)
+    for i in range(n):
+        od, _ = octx.lora_delta(osk, H[i], A[expert[i]], B[expert[i]], enc_seed=int(seeds[i]))
+        assert np.abs(before[i] - od).max() < 1e-4, i
+    lora.set_expert(1, A2, B2)
+    g.replay()
+    torch.cuda.synchronize()
+    after = out.cpu().numpy()
+    for i in range(n):
+        if expert[i] == 1:
+            od, _ = octx.lora_delta(osk, H[i], A2, B2, enc_seed=int(seeds[i]))
+            assert np.abs(after[i] - od).max() < 1e-4, i
+            assert np.abs(after[i] - before[i]).max() > 1e-6, i
+        else:
+            assert np.array_equal(after[i], before[i]), i
+    with pytest.raises(ValueError):
+        lora.set_expert(3, A2, B2)
+    with pytest.raises(ValueError):
+        lora.set_expert(0, A2[:8], B2)
+    del g
+    _lib.check(_lib.lib().ts_ctx_reset_stream(ctx.handle), "reset_stream")

@@ -5,6 +5,7 @@ used for ncu captures).
     python -m provenloop_b200.microbench hadamard [--polys 1024] [--reps 4]
     python -m provenloop_b200.microbench delta [--batch 256] [--reps 3]
     python -m provenloop_b200.microbench latency [--batch 1] [--reps 50]
+    python -m provenloop_b200.microbench kernels
 
 `ntt` is the C2 configuration: `polys` polynomials x 3 limbs x N = 16384 with
 the three largest distinct 50-bit primes == 1 mod 2N, forward then inverse
@@ -251,9 +252,46 @@ def latency(batch=1, reps=50, rank=32, device=0):
             "kernels_ms_per_call": kern, "kernels_cold_l2_ms_per_call": kern_cold}
 
 
+def kernels(device=0):
+    """One call of every path of the library at sizes whose data exceed L2
+    where the path allows (the case the per-kernel ncu summary is captured
+    on): batched keygen, secret- and public-key encryption, decrypt of fresh
+    and ct x pt ciphertexts, rescale, DP noise, the small-batch delta (the
+    decode step's latency form), and an N = 32768 delta batch."""
+    import torch
+
+    from . import _lib, tensafe_he
+    from .backend import ZeroMoaiLora, add_dp_noise, dp_sigma
+
+    rng = np.random.default_rng(0)
+    ctx, stream = _ctx(None, device)
+    with torch.cuda.stream(stream):
+        skb = ctx.keygen_batch(list(range(128)))                     # 128 keys (64 MiB)
+        sk = ctx.keygen(7)
+        X = rng.standard_normal((128, 8192))
+        ct = ctx.encrypt_batch(X, sk, list(range(128)))              # 128 MiB of ciphertexts
+        ctx.decrypt(ct, sk)                                          # fresh: limb 0, decode
+        prod = ct * rng.standard_normal(8192)                        # encode_to_ntt + Hadamard
+        ctx.decrypt(prod, sk)                                        # CRT decode
+        ctx.rescale(prod)
+        pk = ctx.keygen_public(sk, seed=3)
+        ctx.encrypt_pk_batch(X[:64], pk, list(range(64)))
+        add_dp_noise(ctx, rng.standard_normal((8192, 1536)), dp_sigma(), list(range(8192)))
+        A = (rng.standard_normal((3, 32, 1536)) * 0.02).astype(np.float32)
+        B = (rng.standard_normal((3, 1536, 32)) * 0.02).astype(np.float32)
+        lora = ZeroMoaiLora(ctx, A, B)
+        lora.delta(sk, rng.standard_normal((1, 1536)), [5], expert=[1])   # small-batch form
+        c32 = tensafe_he.CkksContext.custom(32768, [60, 40, 40, 40, 60], device=device)
+        _lib.check(_lib.lib().ts_ctx_set_stream(c32.handle, stream.cuda_stream), "ts_ctx_set_stream")
+        l32 = ZeroMoaiLora(c32, A[0], B[0])
+        l32.delta(c32.keygen(3), rng.standard_normal((64, 1536)), list(range(64)))
+        stream.synchronize()
+    return {"kernel": "all_paths", "launches_total": _lib.launch_count()}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["ntt", "hadamard", "delta", "latency"])
+    ap.add_argument("what", choices=["ntt", "hadamard", "delta", "latency", "kernels"])
     ap.add_argument("--polys", type=int, default=1024)
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--reps", type=int, default=None)
@@ -264,6 +302,8 @@ def main():
         r = hadamard(a.polys, a.reps or 4)
     elif a.what == "latency":
         r = latency(a.batch if a.batch != 256 else 1, a.reps or 50)
+    elif a.what == "kernels":
+        r = kernels()
     else:
         r = delta(a.batch, a.reps or 3)
     print(json.dumps(r))

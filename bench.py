@@ -336,7 +336,8 @@ def run_reference(args):
 #   decrypt_limb  per (ct, batch, limb): read c0, c1 (16N) + s (8N) + NTT(pt) (8N), write M (8N) = 40N
 #   decode_a      per (ct, batch):       read M (2 x 8N), write 16N = 32N
 #   decode_b      per (ct, batch):       read 16N
-#   encode        per ct (N = 16384, one kernel): read h (d*8), write m (8N) + e (N)
+#   encode        per ct (N = 16384, one kernel): read h (d*8), write m (8N) (+ e (N) when fused)
+#   gauss_gen     per ct:                write e (N)
 #   encode_a      per ct:                write 16N (+ d*8 read)
 #   encode_b      per ct:                read 16N, write m (8N) + e (N) = 25N
 #   dec_fused     per delta:             the decrypt side of the compulsory-traffic model:
@@ -353,6 +354,7 @@ def kernel_bytes_per_delta(name: str, L: int = 4, nb: int = 4) -> float:
         "decode_a": 32 * n * nb,
         "decode_b": 16 * n * nb,
         "encode": 9 * n + D * 8,
+        "gauss_gen": n,
         "encode_a": 16 * n + D * 8,
         "encode_b": 25 * n,
         "dec_fused": 8 * n * (6 + 2 * nb) + 8 * nb * 5,

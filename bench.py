@@ -33,6 +33,11 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    # NCCL's init lines name every rank's communicator size; set before torch
+    # loads NCCL, which reads these once
+    os.environ["NCCL_DEBUG"] = "INFO"
+    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
 
 N_POLY, D, R = 16384, 1536, 16
 METRIC = "encrypted LoRA deltas/sec (CKKS N=16384, d=1536, r=16, ZeRo-MOAI)"
@@ -244,6 +249,21 @@ def cpu_c3_layer(cd: CpuDeltas, threads: int):
     return time.perf_counter() - t0
 
 
+def oracle_spot_check(rows, seeds, got):
+    """The CPU leg's checker: the oracle recomputes the deltas of the given
+    hidden-state rows and encryption seeds (cached NTT(pt), as the GPU arm's
+    adapter); max-abs error against the GPU deltas, tolerance 1e-4."""
+    from oracle import oracle as O
+
+    H, A, B = inputs(1)
+    octx = O.Ctx(N_POLY)
+    osk = octx.keygen(0)
+    pc = octx.lora_pack(A)
+    errs = [float(np.abs(octx.lora_delta(osk, h, A, B, enc_seed=int(s), mode=0, pt_cache=pc)[0] - g).max())
+            for h, s, g in zip(rows, seeds, got)]
+    return {"rows": len(errs), "max_abs_err_vs_oracle": max(errs), "tolerance": 1e-4, "ok": max(errs) < 1e-4}
+
+
 def cpu_baseline_leg(seconds: float = 10.0, check=None):
     """CPU baseline on the box's host cores (rank 0, N = 1): the oracle
     restatement of tensafe-he-core.  The headline `value` is the all-core
@@ -254,15 +274,7 @@ def cpu_baseline_leg(seconds: float = 10.0, check=None):
     threads = cpu_threads()
     cd = CpuDeltas(threads)
     try:
-        parity = None
-        if check is not None:
-            rows, seeds, got = check
-            errs = []
-            for h, s, g in zip(rows, seeds, got):
-                od, _ = cd.one(0, int(s), "cached", h=h)
-                errs.append(float(np.abs(od - g).max()))
-            parity = {"rows": len(errs), "max_abs_err_vs_oracle": max(errs), "tolerance": 1e-4,
-                      "ok": max(errs) < 1e-4}
+        parity = oracle_spot_check(*check) if check is not None else None
         rate, n, wall = cd.rate(seconds, "cached")
         r1, n1, w1 = cd.rate(3.0, "cached", 1)
         ra, na, wa = cd.rate(3.0, "as_invoked")
@@ -353,7 +365,7 @@ def kernel_bytes_per_delta(name: str, L: int = 4, nb: int = 4) -> float:
         "decrypt_limb": 40 * n * nb * 2,
         "decode_a": 32 * n * nb,
         "decode_b": 16 * n * nb,
-        "encode": 9 * n + D * 8,
+        "encode": 8 * n + D * 8,
         "gauss_gen": n,
         "encode_a": 16 * n + D * 8,
         "encode_b": 25 * n,
@@ -441,9 +453,6 @@ def run_ours(args):
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        # NCCL's init lines name the communicator size of every rank
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     batch = args.batch
@@ -601,8 +610,11 @@ def run_ours(args):
         c3 = c3_leg(dev)
 
     base, parity = None, None
+    check = (H[last_rows], last_seeds[last_rows], last_delta[last_rows])
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        base, parity = cpu_baseline_leg(check=(H[last_rows], last_seeds[last_rows], last_delta[last_rows]))
+        base, parity = cpu_baseline_leg(check=check)
+    elif rank == 0:
+        parity = oracle_spot_check(*check)
 
     if rank == 0:
         line = {
@@ -627,10 +639,12 @@ def run_ours(args):
             line["c3"] = c3
         if c4:
             line["c4"] = c4
-        print(json.dumps(line))
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+        time.sleep(1.0)   # the other ranks' NCCL teardown lines come first; the JSON line is the last
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 def ctx_sms(dev):
@@ -857,13 +871,14 @@ def run_c4(args):
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-    c4_leg(args, torch.device("cuda", local), world, rank, local, args.steps, args.warmup, print_line=True)
+    out = c4_leg(args, torch.device("cuda", local), world, rank, local, args.steps, args.warmup, print_line=False)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+        time.sleep(1.0)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
 
 
 def run_c5(args):

@@ -373,62 +373,78 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     }
 }
 
-// The same decrypt for N = 8192 and 16384 on a cluster of four CTAs per
-// (delta, batch) vector, two CTAs per SM: one pair of ranks (0-1 in even
-// clusters, 2-3 in odd ones) runs the limb-0 INTT, the other pair the limb-1
-// INTT (each CTA half a poly-limb; FP64 butterflies for a limb below 2^50),
-// both parked in shared memory.  Then CTA (l, h) takes the l-th half of half
-// h's positions, reading both limbs through DSMEM, into the CRT, / Delta^2
-// and the segment functionals; rank 0 adds the four CTAs' partials in
-// (limb, half) order.
-// No limb-0 round trip through memory, and one CTA's loads overlap the
-// other's butterflies on each SM.
+// The fused decrypt at N = 8192 and 16384, split in two kernels.  With both
+// limbs' INTTs in one four-CTA cluster (an FP64 pair for the 40-bit limb 1
+// beside an integer pair for the 60-bit limb 0) the FP64 pair finished well
+// before the integer pair and waited at the cluster barrier, holding its SM
+// slots (4.34 ms against 1.52 + 2.45 ms per C1 step for the split form).
+// Here each kernel's CTA pairs do one kind of transform:
+//   k_dec_limb1: p*(c0 + c1*s) and the INTT of limb 1 for every vector
+//     (FP64 butterflies), canonical results to M1 [nvec][N];
+//   k_dec_pair: the same for limb 0 (IMAD butterflies), parked in shared
+//     memory, then the CRT with M1, / Delta^2 and the segment functionals
+//     over the pair's positions; rank 0 adds the two CTAs' partials in rank
+//     order.
+template <int LOGN>
+__global__ void __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
+    k_dec_limb1(uint64_t* __restrict__ M1, const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs,
+                const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
+                const uint64_t* __restrict__ pt, const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel,
+                int per_ct, const LimbTab* __restrict__ tabs, int L) {
+    extern __shared__ __align__(16) uint64_t sm[];
+    const int v = blockIdx.x >> 1;
+    const int ci = v / per_ct;
+    const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
+    const size_t key = (size_t)(sk_of ? sk_of[ci] : 0) * L;
+    const LimbTab T = tabs[1];
+    const uint64_t* c0 = cts + (size_t)ci * ct_stride + ((size_t)1 << LOGN);
+    const uint64_t* c1 = cts + (size_t)ci * ct_stride + ((size_t)(ct_limbs + 1) << LOGN);
+    const uint64_t* s = sk + ((key + 1) << LOGN);
+    const uint64_t* sp = sks + ((key + 1) << LOGN);
+    const uint64_t* p = pt + (((size_t)pv * L + 1) << LOGN);
+    const uint64_t* pp = pts + (((size_t)pv * L + 1) << LOGN);
+    uint64_t* out = M1 + ((size_t)v << LOGN);
+    // p*(c0 + c1*s): c0 + c1*s < 5q, the product lies in [0, 4q)
+    ntt_inverse_block<LOGN, 2>(
+        sm, T, [&](int j) { return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q); },
+        [&](int j, uint64_t x) { out[j] = x; });
+}
+
 template <int LOGN, int MAXC, bool FPC>
-__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
-    k_dec_quad(const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs, const uint64_t* __restrict__ sk,
-               const uint64_t* __restrict__ sks, const int* __restrict__ sk_of, const uint64_t* __restrict__ pt,
-               const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel, int per_ct,
-               const LimbTab* __restrict__ tabs, int L, CrtConst K, double inv_scale, const double* __restrict__ W,
-               int cols, double* __restrict__ seg_out) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
+    k_dec_pair(const uint64_t* __restrict__ M1, const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs,
+               const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
+               const uint64_t* __restrict__ pt, const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel,
+               int per_ct, const LimbTab* __restrict__ tabs, int L, CrtConst K, double inv_scale,
+               const double* __restrict__ W, int cols, double* __restrict__ seg_out) {
     extern __shared__ __align__(16) uint64_t sm[];
     using C = NttCfg<LOGN, 2>;
     constexpr int N = C::N, NT = C::NT, H = C::H;
-    __shared__ double red[NT / 32][kMaxSegCols];
-    const int tid = threadIdx.x;
-    const int v = blockIdx.x >> 2;
-    // The scheduler puts the four CTAs of a cluster on four SMs and refills a
-    // finished cluster's slots with the next cluster in the same rank order,
-    // so with fixed roles an SM would host limb-0 CTAs (IMAD butterflies)
-    // only, or limb-1 CTAs (FP64 butterflies) only.  Odd clusters swap which
-    // pair takes limb 0, which mixes the two pipes' work on an SM.
-    const int swap = v & 1;
-    const int rank = cluster_rank(), limb = (rank >> 1) ^ swap, h = rank & 1;
+    __shared__ double red[NT / 32][MAXC];
+    const int tid = threadIdx.x, v = blockIdx.x >> 1, h = cluster_rank();
     const int ci = v / per_ct;
     const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
     const size_t key = (size_t)(sk_of ? sk_of[ci] : 0) * L;
     {
-        const LimbTab T = tabs[limb];
-        const uint64_t* c0 = cts + (size_t)ci * ct_stride + ((size_t)limb << LOGN);
-        const uint64_t* c1 = cts + (size_t)ci * ct_stride + ((size_t)(ct_limbs + limb) << LOGN);
-        const uint64_t* s = sk + ((key + limb) << LOGN);
-        const uint64_t* sp = sks + ((key + limb) << LOGN);
-        const uint64_t* p = pt + (((size_t)pv * L + limb) << LOGN);
-        const uint64_t* pp = pts + (((size_t)pv * L + limb) << LOGN);
-        // p*(c0 + c1*s): c0 + c1*s < 5q, the product lies in [0, 4q)
+        const LimbTab T = tabs[0];
+        const uint64_t* c0 = cts + (size_t)ci * ct_stride;
+        const uint64_t* c1 = cts + (size_t)ci * ct_stride + ((size_t)ct_limbs << LOGN);
+        const uint64_t* s = sk + (key << LOGN);
+        const uint64_t* sp = sks + (key << LOGN);
+        const uint64_t* p = pt + ((size_t)pv * L << LOGN);
+        const uint64_t* pp = pts + ((size_t)pv * L << LOGN);
         auto ld = [&](int j) { return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q); };
-        ntt_inverse_to_smem<LOGN, false, 2>(sm, T, ld);  // ends with a cluster barrier
+        ntt_inverse_to_smem<LOGN, false, 2>(sm, T, ld);  // this CTA's half at its padded local positions
     }
-    const uint64_t* m0 = cluster_smem(sm, (swap << 1) + h);
-    const uint64_t* m1 = cluster_smem(sm, ((swap ^ 1) << 1) + h);
-    double acc[MAXC];  // MAXC >= cols: 5 covers N = 16384 at d >= 1366
+    const uint64_t* m1 = M1 + ((size_t)v << LOGN) + (size_t)h * H;
+    double acc[MAXC];
 #pragma unroll
     for (int c = 0; c < MAXC; c++) acc[c] = 0.0;
-    constexpr int Q = H / 2;  // positions per CTA
-#pragma unroll 2  // (4 spilled more at 64 registers)
-    for (int jq = tid; jq < Q; jq += NT) {
-        const int jl = limb * Q + jq;
+#pragma unroll 2
+    for (int k = 0; k < C::E; k++) {
+        const int jl = tid + k * NT;
         const int j = h * H + jl;
-        const double coeff = __dmul_rn(crt_seg_coeff<FPC>(m0[pad(jl)], m1[pad(jl)], K), inv_scale);
+        const double coeff = __dmul_rn(crt_seg_coeff<FPC>(sm[pad(jl)], m1[jl], K), inv_scale);
 #pragma unroll
         for (int c = 0; c < MAXC; c++)
             if (c < cols) acc[c] = fma(coeff, __ldg(W + (size_t)c * N + j), acc[c]);
@@ -441,13 +457,12 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT,
         for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
         if (lane == 0) red[wid][c] = a;
     }
-    cluster_sync();  // every CTA done reading the parked limbs; partials written
-    if (rank == 0 && tid < cols) {
+    cluster_sync();  // both CTAs' partials written
+    if (h == 0 && tid < cols) {
         double a = 0.0;
-        for (int role = 0; role < 4; role++) {  // (limb, half) order, whichever rank took it
-            const int r = ((((role >> 1) ^ swap) << 1) | (role & 1));
+        for (int r = 0; r < 2; r++) {
             const double* rr = cooperative_groups::this_cluster().map_shared_rank(&red[0][0], r);
-            for (int w = 0; w < NT / 32; w++) a += rr[w * kMaxSegCols + tid];
+            for (int w = 0; w < NT / 32; w++) a += rr[w * MAXC + tid];
         }
         seg_out[(size_t)v * cols + tid] = a;
     }
@@ -469,17 +484,26 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
         // N = 8192, 16384: four-CTA clusters (LQ: other sizes never take it)
         constexpr int LQ = (LG == 13 || LG == 14) ? LG : 14;
         if (LG == 13 || LG == 14) {
+            // split form: limb-1 INTTs to M0 (nvec x N words), then limb 0 + CRT
             constexpr size_t smemq = (size_t)NttCfg<LQ, 2>::SMEM_WORDS * 8;
+            cudaError_t er = ensure_smem(k_dec_limb1<LQ>, smemq);
+            if (er != cudaSuccess) return er;
+            {
+                KScope ks("dec_limb1", s);
+                er = launch_cl(2, k_dec_limb1<LQ>, dim3((unsigned)nvec * 2), NttCfg<LQ, 2>::NT, smemq, s, M0, cts,
+                               ct_stride, ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L);
+                if (er != cudaSuccess) return er;
+            }
             // accumulators for at most 5 segment columns where that suffices
             const bool fpc = c.crt.q1d != 0.0;
-            auto kq = seg_cols <= 5 ? (fpc ? k_dec_quad<LQ, 5, true> : k_dec_quad<LQ, 5, false>)
-                                    : (fpc ? k_dec_quad<LQ, kMaxSegCols, true> : k_dec_quad<LQ, kMaxSegCols, false>);
-            cudaError_t er = ensure_smem(kq, smemq);
+            auto kp = seg_cols <= 5 ? (fpc ? k_dec_pair<LQ, 5, true> : k_dec_pair<LQ, 5, false>)
+                                    : (fpc ? k_dec_pair<LQ, kMaxSegCols, true> : k_dec_pair<LQ, kMaxSegCols, false>);
+            er = ensure_smem(kp, smemq);
             if (er != cudaSuccess) return er;
             KScope ks("dec_fused", s);
-            kq<<<dim3((unsigned)nvec * 4), NttCfg<LQ, 2>::NT, smemq, s>>>(
-                cts, ct_stride, ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L, c.crt, inv_scale, W,
-                seg_cols, seg_out);
+            kp<<<dim3((unsigned)nvec * 2), NttCfg<LQ, 2>::NT, smemq, s>>>(
+                M0, cts, ct_stride, ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L, c.crt, inv_scale,
+                W, seg_cols, seg_out);
             return cudaGetLastError();
         }
         constexpr size_t smem = ntt_smem_bytes<LG>();

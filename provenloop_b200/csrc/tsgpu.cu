@@ -1640,9 +1640,11 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
                      i_ct = cv.add(nv * 2 * L * N * 8), i_m = cv.add(nv * N * 8), i_e = cv.add(nv * N),
                      i_fe = cv.add(nv * 2 * N * 8), i_fl = cv.add((2 * nv + 1) * 4),
                      i_pl = cv.add(nv * sizeof(StreamPlan)),
-                     // fused decrypt (N <= 16384): one limb-0 buffer per CTA; otherwise
-                     // both limbs of every vector (and the FFT scratch of the decode)
-                     i_M = cv.add(lo->d_w && c->logn < 15 ? (size_t)c->dc.sms * N * 8 : nv * nb * 2 * N * 8),
+                     // fused decrypt: limb 1 of every vector at N = 8192 / 16384 (split
+                     // form), one limb-0 buffer per CTA below; otherwise both limbs of
+                     // every vector (and the FFT scratch of the decode)
+                     i_M = cv.add(lo->d_w && (c->logn == 13 || c->logn == 14) ? nv * nb * N * 8
+                                  : lo->d_w && c->logn < 13 ? (size_t)c->dc.sms * N * 8 : nv * nb * 2 * N * 8),
                      i_fd = cv.add(lo->d_w ? 0 : nv * nb * 2 * N * 8), i_sg = cv.add(nv * nb * cols * 8);
         // Small batches (a decode step): the weight stream of the model
         // between two calls evicts the kernels' code from L2, and a lone

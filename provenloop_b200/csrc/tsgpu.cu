@@ -202,6 +202,10 @@ struct ts_ctx {
     // their first use
     cudaStream_t side = nullptr, warm = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_gauss = nullptr, ev_warm0 = nullptr, ev_warm1 = nullptr;
+    // copy streams and events of the pipelined host-buffer delta path: the
+    // H2D of chunk k+1 and the D2H of chunk k-1 overlap chunk k's kernels
+    cudaStream_t s_h2d = nullptr, s_d2h = nullptr;
+    cudaEvent_t ev_start = nullptr, ev_h2d[2] = {}, ev_comp[2] = {}, ev_d2h[2] = {};
     // grow-only scratch
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
@@ -553,6 +557,18 @@ int ensure_side_streams(ts_ctx* c) {
     return TS_OK;
 }
 
+// The copy streams and events of the pipelined host-buffer delta path
+// (first use).
+int ensure_copy_streams(ts_ctx* c) {
+    if (c->s_h2d) return TS_OK;
+    for (cudaEvent_t* e : {&c->ev_start, &c->ev_h2d[0], &c->ev_h2d[1], &c->ev_comp[0], &c->ev_comp[1], &c->ev_d2h[0],
+                           &c->ev_d2h[1]})
+        CU(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+    CU(cudaStreamCreateWithFlags(&c->s_d2h, cudaStreamNonBlocking));
+    CU(cudaStreamCreateWithFlags(&c->s_h2d, cudaStreamNonBlocking));
+    return TS_OK;
+}
+
 // Core of every secret-key encryption: `count` vectors already on the device
 // (SlotSrc), seeds / key indexes on the device, output ct [count][2][L][n].
 // Uses only the work buffers in `w` (callers own the scratch layout).
@@ -767,12 +783,13 @@ void ctx_free(ts_ctx* c) {
     cudaFree(c->d_tabs);
     cudaFree(c->d_fft);
     cudaFree(c->d_stats);
-    for (cudaStream_t st : {c->side, c->warm})
+    for (cudaStream_t st : {c->side, c->warm, c->s_h2d, c->s_d2h})
         if (st) {
             cudaStreamSynchronize(st);
             cudaStreamDestroy(st);
         }
-    for (cudaEvent_t e : {c->ev_fork, c->ev_join, c->ev_gauss, c->ev_warm0, c->ev_warm1})
+    for (cudaEvent_t e : {c->ev_fork, c->ev_join, c->ev_gauss, c->ev_warm0, c->ev_warm1, c->ev_start, c->ev_h2d[0],
+                          c->ev_h2d[1], c->ev_comp[0], c->ev_comp[1], c->ev_d2h[0], c->ev_d2h[1]})
         if (e) cudaEventDestroy(e);
     if (c->own) cudaStreamDestroy(c->own);
     delete c;
@@ -1605,8 +1622,24 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
     int rc = set_device(c);
     if (rc) return rc;
     const size_t N = c->n, L = c->L, d = lo->d, r = lo->r, cols = lo->cols, nb = lo->batches;
-    // deltas per pass: large enough that every kernel's grid spans many waves
-    const size_t CH = 2048;
+    // Passes of at most 2048 deltas: large enough that every kernel's grid
+    // spans many waves.  With host buffers and more than 1024 deltas the
+    // passes are pipelined: the H2D of pass k+1 and the D2H of pass k-1 run on
+    // the context's copy streams while pass k's kernels run, and the first
+    // and last passes are 256 deltas, so that only their copies are exposed.
+    const bool pipe = !io_on_device && n > 1024;
+    std::vector<size_t> pass_start;
+    {
+        const size_t edge = pipe ? 256 : 0, mid = n - 2 * edge, per = (mid + 2047) / 2048;
+        if (pipe) pass_start.push_back(0);
+        for (size_t i = 0; i < per; i++) pass_start.push_back(edge + mid * i / per);
+        if (pipe) pass_start.push_back(n - edge);
+        pass_start.push_back(n);
+    }
+    size_t cap = 0;  // scratch is carved once, for the largest pass
+    for (size_t i = 0; i + 1 < pass_start.size(); i++)
+        cap = std::max(cap, pass_start[i + 1] - pass_start[i]);
+    const size_t nbuf = pipe ? 2 : 1;  // host-facing buffers per pass (double-buffered when pipelined)
     const double scale2 = c->dc.scale * c->dc.scale;
     // small per-delta inputs: staged once through pinned memory (async H2D)
     void* small = nullptr;
@@ -1632,20 +1665,28 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         d_ex_all = reinterpret_cast<const int*>(d_seeds_all + n);
         d_sk_all = d_ex_all + n;
     }
-    for (size_t v0 = 0; v0 < n && !rc; v0 += CH) {
-        const size_t nv = n - v0 < CH ? n - v0 : CH;
+    if (pipe) {
+        rc = ensure_copy_streams(c);
+        if (rc) return rc;
+    }
+    for (size_t k = 0; k + 1 < pass_start.size() && !rc; k++) {
+        const size_t v0 = pass_start[k], nv = pass_start[k + 1] - v0;
+        const bool last_pass = k + 2 == pass_start.size();
+        const size_t b = pipe ? (k & 1) : 0;  // host-facing buffer of this pass
         Carve cv;
-        const size_t i_h = cv.add(io_on_device ? 0 : nv * d * 8), i_o = cv.add(io_on_device ? 0 : nv * d * 8),
-                     i_in = cv.add(nv * r * 8),
-                     i_ct = cv.add(nv * 2 * L * N * 8), i_m = cv.add(nv * N * 8), i_e = cv.add(nv * N),
-                     i_fe = cv.add(nv * 2 * N * 8), i_fl = cv.add((2 * nv + 1) * 4),
-                     i_pl = cv.add(nv * sizeof(StreamPlan)),
+        const size_t i_h = cv.add(io_on_device ? 0 : nbuf * cap * d * 8),
+                     i_o = cv.add(io_on_device ? 0 : nbuf * cap * d * 8), i_in = cv.add(nbuf * cap * r * 8),
+                     i_ct = cv.add(cap * 2 * L * N * 8), i_m = cv.add(cap * N * 8), i_e = cv.add(cap * N),
+                     i_fe = cv.add(cap * 2 * N * 8), i_fl = cv.add((2 * cap + 1) * 4),
+                     i_pl = cv.add(cap * sizeof(StreamPlan)),
                      // fused decrypt: limb 1 of every vector at N = 8192 / 16384 (split
-                     // form), one limb-0 buffer per CTA below; otherwise both limbs of
+                     // form; both limbs when the pass is small enough for the per-limb
+                     // path), one limb-0 buffer per CTA below; otherwise both limbs of
                      // every vector (and the FFT scratch of the decode)
-                     i_M = cv.add(lo->d_w && (c->logn == 13 || c->logn == 14) ? nv * nb * N * 8
-                                  : lo->d_w && c->logn < 13 ? (size_t)c->dc.sms * N * 8 : nv * nb * 2 * N * 8),
-                     i_fd = cv.add(lo->d_w ? 0 : nv * nb * 2 * N * 8), i_sg = cv.add(nv * nb * cols * 8);
+                     i_M = cv.add(lo->d_w && (c->logn == 13 || c->logn == 14)
+                                      ? cap * nb * N * 8 * ((int)(cap * nb * 2) <= c->dc.sms ? 2 : 1)
+                                  : lo->d_w && c->logn < 13 ? (size_t)c->dc.sms * N * 8 : cap * nb * 2 * N * 8),
+                     i_fd = cv.add(lo->d_w ? 0 : cap * nb * 2 * N * 8), i_sg = cv.add(cap * nb * cols * 8);
         // Small batches (a decode step): the weight stream of the model
         // between two calls evicts the kernels' code from L2, and a lone
         // transform's CTA then stalls on instruction fetches from HBM.  A
@@ -1654,15 +1695,15 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         // of the call and brings their code back into L2 before the real
         // launches need it.
         const int cl = c->logn >= 15 ? 2 : 1;
-        const bool code_warm = lo->d_w && (int)(nv * L * cl * 2) <= c->dc.sms &&
+        const bool code_warm = !pipe && lo->d_w && (int)(nv * L * cl * 2) <= c->dc.sms &&
                           (c->logn == 15 || (c->logn >= 13 && (int)(nv * nb * 2 * 2) <= c->dc.sms));
         const size_t i_wm = cv.add(code_warm ? 2 * N * 8 + kMaxSegCols * 8 : 0);
-        rc = ensure_scratch(c, cv.total());
+        rc = ensure_scratch(c, cv.total());  // grows on the first pass only
         if (rc) break;
         void* S = c->scratch;
-        double* dh = io_on_device ? const_cast<double*>(h) + v0 * d : cv.at<double>(S, i_h);
-        double* dout = io_on_device ? delta + v0 * d : cv.at<double>(S, i_o);
-        double* dinter = (io_on_device && inter) ? inter + v0 * r : cv.at<double>(S, i_in);
+        double* dh = io_on_device ? const_cast<double*>(h) + v0 * d : cv.at<double>(S, i_h) + b * cap * d;
+        double* dout = io_on_device ? delta + v0 * d : cv.at<double>(S, i_o) + b * cap * d;
+        double* dinter = (io_on_device && inter) ? inter + v0 * r : cv.at<double>(S, i_in) + b * cap * r;
         const uint64_t* ds = d_seeds_all + v0;
         const int* dex = expert ? d_ex_all + v0 : nullptr;
         const int* dsk = sk_index ? d_sk_all + v0 : nullptr;
@@ -1670,8 +1711,31 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         uint64_t* M = cv.at<uint64_t>(S, i_M);
         double* fd = cv.at<double>(S, i_fd);
         double* sg = cv.at<double>(S, i_sg);
-        if (!io_on_device) rc = h2d_small(c, dh, h + v0 * d, nv * d);
-        if (rc) break;
+        if (pipe) {
+            double* dh0 = cv.at<double>(S, i_h);
+            if (k == 0) {
+                // the scratch (and the staged seeds) are ready in the context's
+                // stream order; pass 0's hidden states go first
+                CU(cudaEventRecord(c->ev_start, c->stream));
+                CU(cudaStreamWaitEvent(c->s_h2d, c->ev_start, 0));
+                CU(cudaMemcpyAsync(dh0, h, nv * d * 8, cudaMemcpyHostToDevice, c->s_h2d));
+                CU(cudaEventRecord(c->ev_h2d[0], c->s_h2d));
+            }
+            if (!last_pass) {
+                // pass k+1's hidden states into the other buffer, once pass k-1
+                // (its last reader) has run
+                const size_t v1 = pass_start[k + 1], nv1 = pass_start[k + 2] - v1;
+                const size_t b1 = (k + 1) & 1;
+                if (k >= 1) CU(cudaStreamWaitEvent(c->s_h2d, c->ev_comp[b1], 0));
+                CU(cudaMemcpyAsync(dh0 + b1 * cap * d, h + v1 * d, nv1 * d * 8, cudaMemcpyHostToDevice, c->s_h2d));
+                CU(cudaEventRecord(c->ev_h2d[b1], c->s_h2d));
+            }
+            CU(cudaStreamWaitEvent(c->stream, c->ev_h2d[b], 0));
+            if (k >= 2) CU(cudaStreamWaitEvent(c->stream, c->ev_d2h[b], 0));  // pass k-2 has left dout / dinter
+        } else if (!io_on_device) {
+            rc = h2d_small(c, dh, h + v0 * d, nv * d);
+            if (rc) break;
+        }
         if (code_warm) {
             rc = ensure_side_streams(c);
             if (rc) break;
@@ -1736,7 +1800,15 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         // 4. delta = B @ intermediate (:1392)
         CU(launch_bmat(lo->d_b, dinter, dout, (int)nv, (int)d, (int)r, expert ? dex : nullptr, (long long)d * r,
                        c->stream));
-        if (!io_on_device) {
+        if (pipe) {
+            // pass k's results leave on the D2H stream while pass k+1 runs
+            CU(cudaEventRecord(c->ev_comp[b], c->stream));
+            CU(cudaStreamWaitEvent(c->s_d2h, c->ev_comp[b], 0));
+            CU(cudaMemcpyAsync(delta + v0 * d, dout, nv * d * 8, cudaMemcpyDeviceToHost, c->s_d2h));
+            if (inter) CU(cudaMemcpyAsync(inter + v0 * r, dinter, nv * r * 8, cudaMemcpyDeviceToHost, c->s_d2h));
+            CU(cudaEventRecord(c->ev_d2h[b], c->s_d2h));
+            if (last_pass) CU(cudaStreamWaitEvent(c->stream, c->ev_d2h[b], 0));  // the call ends after the last copy
+        } else if (!io_on_device) {
             CU(cudaMemcpyAsync(delta + v0 * d, dout, nv * d * 8, cudaMemcpyDeviceToHost, c->stream));
             if (inter) CU(cudaMemcpyAsync(inter + v0 * r, dinter, nv * r * 8, cudaMemcpyDeviceToHost, c->stream));
         }

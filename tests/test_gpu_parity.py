@@ -425,8 +425,8 @@ def test_lora_delta_more_vectors_than_sms(T, ctx16, octx16):
 
 def test_lora_delta_two_chunks_c1(T, ctx16, octx16):
     """The benchmarked shape and beyond: C1 with 2100 hidden states in one
-    call, so the library's 2048-delta passes run twice (a full pass as the
-    bench times it, then a ragged one).  Rows from both passes, including
+    call: through host buffers, three pipelined passes (256, 1588, 256);
+    through device buffers, two passes of 1050 (the bench's 2048 is one).  Rows from both passes, including
     the first and last of each, against the oracle; every row against
     float64 B (A h) (inference_engine.py:1244-1392)."""
     from provenloop_b200.backend import ZeroMoaiLora
@@ -446,6 +446,15 @@ def test_lora_delta_two_chunks_c1(T, ctx16, octx16):
         assert np.abs(inter[i] - oi).max() < 1e-8, i
     plain = (H @ A.astype(np.float64).T) @ B.astype(np.float64).T
     assert np.abs(delta - plain).max() < 1e-4
+    # host buffers and device buffers run different passes: the same deltas
+    # bit for bit
+    import torch
+    h_dev = torch.from_numpy(H).cuda()
+    d_dev = torch.empty_like(h_dev)
+    torch.cuda.synchronize()
+    lora.delta_device(ctx16.keygen(0), h_dev, seeds, d_dev)
+    ctx16.synchronize()
+    assert np.array_equal(d_dev.cpu().numpy(), delta)
 
 
 def test_lora_delta_eight_columns_fused(T, ctx16, octx16):

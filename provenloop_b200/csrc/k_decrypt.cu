@@ -385,38 +385,69 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
 //     memory, then the CRT with M1, / Delta^2 and the segment functionals
 //     over the pair's positions; rank 0 adds the two CTAs' partials in rank
 //     order.
+// u = c0 + c1*s (in [0, 5q)) of limb `limb` of ciphertext ci on the elements
+// this thread later loads into its transforms (j = h*H + tid + k*NT), to the
+// ciphertext's row of U.  The same thread reads them back for every batch,
+// so the row stays in L2 and needs no barrier.
+template <int LOGN>
+__device__ __forceinline__ void dec_u_row(uint64_t* __restrict__ u, const uint64_t* __restrict__ c0,
+                                          const uint64_t* __restrict__ c1, const uint64_t* __restrict__ s,
+                                          const uint64_t* __restrict__ sp, uint64_t q) {
+    using C = NttCfg<LOGN, 2>;
+    const int base = ntt_rank<LOGN, 2>() * C::H + (int)threadIdx.x;
+#pragma unroll 4
+    for (int k = 0; k < C::E; k++) {
+        const int j = base + k * C::NT;
+        u[j] = c0[j] + mul_shoup4(c1[j], s[j], sp[j], q);
+    }
+}
+
+// One batch of k_dec_limb1: INTT of p*u (p*u = p*(c0 + c1*s) = c0*p +
+// (c1*p)*s mod q, in [0, 4q)) to out.  Kept out of line, so that the batch
+// loop's state and the transform's registers are allocated apart.
+template <int LOGN>
+__device__ __noinline__ void dec_limb1_batch(uint64_t* sm, const LimbTab* tab, const uint64_t* __restrict__ u,
+                                             const uint64_t* __restrict__ p, const uint64_t* __restrict__ pp,
+                                             uint64_t* __restrict__ out) {
+    const LimbTab T = *tab;
+    ntt_inverse_block<LOGN, 2>(
+        sm, T, [&](int j) { return mul_shoup4(u[j], p[j], pp[j], T.q); }, [&](int j, uint64_t x) { out[j] = x; });
+}
+
 template <int LOGN>
 __global__ void __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
-    k_dec_limb1(uint64_t* __restrict__ M1, const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs,
-                const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
-                const uint64_t* __restrict__ pt, const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel,
-                int per_ct, const LimbTab* __restrict__ tabs, int L) {
+    k_dec_limb1(uint64_t* __restrict__ M1, uint64_t* __restrict__ U, const uint64_t* __restrict__ cts,
+                long long ct_stride, int ct_limbs, const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks,
+                const int* __restrict__ sk_of, const uint64_t* __restrict__ pt, const uint64_t* __restrict__ pts,
+                const int* __restrict__ pt_sel, int per_ct, const LimbTab* __restrict__ tabs, int L) {
     extern __shared__ __align__(16) uint64_t sm[];
-    const int v = blockIdx.x >> 1;
-    const int ci = v / per_ct;
-    const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
+    const int ci = blockIdx.x >> 1;  // one CTA pair per ciphertext, its per_ct batches in turn
     const size_t key = (size_t)(sk_of ? sk_of[ci] : 0) * L;
-    const LimbTab T = tabs[1];
-    const uint64_t* c0 = cts + (size_t)ci * ct_stride + ((size_t)1 << LOGN);
-    const uint64_t* c1 = cts + (size_t)ci * ct_stride + ((size_t)(ct_limbs + 1) << LOGN);
-    const uint64_t* s = sk + ((key + 1) << LOGN);
-    const uint64_t* sp = sks + ((key + 1) << LOGN);
-    const uint64_t* p = pt + (((size_t)pv * L + 1) << LOGN);
-    const uint64_t* pp = pts + (((size_t)pv * L + 1) << LOGN);
-    uint64_t* out = M1 + ((size_t)v << LOGN);
-    // p*(c0 + c1*s): c0 + c1*s < 5q, the product lies in [0, 4q)
-    ntt_inverse_block<LOGN, 2>(
-        sm, T, [&](int j) { return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q); },
-        [&](int j, uint64_t x) { out[j] = x; });
+    // limb 0's row for k_dec_pair (this kernel's IMAD pipe is otherwise
+    // idle), then limb 1's, which this kernel's transforms read
+    dec_u_row<LOGN>(U + ((size_t)ci * 2 << LOGN), cts + (size_t)ci * ct_stride,
+                    cts + (size_t)ci * ct_stride + ((size_t)ct_limbs << LOGN), sk + (key << LOGN), sks + (key << LOGN),
+                    tabs[0].q);
+    uint64_t* u = U + (((size_t)ci * 2 + 1) << LOGN);
+    dec_u_row<LOGN>(u, cts + (size_t)ci * ct_stride + ((size_t)1 << LOGN),
+                    cts + (size_t)ci * ct_stride + ((size_t)(ct_limbs + 1) << LOGN), sk + ((key + 1) << LOGN),
+                    sks + ((key + 1) << LOGN), tabs[1].q);
+#pragma unroll 1
+    for (int b = 0; b < per_ct; b++) {
+        const int v = ci * per_ct + b;
+        const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + b;
+        dec_limb1_batch<LOGN>(sm, tabs + 1, u, pt + (((size_t)pv * L + 1) << LOGN),
+                              pts + (((size_t)pv * L + 1) << LOGN), M1 + ((size_t)v << LOGN));
+        __syncthreads();
+    }
 }
 
 template <int LOGN, int MAXC, bool FPC>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
-    k_dec_pair(const uint64_t* __restrict__ M1, const uint64_t* __restrict__ cts, long long ct_stride, int ct_limbs,
-               const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks, const int* __restrict__ sk_of,
-               const uint64_t* __restrict__ pt, const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel,
-               int per_ct, const LimbTab* __restrict__ tabs, int L, CrtConst K, double inv_scale,
-               const double* __restrict__ W, int cols, double* __restrict__ seg_out) {
+    k_dec_pair(const uint64_t* __restrict__ M1, const uint64_t* __restrict__ U, const uint64_t* __restrict__ pt,
+               const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel, int per_ct,
+               const LimbTab* __restrict__ tabs, int L, CrtConst K, double inv_scale, const double* __restrict__ W,
+               int cols, double* __restrict__ seg_out) {
     extern __shared__ __align__(16) uint64_t sm[];
     using C = NttCfg<LOGN, 2>;
     constexpr int N = C::N, NT = C::NT, H = C::H;
@@ -424,16 +455,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT,
     const int tid = threadIdx.x, v = blockIdx.x >> 1, h = cluster_rank();
     const int ci = v / per_ct;
     const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + v % per_ct;
-    const size_t key = (size_t)(sk_of ? sk_of[ci] : 0) * L;
     {
         const LimbTab T = tabs[0];
-        const uint64_t* c0 = cts + (size_t)ci * ct_stride;
-        const uint64_t* c1 = cts + (size_t)ci * ct_stride + ((size_t)ct_limbs << LOGN);
-        const uint64_t* s = sk + (key << LOGN);
-        const uint64_t* sp = sks + (key << LOGN);
+        const uint64_t* u = U + ((size_t)ci * 2 << LOGN);  // c0 + c1*s of limb 0, from k_dec_limb1
         const uint64_t* p = pt + ((size_t)pv * L << LOGN);
         const uint64_t* pp = pts + ((size_t)pv * L << LOGN);
-        auto ld = [&](int j) { return mul_shoup4(c0[j] + mul_shoup4(c1[j], s[j], sp[j], T.q), p[j], pp[j], T.q); };
+        auto ld = [&](int j) { return mul_shoup4(u[j], p[j], pp[j], T.q); };
         ntt_inverse_to_smem<LOGN, false, 2>(sm, T, ld);  // this CTA's half at its padded local positions
     }
     const uint64_t* m1 = M1 + ((size_t)v << LOGN) + (size_t)h * H;
@@ -472,8 +499,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT,
 cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_stride, int ct_limbs,
                              const uint64_t* sk, const uint64_t* sks, const int* sk_of, const uint64_t* pt,
                              const uint64_t* pts, const int* pt_sel, int per_ct,
-                             int nvec, double inv_scale, const double* W, int seg_cols, uint64_t* M0, double* seg_out,
-                             cudaStream_t s) {
+                             int nvec, double inv_scale, const double* W, int seg_cols, uint64_t* M0, uint64_t* U,
+                             double* seg_out, cudaStream_t s) {
     if (nvec <= 0) return cudaSuccess;
     if (seg_cols < 1 || seg_cols > kMaxSegCols || c.L < 2) return cudaErrorInvalidValue;
     // correction-free INTT where the modulus leaves the headroom (as in
@@ -488,10 +515,12 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
             constexpr size_t smemq = (size_t)NttCfg<LQ, 2>::SMEM_WORDS * 8;
             cudaError_t er = ensure_smem(k_dec_limb1<LQ>, smemq);
             if (er != cudaSuccess) return er;
+            // one CTA pair per ciphertext (nvec / per_ct of them), u rows in U
+            const unsigned pairs = (unsigned)(nvec / per_ct);
             {
                 KScope ks("dec_limb1", s);
-                er = launch_cl(2, k_dec_limb1<LQ>, dim3((unsigned)nvec * 2), NttCfg<LQ, 2>::NT, smemq, s, M0, cts,
-                               ct_stride, ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L);
+                er = launch_cl(2, k_dec_limb1<LQ>, dim3(pairs * 2), NttCfg<LQ, 2>::NT, smemq, s, M0, U, cts, ct_stride,
+                               ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L);
                 if (er != cudaSuccess) return er;
             }
             // accumulators for at most 5 segment columns where that suffices
@@ -501,9 +530,8 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
             er = ensure_smem(kp, smemq);
             if (er != cudaSuccess) return er;
             KScope ks("dec_fused", s);
-            kp<<<dim3((unsigned)nvec * 2), NttCfg<LQ, 2>::NT, smemq, s>>>(
-                M0, cts, ct_stride, ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L, c.crt, inv_scale,
-                W, seg_cols, seg_out);
+            kp<<<dim3((unsigned)nvec * 2), NttCfg<LQ, 2>::NT, smemq, s>>>(M0, U, pt, pts, pt_sel, per_ct, c.tabs,
+                                                                         c.L, c.crt, inv_scale, W, seg_cols, seg_out);
             return cudaGetLastError();
         }
         constexpr size_t smem = ntt_smem_bytes<LG>();

@@ -222,14 +222,15 @@ cudaError_t launch_decode(const DevCtx& c, const uint64_t* M, int nl, bool crt, 
 // sks / pts hold the Shoup companions of the keys / plaintexts.
 // Supports seg_cols <= kMaxSegCols.  M0 is u64 scratch: [nvec][n] at
 // N = 8192 and 16384 (the split form's limb-1 INTT outputs), else
-// [min(nvec, sms)][n]
+// [min(nvec, sms)][n]; U (N = 8192, 16384 only) is [nvec / per_ct][2][n], the
+// rows of c0 + c1*s of limbs 0 and 1
 // (one limb per persistent group).
 constexpr int kMaxSegCols = 10;
 cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_stride, int ct_limbs,
                              const uint64_t* sk, const uint64_t* sks, const int* sk_of, const uint64_t* pt,
                              const uint64_t* pts, const int* pt_sel, int per_ct,
-                             int nvec, double inv_scale, const double* W, int seg_cols, uint64_t* M0, double* seg_out,
-                             cudaStream_t s);
+                             int nvec, double inv_scale, const double* W, int seg_cols, uint64_t* M0, uint64_t* U,
+                             double* seg_out, cudaStream_t s);
 
 // seg_out[v][c] = sum_j CRT(M[v][0][j], M[v][1][j]) * inv_scale * W[c][j]:
 // the back half of the fused decrypt for INTT outputs already in M.

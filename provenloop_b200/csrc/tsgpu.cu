@@ -1686,7 +1686,9 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
                      i_M = cv.add(lo->d_w && (c->logn == 13 || c->logn == 14)
                                       ? cap * nb * N * 8 * ((int)(cap * nb * 2) <= c->dc.sms ? 2 : 1)
                                   : lo->d_w && c->logn < 13 ? (size_t)c->dc.sms * N * 8 : cap * nb * 2 * N * 8),
-                     i_fd = cv.add(lo->d_w ? 0 : cap * nb * 2 * N * 8), i_sg = cv.add(cap * nb * cols * 8);
+                     i_fd = cv.add(lo->d_w ? 0 : cap * nb * 2 * N * 8), i_sg = cv.add(cap * nb * cols * 8),
+                     // the split decrypt's c0 + c1*s rows of limbs 0 and 1
+                     i_U = cv.add(lo->d_w && (c->logn == 13 || c->logn == 14) ? cap * 2 * N * 8 : 0);
         // Small batches (a decode step): the weight stream of the model
         // between two calls evicts the kernels' code from L2, and a lone
         // transform's CTA then stalls on instruction fetches from HBM.  A
@@ -1785,7 +1787,7 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
             CU(launch_dec_fused(c->dc, ct, (long long)2 * L * N, (int)L, sk->d, sk_shoup(sk), sk_index ? dsk : nullptr,
                                 lo->d_pt, lo->d_pt + (size_t)lo->experts * nb * L * N,
                                 expert ? dex : nullptr, (int)nb, (int)(nv * nb), 1.0 / scale2, lo->d_w, (int)cols, M,
-                                sg, c->stream));
+                                cv.at<uint64_t>(S, i_U), sg, c->stream));
         } else {
             // 2. ct x packed_pt (limbs 0/1) fused with decrypt's c0 + c1*s, INTT (:1311-1315)
             CU(launch_decrypt_limbs(c->dc, M, 2, ct, (long long)2 * L * N, (int)L, sk->d, sk_shoup(sk),

@@ -352,14 +352,14 @@ def run_reference(args):
 #   gauss_gen     per ct:                write e (N)
 #   encode_a      per ct:                write 16N (+ d*8 read)
 #   encode_b      per ct:                read 16N, write m (8N) + e (N) = 25N
-#   dec_limb1     per delta:             limb 1 of the split decrypt: read ct limb 1 (2 x 8N) + s limb 1
-#                                        (8N) + NTT(pt) limb 1 per batch (B x 8N), write the INTT
-#                                        output per batch (B x 8N) = 8N(3 + 2B)
-#   dec_fused     per delta:             limb 0 of the split decrypt with the CRT and the
-#                                        functionals: read ct limb 0 (2 x 8N) + s limb 0 (8N)
-#                                        + NTT(pt) limb 0 per batch (B x 8N) + limb 1's INTT
-#                                        output per batch (B x 8N), write B*cols segment sums
-#                                        = 8N(3 + 2B) + 8*B*cols
+#   dec_limb1     per delta:             the split decrypt's first kernel: read ct limbs 0-1
+#                                        (4 x 8N) + s limbs 0-1 (2 x 8N), write the u rows of
+#                                        limbs 0-1 (2 x 8N), read NTT(pt) limb 1 per batch (B x 8N),
+#                                        write limb 1's INTT per batch (B x 8N) = 8N(8 + 2B)
+#   dec_fused     per delta:             the second (limb 0, CRT, functionals): read limb 0's u
+#                                        row (8N) + NTT(pt) limb 0 per batch (B x 8N) + limb 1's
+#                                        INTT per batch (B x 8N), write B*cols segment sums
+#                                        = 8N(1 + 2B) + 8*B*cols
 #   ntt_*         per poly-limb:         read 8N + write 8N = 16N
 def kernel_bytes_per_delta(name: str, L: int = 4, nb: int = 4) -> float:
     n = N_POLY
@@ -373,8 +373,8 @@ def kernel_bytes_per_delta(name: str, L: int = 4, nb: int = 4) -> float:
         "gauss_gen": n,
         "encode_a": 16 * n + D * 8,
         "encode_b": 25 * n,
-        "dec_fused": 8 * n * (3 + 2 * nb) + 8 * nb * 5,
-        "dec_limb1": 8 * n * (3 + 2 * nb),
+        "dec_fused": 8 * n * (1 + 2 * nb) + 8 * nb * 5,
+        "dec_limb1": 8 * n * (8 + 2 * nb),
     }
     return float(table.get(name, 0))
 

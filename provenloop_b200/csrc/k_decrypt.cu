@@ -419,21 +419,28 @@ __global__ void __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
     k_dec_limb1(uint64_t* __restrict__ M1, uint64_t* __restrict__ U, const uint64_t* __restrict__ cts,
                 long long ct_stride, int ct_limbs, const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks,
                 const int* __restrict__ sk_of, const uint64_t* __restrict__ pt, const uint64_t* __restrict__ pts,
-                const int* __restrict__ pt_sel, int per_ct, const LimbTab* __restrict__ tabs, int L) {
+                const int* __restrict__ pt_sel, int per_ct, int bpp, const LimbTab* __restrict__ tabs, int L) {
     extern __shared__ __align__(16) uint64_t sm[];
-    const int ci = blockIdx.x >> 1;  // one CTA pair per ciphertext, its per_ct batches in turn
+    // CTA pair g of ciphertext ci takes batches [g*bpp, g*bpp + bpp): all of
+    // them when there are enough ciphertexts to fill the GPU, fewer otherwise
+    const int ngrp = (per_ct + bpp - 1) / bpp;
+    const int ci = (blockIdx.x >> 1) / ngrp, b0 = ((blockIdx.x >> 1) % ngrp) * bpp;
+    const int b1 = b0 + bpp < per_ct ? b0 + bpp : per_ct;
     const size_t key = (size_t)(sk_of ? sk_of[ci] : 0) * L;
     // limb 0's row for k_dec_pair (this kernel's IMAD pipe is otherwise
-    // idle), then limb 1's, which this kernel's transforms read
-    dec_u_row<LOGN>(U + ((size_t)ci * 2 << LOGN), cts + (size_t)ci * ct_stride,
-                    cts + (size_t)ci * ct_stride + ((size_t)ct_limbs << LOGN), sk + (key << LOGN), sks + (key << LOGN),
-                    tabs[0].q);
+    // idle; the first group writes it), then limb 1's, which this pair's
+    // transforms read (each group writes the same values and reads back its
+    // own threads' writes)
+    if (b0 == 0)
+        dec_u_row<LOGN>(U + ((size_t)ci * 2 << LOGN), cts + (size_t)ci * ct_stride,
+                        cts + (size_t)ci * ct_stride + ((size_t)ct_limbs << LOGN), sk + (key << LOGN),
+                        sks + (key << LOGN), tabs[0].q);
     uint64_t* u = U + (((size_t)ci * 2 + 1) << LOGN);
     dec_u_row<LOGN>(u, cts + (size_t)ci * ct_stride + ((size_t)1 << LOGN),
                     cts + (size_t)ci * ct_stride + ((size_t)(ct_limbs + 1) << LOGN), sk + ((key + 1) << LOGN),
                     sks + ((key + 1) << LOGN), tabs[1].q);
 #pragma unroll 1
-    for (int b = 0; b < per_ct; b++) {
+    for (int b = b0; b < b1; b++) {
         const int v = ci * per_ct + b;
         const int pv = (pt_sel ? pt_sel[ci] : 0) * per_ct + b;
         dec_limb1_batch<LOGN>(sm, tabs + 1, u, pt + (((size_t)pv * L + 1) << LOGN),
@@ -515,12 +522,16 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
             constexpr size_t smemq = (size_t)NttCfg<LQ, 2>::SMEM_WORDS * 8;
             cudaError_t er = ensure_smem(k_dec_limb1<LQ>, smemq);
             if (er != cudaSuccess) return er;
-            // one CTA pair per ciphertext (nvec / per_ct of them), u rows in U
-            const unsigned pairs = (unsigned)(nvec / per_ct);
+            // u rows once per ciphertext where the ciphertexts alone fill two
+            // waves of CTA pairs; otherwise batches spread over more pairs
+            const int nct = nvec / per_ct;
+            int bpp = nvec / (2 * c.sms);
+            bpp = bpp < 1 ? 1 : (bpp > per_ct ? per_ct : bpp);
+            const unsigned pairs = (unsigned)nct * (unsigned)((per_ct + bpp - 1) / bpp);
             {
                 KScope ks("dec_limb1", s);
                 er = launch_cl(2, k_dec_limb1<LQ>, dim3(pairs * 2), NttCfg<LQ, 2>::NT, smemq, s, M0, U, cts, ct_stride,
-                               ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, c.tabs, c.L);
+                               ct_limbs, sk, sks, sk_of, pt, pts, pt_sel, per_ct, bpp, c.tabs, c.L);
                 if (er != cudaSuccess) return er;
             }
             // accumulators for at most 5 segment columns where that suffices

@@ -29,7 +29,7 @@ DS = (1536, 3584)
 RS = (8, 16, 32, 64)
 
 KERNELS = ("encode", "encode_a", "encode_b", "gauss_gen", "enc_a", "enc_u", "enc_x", "enc_combine", "plan",
-           "gauss_fix", "enc_a_fix", "enc_u_fix", "dec_fused", "decrypt_limb", "crt_seg", "decode_a", "decode_b",
+           "gauss_fix", "enc_a_fix", "enc_u_fix", "dec_limb1", "dec_fused", "decrypt_limb", "crt_seg", "decode_a", "decode_b",
            "gather_inter", "bmat")
 
 
@@ -45,8 +45,14 @@ def kernel_bytes_per_delta(name: str, n: int, L: int, nb: int, cols: int, d: int
     enc_u         per limb: m, e, s, c1 in, c0 out (33N)
     enc_x         per limb: m, e in, c0 out (17N)
     enc_combine   per limb: c0, c1, s in, c0 out (32N)
-    dec_fused     ct limbs 0-1, s limbs 0-1, NTT(pt) limbs 0-1 per batch in,
-                  segment sums out: 8N(6 + 2B) + 8B*cols
+    dec_limb1     (N = 8192, 16384) ct limbs 0-1 and s limbs 0-1 in, the u
+                  rows of limbs 0-1 out, NTT(pt) limb 1 per batch in, limb 1's
+                  INTT per batch out: 8N(8 + 2B)
+    dec_fused     N = 8192, 16384 (k_dec_pair): limb 0's u row, NTT(pt) limb 0
+                  and limb 1's INTT per batch in, segment sums out:
+                  8N(1 + 2B) + 8B*cols; other N (k_dec_fused): ct limbs 0-1,
+                  s limbs 0-1, NTT(pt) limbs 0-1 per batch in, segment sums
+                  out: 8N(6 + 2B) + 8B*cols
     decrypt_limb  per (batch, limb 0/1): c0, c1, s, pt in, INTT out (40N)
     crt_seg       per batch: both INTT limbs in (16N)
     decode_a/b    per batch: 32N and 16N
@@ -62,7 +68,8 @@ def kernel_bytes_per_delta(name: str, n: int, L: int, nb: int, cols: int, d: int
         "enc_u": 33 * n * L,
         "enc_x": 17 * n * L,
         "enc_combine": 32 * n * L,
-        "dec_fused": 8 * n * (6 + 2 * nb) + 8 * nb * cols,
+        "dec_limb1": 8 * n * (8 + 2 * nb),
+        "dec_fused": (8 * n * (1 + 2 * nb) if n in (8192, 16384) else 8 * n * (6 + 2 * nb)) + 8 * nb * cols,
         "decrypt_limb": 80 * n * nb,
         "crt_seg": 16 * n * nb,
         "decode_a": 32 * n * nb,

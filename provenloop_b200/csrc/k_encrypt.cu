@@ -30,9 +30,13 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
     extern __shared__ __align__(16) uint64_t sm[];
     using C = NttCfg<LOGN, CLX>;
     constexpr int N = 1 << LOGN, NT = C::NT, H = C::H;
+    // the throughput form (CTA pairs, two per SM) stages FP64 limbs' draws as
+    // exact doubles; the repair and small-batch forms stage residues
+    constexpr bool kDblStage = MINB == 2 && kPairFp<LOGN, CLX, MINB>;
     const int limb = blockIdx.x / C::CL, tid = threadIdx.x;
     const int h0 = ntt_rank<LOGN, CLX>() * H;  // first element of this CTA's share
     const LimbTab T = tabs[limb];
+    if (kDblStage) plan_mode = 0;  // the throughput form is launched for the speculative pass only
     const int nwork = plan_mode ? (int)flags[nvec] : 1;
     for (int it = blockIdx.y; it < (plan_mode ? nwork : (int)blockIdx.y + 1); it += gridDim.y) {
         const int v = plan_mode ? (int)flags[nvec + 1 + it] : it;
@@ -42,14 +46,37 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
             // this CTA's share: candidates h0 .. h0 + H - 1, 8 per block
             const uint32_t blk0 = (uint32_t)limb * (N / 8);
             bool rej = false;
-            for (int b = h0 / 8 + tid; b < (h0 + H) / 8; b += NT) {
-                uint32_t w[16];
-                chacha_block(seed, blk0 + (uint32_t)b, w);
+            if (kDblStage && T.fp) {  // (kDblStage: every staged FP64-limb word is a double)
+                // FP64 limb: u = hi 2^32 + lo = hi (2^32 mod q) + lo (mod q),
+                // staged as the exact double fp_mulmod(hi, 2^32 mod q) + lo
+                // (|x| <= q + 2^32), which the transform's input reduction
+                // takes like the residue; the IMAD pipe is the busier one here
+                const double q = __ull2double_rn(T.q);
+                const uint64_t r = ((uint64_t)1 << 32) % T.q;
+                const double r32 = r > T.q / 2 ? -__ull2double_rn(T.q - r) : __ull2double_rn(r);
+                const double r32q = __ddiv_rn(r32, q);
+                for (int b = h0 / 8 + tid; b < (h0 + H) / 8; b += NT) {
+                    uint32_t w[16];
+                    chacha_block(seed, blk0 + (uint32_t)b, w);
 #pragma unroll
-                for (int c = 0; c < 8; c++) {
-                    const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
-                    rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
-                    sm[pad(8 * b + c - h0)] = mod_u64(u, T.q, T.mu64);
+                    for (int c = 0; c < 8; c++) {
+                        const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
+                        rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
+                        const double x = __dadd_rn(fp_mulmod(__uint2double_rn(w[2 * c + 1]), r32, r32q, q),
+                                                   __uint2double_rn(w[2 * c]));
+                        sm[pad(8 * b + c - h0)] = vbits(x);
+                    }
+                }
+            } else {
+                for (int b = h0 / 8 + tid; b < (h0 + H) / 8; b += NT) {
+                    uint32_t w[16];
+                    chacha_block(seed, blk0 + (uint32_t)b, w);
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
+                        rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
+                        sm[pad(8 * b + c - h0)] = mod_u64(u, T.q, T.mu64);
+                    }
                 }
             }
             if (rej) flag_stream(flags, nvec, v);
@@ -89,7 +116,8 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
         }
         if constexpr (C::CL == 2) cluster_sync();  // the transform reads both shares
         else __syncthreads();
-        ntt_forward_from_smem<LOGN, CLX, kPairFp<LOGN, CLX, MINB>>(sm, T, [&](int j, uint64_t x) { c1[j] = x; });
+        ntt_forward_from_smem<LOGN, CLX, kPairFp<LOGN, CLX, MINB>, kDblStage>(sm, T,
+                                                                              [&](int j, uint64_t x) { c1[j] = x; });
         __syncthreads();
     }
 }
@@ -116,13 +144,8 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
         const int64_t* mv = m + ((size_t)v << LOGN);
         const int8_t* ev = e + ((size_t)v << LOGN);
         if (sub && threadIdx.x == 0) prefetch_l2(c1 + h0, (unsigned)C::H * 8u);  // this CTA's share, read by the epilogue
-        ntt_forward_block<LOGN, CLX, kPairFp<LOGN, CLX, MINB>>(
-            sm, T,
-            [&](int j) {
-                // |e| < q: the reference's residue of a negative e is q + e
-                const int ej = ev[j];
-                return add_mod(signed_residue(mv[j], T.q, T.mu64), ej >= 0 ? (uint64_t)ej : T.q + ej, T.q);
-            },
+        ntt_forward_signed<LOGN, CLX, kPairFp<LOGN, CLX, MINB>>(
+            sm, T, [&](int j) { return mv[j]; }, [&](int j) { return (int)ev[j]; },
             [&](int j, uint64_t x) {
                 if (!sub) {  // x alone; k_enc_combine subtracts c1*s later
                     c0[j] = x;

@@ -451,6 +451,15 @@ __device__ __forceinline__ NttV<M> ntt_in(uint64_t x, const K& T) {
     else return x;
 }
 
+// An exact integer-valued double (|x| < 2^52) as a value of an FP64 mode:
+// reduced like fp_in reduces a residue (|x * fl(1/q)| stays far inside the
+// rounding constant's 2^51, and x - q*round(x/q) is an exact integer).
+template <int M, class K>
+__device__ __forceinline__ NttV<M> ntt_in(double x, const K& T) {
+    static_assert(is_fp(M), "signed double inputs enter the FP64 modes only");
+    return fp_reduce(x, T.q, T.qinv);
+}
+
 // The transform's constants for mode M: the table entry itself, or FpK.
 template <int LOGN, int M>
 __device__ __forceinline__ auto ntt_consts(const LimbTab& T) {
@@ -549,12 +558,53 @@ __device__ __forceinline__ void ntt_forward_block(uint64_t* sm, const LimbTab& T
         ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
 }
 
+// Forward transform of the signed integers x_j = m_j + e_j (ldm(j): the
+// i64 coefficient m_j; lde(j): the small error |e_j| < 128), congruent to the
+// residue the reference forms per limb, signed_residue(m) + residue(e) mod q
+// (encoding.rs:198-202, ciphertext.rs:196-201).  The FP64 modes take x_j as
+// an exact double when |m_j| < 2^52 (their input reduction does the rest);
+// the integer modes take x_j or q + x_j when |m_j| < q - 128.  Coefficients
+// outside those ranges go through the exact 64-bit reduction.  The outputs
+// equal those of ntt_forward_block on the reference's residues.
+template <int LOGN, int CL = ntt_default_cl(LOGN), bool FPOK = true, class Ldm, class Lde, class St>
+__device__ __forceinline__ void ntt_forward_signed(uint64_t* sm, const LimbTab& T, Ldm ldm, Lde lde, St st) {
+    using C = NttCfg<LOGN, CL>;
+    auto slow = [&](int64_t m, int e) {  // the reference's two residues, added mod q
+        return add_mod(signed_residue(m, T.q, T.mu64), e >= 0 ? (uint64_t)e : T.q + e, T.q);
+    };
+    if (FPOK && T.fp) {
+        auto first = [&](int k, int sg) -> double {
+            const int j = sg + k * C::JS;
+            const int64_t m = ldm(j);
+            const int e = lde(j);
+            if (m > -(1LL << 52) && m < (1LL << 52)) return (double)(m + e);  // exact below 2^53
+            return __ull2double_rn(slow(m, e));                              // < q < 2^50: exact
+        };
+        ntt_forward_fp<LOGN, CL>(sm, T, first, st);
+    } else {
+        const int64_t lim = (int64_t)T.q - 128;
+        auto first = [&](int k, int sg) -> uint64_t {
+            const int j = sg + k * C::JS;
+            const int64_t m = ldm(j);
+            const int e = lde(j);
+            if (m > -lim && m < lim) {
+                const int64_t x = m + e;  // |x| < q
+                return x >= 0 ? (uint64_t)x : T.q - (uint64_t)(-x);
+            }
+            return slow(m, e);
+        };
+        ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
+    }
+}
+
 // Forward transform of a poly-limb already staged in shared memory (u64
 // residues): each CTA's share at its own padded local positions, complete
 // (__syncthreads, or cluster_sync for CL = 2) before the call.  The first
 // pass reads it with the half chosen at compile time, so no per-element
 // address selection.
-template <int LOGN, int CL = ntt_default_cl(LOGN), bool FPOK = true, class St>
+// DBL: for limbs in an FP64 mode the staged words are the bits of exact
+// integer-valued doubles (|x| < 2^52) instead of u64 residues.
+template <int LOGN, int CL = ntt_default_cl(LOGN), bool FPOK = true, bool DBL = false, class St>
 __device__ __forceinline__ void ntt_forward_from_smem(uint64_t* sm, const LimbTab& T, St st) {
     using C = NttCfg<LOGN, CL>;
     if constexpr (CL == 2) {
@@ -562,16 +612,28 @@ __device__ __forceinline__ void ntt_forward_from_smem(uint64_t* sm, const LimbTa
         const uint64_t* s0 = cluster_smem(sm, pair_base()) + pad(sg0);
         const uint64_t* s1 = cluster_smem(sm, pair_base() + 1) + pad(sg0);
         auto first = [&](int k, int) { return (k < C::E / 2 ? s0 : s1)[xoff<LOGN, CL>(k & (C::E / 2 - 1))]; };
-        if (FPOK && T.fp)
-            ntt_forward_fp<LOGN, CL>(sm, T, first, st);
-        else
+        if (FPOK && T.fp) {
+            if constexpr (DBL) {
+                auto firstd = [&](int k, int sg) { return vfrom<double>(first(k, sg)); };
+                ntt_forward_fp<LOGN, CL>(sm, T, firstd, st);
+            } else {
+                ntt_forward_fp<LOGN, CL>(sm, T, first, st);
+            }
+        } else {
             ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
+        }
     } else {
         auto first = [&](int k, int sg) { return sm[pad(sg + k * C::JS)]; };
-        if (FPOK && T.fp)
-            ntt_forward_fp<LOGN, CL>(sm, T, first, st);
-        else
+        if (FPOK && T.fp) {
+            if constexpr (DBL) {
+                auto firstd = [&](int k, int sg) { return vfrom<double>(first(k, sg)); };
+                ntt_forward_fp<LOGN, CL>(sm, T, firstd, st);
+            } else {
+                ntt_forward_fp<LOGN, CL>(sm, T, first, st);
+            }
+        } else {
             ntt_forward_core<LOGN, kModeInt, CL>(sm, T, first, st);
+        }
     }
 }
 

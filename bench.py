@@ -33,11 +33,46 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+NCCL_LOG_DIR = None
 if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-    # NCCL's init lines name every rank's communicator size; set before torch
-    # loads NCCL, which reads these once
+    # NCCL's init lines name every rank's communicator size.  They go to one
+    # file per process in a folder named for the launching torchrun agent (the
+    # ranks' common parent), not to stdout, whose last line is the JSON
+    # result; rank 0 reads the sizes back into that line.  Set before torch
+    # loads NCCL, which reads these once.
+    import tempfile
+    NCCL_LOG_DIR = os.path.join(tempfile.gettempdir(),
+                                f"provenloop_nccl_{os.getppid()}_{os.environ.get('MASTER_PORT', '0')}")
+    os.makedirs(NCCL_LOG_DIR, exist_ok=True)
     os.environ["NCCL_DEBUG"] = "INFO"
     os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+    os.environ["NCCL_DEBUG_FILE"] = os.path.join(NCCL_LOG_DIR, "nccl.%h.%p.log")
+
+
+def drop_nccl_logs():
+    """Removes this launch's NCCL log folder (rank 0, after the result line;
+    the other ranks' open log files stay writable until they exit)."""
+    if NCCL_LOG_DIR is not None:
+        import shutil
+        shutil.rmtree(NCCL_LOG_DIR, ignore_errors=True)
+
+
+def nccl_comm_sizes():
+    """(rank, nRanks) pairs from the NCCL init lines of every process of this
+    launch, read from NCCL_LOG_DIR; None outside torchrun."""
+    import re
+    if NCCL_LOG_DIR is None or not os.path.isdir(NCCL_LOG_DIR):
+        return None
+    seen = set()
+    for f in sorted(os.listdir(NCCL_LOG_DIR)):
+        try:
+            with open(os.path.join(NCCL_LOG_DIR, f), errors="replace") as fh:
+                for m in re.finditer(r" rank (\d+) nRanks (\d+) ", fh.read()):
+                    seen.add((int(m.group(1)), int(m.group(2))))
+        except OSError:
+            continue
+    return {"ranks_reporting": sorted(r for r, _ in seen), "nRanks": sorted({n for _, n in seen}),
+            "log_dir": NCCL_LOG_DIR}
 
 N_POLY, D, R = 16384, 1536, 16
 METRIC = "encrypted LoRA deltas/sec (CKKS N=16384, d=1536, r=16, ZeRo-MOAI)"
@@ -97,7 +132,13 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons during the timed region."""
+    """nvidia-smi clocks / throttle reasons during the timed region.
+
+    nvidia-smi's start-up touches every GPU of the node and stalls work
+    running on them for tens of milliseconds (up to 130 ms measured on an
+    8-GPU box).  So every rank starts its sampler, and waits for its first
+    samples, before the barrier that opens the timed region: no rank's start-up
+    then falls inside another rank's timed steps."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -108,17 +149,19 @@ class ClockSampler:
         self.proc = None
         self.lines = []
 
-    def start(self):
+    def start(self, samples: int = 2):
+        """Starts sampling every 100 ms; returns after `samples` samples (or
+        5 s), so that the start-up is over before the timed region, and drops
+        those samples (taken on an idle GPU)."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
                  "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
-            # nvidia-smi takes a moment to start: wait for its first sample so
-            # the samples cover the timed region that follows
             t0 = time.time()
-            while not self.lines and time.time() - t0 < 5.0:
+            while len(self.lines) < samples and time.time() - t0 < 5.0:
                 time.sleep(0.02)
+            self.lines.clear()
         except Exception:
             self.proc = None
 
@@ -129,6 +172,9 @@ class ClockSampler:
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 0.3:   # a timed region shorter than the period
+            time.sleep(0.01)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -501,12 +547,12 @@ def run_ours(args):
     for i in range(args.warmup):
         step(i, last=i == args.warmup - 1)
     torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
     # ---- timed region
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    clocks = ClockSampler(local)
-    clocks.start()
     launches0 = _lib.launch_count()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     for k in range(args.steps):
@@ -638,6 +684,7 @@ def run_ours(args):
         if world > 1:
             line["gather_ms_per_step_unoverlapped"] = gather_ms
             line["kernel_ms_per_step_sum"] = sum(v[0] for v in kern.values()) / args.steps
+            line["nccl_comm"] = nccl_comm_sizes()
         if micro:
             line["ntt_c2"] = micro
         if c3:
@@ -647,9 +694,9 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-        time.sleep(1.0)   # the other ranks' NCCL teardown lines come first; the JSON line is the last
     if rank == 0:
         print(json.dumps(line), flush=True)
+        drop_nccl_logs()
 
 
 def ctx_sms(dev):
@@ -774,11 +821,11 @@ def c4_leg(args, dev, world, rank, local, steps, warmup, print_line):
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    clocks = ClockSampler(local)
-    clocks.start()
     launches0 = _lib.launch_count()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     for k in range(steps):
@@ -880,10 +927,12 @@ def run_c4(args):
     out = c4_leg(args, torch.device("cuda", local), world, rank, local, args.steps, args.warmup, print_line=False)
     if world > 1:
         dist.barrier()
+        if rank == 0:
+            out["nccl_comm"] = nccl_comm_sizes()
         dist.destroy_process_group()
-        time.sleep(1.0)
     if rank == 0:
         print(json.dumps(out), flush=True)
+        drop_nccl_logs()
 
 
 def run_c5(args):
@@ -905,6 +954,8 @@ def run_c5(args):
     launches0 = _lib.launch_count()
     clocks = ClockSampler(local)
     clocks.start()
+    if world > 1:
+        dist.barrier()
     pts = sweep.run(args.steps, args.warmup, peak_gbs=peak, device=local)
     clk = clocks.stop()
     head = next(p for p in pts if (p["n"], p["batch"], p["d"], p["r"]) == (16384, 4096, 1536, 16))
@@ -921,16 +972,21 @@ def run_c5(args):
             "peak_gbs": peak, "peak_kind": peak_kind, "clocks": clk,
             "gpu_launches": _lib.launch_count() - launches0, "points": pts,
         }
+        if world > 1:
+            line["nccl_comm"] = nccl_comm_sizes()
         print(json.dumps(line))
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if rank == 0:
+        drop_nccl_logs()
 
 
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        drop_nccl_logs()   # no process group on this arm: nothing was logged
     elif args.config == "c4":
         run_c4(args)
     elif args.config == "c5":

@@ -33,46 +33,41 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
-NCCL_LOG_DIR = None
 if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-    # NCCL's init lines name every rank's communicator size.  They go to one
-    # file per process in a folder named for the launching torchrun agent (the
-    # ranks' common parent), not to stdout, whose last line is the JSON
-    # result; rank 0 reads the sizes back into that line.  Set before torch
-    # loads NCCL, which reads these once.
-    import tempfile
-    NCCL_LOG_DIR = os.path.join(tempfile.gettempdir(),
-                                f"provenloop_nccl_{os.getppid()}_{os.environ.get('MASTER_PORT', '0')}")
-    os.makedirs(NCCL_LOG_DIR, exist_ok=True)
+    # NCCL's init lines name every rank's communicator size; set before torch
+    # loads NCCL, which reads these once
     os.environ["NCCL_DEBUG"] = "INFO"
     os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
-    os.environ["NCCL_DEBUG_FILE"] = os.path.join(NCCL_LOG_DIR, "nccl.%h.%p.log")
+
+_RESULT_FD = None
 
 
-def drop_nccl_logs():
-    """Removes this launch's NCCL log folder (rank 0, after the result line;
-    the other ranks' open log files stay writable until they exit)."""
-    if NCCL_LOG_DIR is not None:
-        import shutil
-        shutil.rmtree(NCCL_LOG_DIR, ignore_errors=True)
+def quiet_stdout():
+    """Points this process's stdout at stderr from here on and keeps the
+    original stdout for the result line.  Every rank calls it before the last
+    barrier: the lines NCCL prints at teardown then go to stderr, and the JSON
+    result stays the last line of stdout."""
+    global _RESULT_FD
+    import ctypes
+    sys.stdout.flush()
+    try:
+        ctypes.CDLL(None).fflush(None)   # C-level buffers (NCCL's log) first
+    except (OSError, AttributeError):
+        pass
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
 
 
-def nccl_comm_sizes():
-    """(rank, nRanks) pairs from the NCCL init lines of every process of this
-    launch, read from NCCL_LOG_DIR; None outside torchrun."""
-    import re
-    if NCCL_LOG_DIR is None or not os.path.isdir(NCCL_LOG_DIR):
-        return None
-    seen = set()
-    for f in sorted(os.listdir(NCCL_LOG_DIR)):
-        try:
-            with open(os.path.join(NCCL_LOG_DIR, f), errors="replace") as fh:
-                for m in re.finditer(r" rank (\d+) nRanks (\d+) ", fh.read()):
-                    seen.add((int(m.group(1)), int(m.group(2))))
-        except OSError:
-            continue
-    return {"ranks_reporting": sorted(r for r, _ in seen), "nRanks": sorted({n for _, n in seen}),
-            "log_dir": NCCL_LOG_DIR}
+def emit(line):
+    """Prints the JSON result line on the original stdout."""
+    text = json.dumps(line)
+    if _RESULT_FD is None:
+        print(text, flush=True)
+        return
+    data = (text + "\n").encode()
+    while data:
+        data = data[os.write(_RESULT_FD, data):]
+
 
 N_POLY, D, R = 16384, 1536, 16
 METRIC = "encrypted LoRA deltas/sec (CKKS N=16384, d=1536, r=16, ZeRo-MOAI)"
@@ -684,7 +679,6 @@ def run_ours(args):
         if world > 1:
             line["gather_ms_per_step_unoverlapped"] = gather_ms
             line["kernel_ms_per_step_sum"] = sum(v[0] for v in kern.values()) / args.steps
-            line["nccl_comm"] = nccl_comm_sizes()
         if micro:
             line["ntt_c2"] = micro
         if c3:
@@ -692,11 +686,11 @@ def run_ours(args):
         if c4:
             line["c4"] = c4
     if world > 1:
+        quiet_stdout()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(line), flush=True)
-        drop_nccl_logs()
+        emit(line)
 
 
 def ctx_sms(dev):
@@ -926,13 +920,11 @@ def run_c4(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     out = c4_leg(args, torch.device("cuda", local), world, rank, local, args.steps, args.warmup, print_line=False)
     if world > 1:
+        quiet_stdout()
         dist.barrier()
-        if rank == 0:
-            out["nccl_comm"] = nccl_comm_sizes()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(out), flush=True)
-        drop_nccl_logs()
+        emit(out)
 
 
 def run_c5(args):
@@ -972,21 +964,18 @@ def run_c5(args):
             "peak_gbs": peak, "peak_kind": peak_kind, "clocks": clk,
             "gpu_launches": _lib.launch_count() - launches0, "points": pts,
         }
-        if world > 1:
-            line["nccl_comm"] = nccl_comm_sizes()
-        print(json.dumps(line))
     if world > 1:
+        quiet_stdout()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        drop_nccl_logs()
+        emit(line)
 
 
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
-        drop_nccl_logs()   # no process group on this arm: nothing was logged
     elif args.config == "c4":
         run_c4(args)
     elif args.config == "c5":

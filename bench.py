@@ -525,7 +525,7 @@ def run_ours(args):
     pending = [None]
 
     def seeds_of(i):
-        return np.asarray([multigpu.stream_seed(int(u), i, n_users) for u in users], dtype=np.uint64)
+        return multigpu.stream_seeds(users, i, n_users)
 
     def step(i, last=False):
         b = i & 1
@@ -614,26 +614,58 @@ def run_ours(args):
             lora.delta(sk, hv, seeds_of(1000 + k), out=dv, want_inter=False)   # H2D, GPU pipeline, D2H, sync
             e2e_ms += (time.perf_counter() - t0) * 1000.0
     else:
-        # each rank: its users' hidden states from pinned host memory, the
-        # pipeline, fp32 deltas gathered to rank 0 over NCCL, rank 0 copies
-        # every rank's deltas to pinned host memory
-        g_pin = torch.empty((world * batch, D), dtype=torch.float32).pin_memory() if rank == 0 else None
+        # each rank streams its users' steps the way a serving loop would:
+        # step k's hidden states go host -> device on a copy stream while
+        # step k-1 computes, the fp32 deltas are gathered to rank 0 over NCCL,
+        # and rank 0 copies every rank's deltas to pinned host memory on a
+        # second copy stream while step k+1 computes.  Every step's copies
+        # are inside the wall-clock region, which ends when the last step's
+        # deltas are in host memory.
+        s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        h_in = [torch.empty_like(h_dev) for _ in range(2)]
+        g_pin = ([torch.empty((world * batch, D), dtype=torch.float32).pin_memory() for _ in range(2)]
+                 if rank == 0 else None)
         d2h = world * batch * D * 4 if rank == 0 else 0
-        for k in range(args.steps + 1):
-            flush.zero_()
+        ev_in = [torch.cuda.Event() for _ in range(2)]     # h_in[b] holds step k's inputs
+        ev_read = [torch.cuda.Event() for _ in range(2)]   # step k's kernels are done with h_in[b]
+        ev_out = [torch.cuda.Event() for _ in range(2)]    # step k's deltas have left recv[b]
+        work = [None, None]
+
+        def e2e_steps(k0, nsteps):
+            for k in range(k0, k0 + nsteps):
+                b = k & 1
+                with torch.cuda.stream(s_in):
+                    s_in.wait_event(ev_read[b])
+                    h_in[b].copy_(h_pin, non_blocking=True)
+                    ev_in[b].record(s_in)
+                stream.wait_event(ev_in[b])
+                flush.zero_()
+                if work[b] is not None:
+                    work[b].wait()                     # step k-2's gather is done with d32[b] and recv[b]
+                lora.delta_device(sk, h_in[b], seeds_of(1000 + k), delta_dev[b])
+                ev_read[b].record(stream)
+                d32[b].copy_(delta_dev[b])
+                if rank == 0:
+                    stream.wait_event(ev_out[b])       # step k-2's deltas have been copied out
+                work[b] = dist.gather(d32[b], gather_list=recv[b], dst=0, async_op=True)
+                if rank == 0:
+                    with torch.cuda.stream(s_out):
+                        work[b].wait()
+                        for r_ in range(world):
+                            g_pin[b][r_ * batch:(r_ + 1) * batch].copy_(recv[b][r_], non_blocking=True)
+                        ev_out[b].record(s_out)
+            for b in range(2):
+                if work[b] is not None:
+                    work[b].wait()
+                    work[b] = None
             torch.cuda.synchronize(dev)
-            dist.barrier()
-            t0 = time.perf_counter()
-            h_dev.copy_(h_pin, non_blocking=True)
-            lora.delta_device(sk, h_dev, seeds_of(1000 + k), delta_dev[0])
-            d32[0].copy_(delta_dev[0])
-            dist.gather(d32[0], gather_list=recv[0], dst=0)
-            if rank == 0:
-                for r_ in range(world):
-                    g_pin[r_ * batch:(r_ + 1) * batch].copy_(recv[0][r_], non_blocking=True)
-            torch.cuda.synchronize(dev)
-            if k > 0:                                   # the first pass warms the path
-                e2e_ms += (time.perf_counter() - t0) * 1000.0
+
+        e2e_steps(0, 2)                                  # warms the path (untimed)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        e2e_steps(2, args.steps)
+        e2e_ms = (time.perf_counter() - t0) * 1000.0
     t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -806,7 +838,7 @@ def c4_leg(args, dev, world, rank, local, steps, warmup, print_line):
     gid = (u0 + user_ix.astype(np.int64)) * C4_ADAPTERS + adapter   # global delta id
 
     def step(i):
-        seeds = np.asarray([multigpu.stream_seed(int(g), i, C4_USERS * C4_ADAPTERS) for g in gid], dtype=np.uint64)
+        seeds = multigpu.stream_seeds(gid, i, C4_USERS * C4_ADAPTERS)
         lora.delta_device(sk, h_dev, seeds, delta_dev, expert=adapter, sk_index=user_ix)
         if world > 1:
             d32[:batch].copy_(delta_dev)
@@ -866,7 +898,7 @@ def c4_leg(args, dev, world, rank, local, steps, warmup, print_line):
         if world > 1:
             dist.barrier()
         t0 = time.perf_counter()
-        seeds = np.asarray([multigpu.stream_seed(int(g), 999 + k, total) for g in gid], dtype=np.uint64)
+        seeds = multigpu.stream_seeds(gid, 999 + k, total)
         if world == 1:
             lora.delta(sk, h_pin.numpy(), seeds, expert=adapter, sk_index=user_ix, out=d_pin.numpy(),
                        want_inter=False)

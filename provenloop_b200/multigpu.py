@@ -27,6 +27,15 @@ def stream_seed(user: int, step: int, n_users: int, seed0: int = 1) -> int:
     return seed0 + step * n_users + user
 
 
+def stream_seeds(users, step: int, n_users: int, seed0: int = 1):
+    """stream_seed for an array of users at once (uint64; the per-call cost of
+    a whole batch is one vector operation, not a Python loop per user)."""
+    import numpy as np
+
+    u = np.asarray(users, dtype=np.uint64)
+    return u + np.uint64(seed0 + step * n_users)
+
+
 def gather_rows(rows, world: int, rank: int, dst: int = 0):
     """Gather each rank's [n_local, d] tensor to `dst` (torch.distributed;
     NCCL for CUDA tensors, gloo on CPU).  All ranks must hold the same

@@ -121,8 +121,7 @@ def run(steps: int = 3, warmup: int = 3, points=None, peak_gbs: float = 6650.0, 
                 users = np.arange(rank * batch, (rank + 1) * batch, dtype=np.uint64)
 
                 def step(i):
-                    seeds = np.asarray([multigpu.stream_seed(int(u), i, world * batch) for u in users],
-                                       dtype=np.uint64)
+                    seeds = multigpu.stream_seeds(users, i, world * batch)
                     lora.delta_device(sk, h_dev, seeds, delta_dev)
 
                 for i in range(warmup):

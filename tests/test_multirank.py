@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch.multiprocessing as mp
 
-from provenloop_b200.multigpu import gather_rows, stream_seed, user_block
+from provenloop_b200.multigpu import gather_rows, stream_seed, stream_seeds, user_block
 
 
 def test_user_blocks_partition_everything():
@@ -28,6 +28,9 @@ def test_stream_seeds_unique_and_rank_independent():
     assert len(s) == 5 * n
     # the owner rank does not enter the seed
     assert stream_seed(17, 3, n) == 1 + 3 * n + 17
+    users = np.arange(5, 40, dtype=np.uint64)
+    v = stream_seeds(users, 3, n)
+    assert v.dtype == np.uint64 and v.tolist() == [stream_seed(int(u), 3, n) for u in users]
 
 
 def _free_port():

@@ -15,6 +15,55 @@ namespace tsg {
 constexpr int kEncPlanRound = 4096;
 constexpr size_t kEncPlanWinBytes = (2 * kEncPlanRound + 16) * 4;
 
+// Staging of c1 = NTT(a)'s input in the speculative pass: this CTA's share
+// of limb `limb`'s candidates (h0 .. h0 + H - 1, 8 per ChaCha20 block) into
+// shared memory.  Returns whether any of them fell in the rejection zone.
+template <int LOGN, int CLX, int MINB>
+__device__ __forceinline__ bool enc_a_stage(uint64_t* sm, uint64_t seed, const LimbTab& T, int limb, int h0, int tid) {
+    using C = NttCfg<LOGN, CLX>;
+    constexpr int N = 1 << LOGN, NT = C::NT, H = C::H;
+    // the throughput form (CTA pairs, two per SM) stages FP64 limbs' draws as
+    // exact doubles; the repair and small-batch forms stage residues
+    constexpr bool kDblStage = MINB == 2 && kPairFp<LOGN, CLX, MINB>;
+    // this CTA's share: candidates h0 .. h0 + H - 1, 8 per block
+    const uint32_t blk0 = (uint32_t)limb * (N / 8);
+    bool rej = false;
+    if (kDblStage && T.fp) {  // (kDblStage: every staged FP64-limb word is a double)
+        // FP64 limb: u = hi 2^32 + lo = hi (2^32 mod q) + lo (mod q),
+        // staged as the exact double fp_mulmod(hi, 2^32 mod q) + lo
+        // (|x| <= q + 2^32), which the transform's input reduction
+        // takes like the residue; the IMAD pipe is the busier one here
+        const double q = __ull2double_rn(T.q);
+        const uint64_t r = ((uint64_t)1 << 32) % T.q;
+        const double r32 = r > T.q / 2 ? -__ull2double_rn(T.q - r) : __ull2double_rn(r);
+        const double r32q = __ddiv_rn(r32, q);
+        for (int b = h0 / 8 + tid; b < (h0 + H) / 8; b += NT) {
+            uint32_t w[16];
+            chacha_block(seed, blk0 + (uint32_t)b, w);
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
+                rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
+                const double x = __dadd_rn(fp_mulmod(__uint2double_rn(w[2 * c + 1]), r32, r32q, q),
+                                           __uint2double_rn(w[2 * c]));
+                sm[pad(8 * b + c - h0)] = vbits(x);
+            }
+        }
+    } else {
+        for (int b = h0 / 8 + tid; b < (h0 + H) / 8; b += NT) {
+            uint32_t w[16];
+            chacha_block(seed, blk0 + (uint32_t)b, w);
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
+                rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
+                sm[pad(8 * b + c - h0)] = mod_u64(u, T.q, T.mu64);
+            }
+        }
+    }
+    return rej;
+}
+
 // Two single-transform kernels (each fits in registers):
 //   k_enc_a: c1 = NTT(a), a = range_u64(q_l) draws (sampling.rs:62-64);
 //   k_enc_u: c0 = NTT(m + e mod q_l) - c1 * s.
@@ -43,43 +92,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
         const uint64_t seed = seeds[v];
         uint64_t* c1 = ct + (((size_t)v * 2 * L + L + limb) << LOGN);
         if (!plan_mode) {
-            // this CTA's share: candidates h0 .. h0 + H - 1, 8 per block
-            const uint32_t blk0 = (uint32_t)limb * (N / 8);
-            bool rej = false;
-            if (kDblStage && T.fp) {  // (kDblStage: every staged FP64-limb word is a double)
-                // FP64 limb: u = hi 2^32 + lo = hi (2^32 mod q) + lo (mod q),
-                // staged as the exact double fp_mulmod(hi, 2^32 mod q) + lo
-                // (|x| <= q + 2^32), which the transform's input reduction
-                // takes like the residue; the IMAD pipe is the busier one here
-                const double q = __ull2double_rn(T.q);
-                const uint64_t r = ((uint64_t)1 << 32) % T.q;
-                const double r32 = r > T.q / 2 ? -__ull2double_rn(T.q - r) : __ull2double_rn(r);
-                const double r32q = __ddiv_rn(r32, q);
-                for (int b = h0 / 8 + tid; b < (h0 + H) / 8; b += NT) {
-                    uint32_t w[16];
-                    chacha_block(seed, blk0 + (uint32_t)b, w);
-#pragma unroll
-                    for (int c = 0; c < 8; c++) {
-                        const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
-                        rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
-                        const double x = __dadd_rn(fp_mulmod(__uint2double_rn(w[2 * c + 1]), r32, r32q, q),
-                                                   __uint2double_rn(w[2 * c]));
-                        sm[pad(8 * b + c - h0)] = vbits(x);
-                    }
-                }
-            } else {
-                for (int b = h0 / 8 + tid; b < (h0 + H) / 8; b += NT) {
-                    uint32_t w[16];
-                    chacha_block(seed, blk0 + (uint32_t)b, w);
-#pragma unroll
-                    for (int c = 0; c < 8; c++) {
-                        const uint64_t u = (uint64_t)w[2 * c] | ((uint64_t)w[2 * c + 1] << 32);
-                        rej |= (u < T.thresh);  // range_u64 rejection zone [0, 2^64 mod q)
-                        sm[pad(8 * b + c - h0)] = mod_u64(u, T.q, T.mu64);
-                    }
-                }
-            }
-            if (rej) flag_stream(flags, nvec, v);
+            if (enc_a_stage<LOGN, CLX, MINB>(sm, seed, T, limb, h0, tid)) flag_stream(flags, nvec, v);
         } else {
             // exact plan: candidates 0 .. N + nrej - 1 of this limb's segment
             // at words off + 2*cidx; the rejected ones are skipped and
@@ -159,6 +172,69 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
     }
 }
 
+// Both transforms of a (ciphertext, limb) on one CTA pair, one after the
+// other (the throughput form: CTA pairs, two CTAs per SM).  c1 = NTT(a) is
+// stored, and t = c1*s goes to c0's place; then c0 = NTT(m + e) - t.  Every
+// forward transform stores element h*H + tid + k*NT from thread tid, so each
+// thread reads back only the t it wrote itself, one transform later, while
+// it is still in L2: the c1 round trip through HBM that k_enc_a + k_enc_u
+// make is gone.  c1 and the final c0 are streaming stores (evicted first).
+// A stream that met a rejection is flagged and redone by the repair pass
+// (k_enc_a's plan mode, then k_enc_u's list mode, which reads c1).
+// Phase 1 of k_enc_fused: c1 = NTT(a) stored, t = c1*s into c0's place.
+// Out of line, like phase 2, so each transform is register-allocated alone.
+template <int LOGN>
+__device__ __noinline__ void enc_fused_c1(uint64_t* sm, uint64_t seed, const LimbTab* __restrict__ tabs, int limb,
+                                          uint64_t* c0, uint64_t* c1, const uint64_t* __restrict__ s,
+                                          const uint64_t* __restrict__ sp, uint32_t* flags, int nvec, int v) {
+    using C = NttCfg<LOGN, 2>;
+    constexpr bool kFp = kPairFp<LOGN, 2, 2>;  // and FP64 limbs' draws staged as doubles
+    const LimbTab T = tabs[limb];
+    const int h0 = ntt_rank<LOGN, 2>() * C::H;
+    if (enc_a_stage<LOGN, 2, 2>(sm, seed, T, limb, h0, (int)threadIdx.x)) flag_stream(flags, nvec, v);
+    cluster_sync();  // the transform reads both shares
+    ntt_forward_from_smem<LOGN, 2, kFp, kFp>(sm, T, [&](int j, uint64_t x) {
+        __stcs(reinterpret_cast<unsigned long long*>(c1 + j), (unsigned long long)x);
+        c0[j] = mul_shoup4(x, s[j], sp[j], T.q);  // t, in [0, 4q)
+    });
+}
+
+// Phase 2 of k_enc_fused: c0 = NTT(m + e) - t.
+template <int LOGN>
+__device__ __noinline__ void enc_fused_c0(uint64_t* sm, const LimbTab* __restrict__ tabs, int limb, uint64_t* c0,
+                                          const int64_t* __restrict__ mv, const int8_t* __restrict__ ev) {
+    constexpr bool kFp = kPairFp<LOGN, 2, 2>;
+    const LimbTab T = tabs[limb];
+    ntt_forward_signed<LOGN, 2, kFp>(
+        sm, T, [&](int j) { return mv[j]; }, [&](int j) { return (int)ev[j]; },
+        [&](int j, uint64_t x) {
+            // x - t with t in [0, 4q): x + 4q - t lies in [1, 5q)
+            const uint64_t t = __ldcs(reinterpret_cast<const unsigned long long*>(c0 + j));
+            __stcs(reinterpret_cast<unsigned long long*>(c0 + j), (unsigned long long)canon8(x + 4 * T.q - t, T.q));
+        });
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
+    k_enc_fused(uint64_t* __restrict__ ct, const uint64_t* __restrict__ seeds, const int64_t* __restrict__ m,
+                const int8_t* __restrict__ e, const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks,
+                const int* __restrict__ sk_of, const LimbTab* __restrict__ tabs, int L, int nvec, uint32_t* flags) {
+    extern __shared__ __align__(16) uint64_t sm[];
+    using C = NttCfg<LOGN, 2>;
+    const int limb = blockIdx.x / C::CL, v = blockIdx.y;
+    uint64_t* c0 = ct + (((size_t)v * 2 * L + limb) << LOGN);
+    uint64_t* c1 = c0 + ((size_t)L << LOGN);
+    const size_t so = ((size_t)(sk_of ? sk_of[v] : 0) * L + limb) << LOGN;
+    if (threadIdx.x == 0) {  // phase 2's inputs (this CTA's half of the m and e rows) into L2 meanwhile
+        const size_t o = ((size_t)v << LOGN) + (size_t)ntt_rank<LOGN, 2>() * C::H;
+        prefetch_l2(m + o, (uint32_t)C::H * 8u);
+        prefetch_l2(e + o, (uint32_t)C::H);
+    }
+    enc_fused_c1<LOGN>(sm, seeds[v], tabs, limb, c0, c1, sk + so, sks + so, flags, nvec, v);
+    __syncthreads();
+    enc_fused_c0<LOGN>(sm, tabs, limb, c0, m + ((size_t)v << LOGN), e + ((size_t)v << LOGN));
+}
+
 // c0 -= c1*s over every limb of nvec ciphertexts, c0 holding NTT(m + e)
 // (the second half of k_enc_u when the two transforms ran concurrently).
 __global__ void k_enc_combine(uint64_t* __restrict__ ct, const uint64_t* __restrict__ sk,
@@ -194,19 +270,11 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
             // butterflies
             if (!plan_mode) {
                 constexpr size_t smem2 = (size_t)NttCfg<LP, 2>::SMEM_WORDS * 8;
-                cudaError_t er = ensure_smem(k_enc_a<LP, 2, 2>, smem2);
+                cudaError_t er = ensure_smem(k_enc_fused<LP>, smem2);
                 if (er != cudaSuccess) return er;
-                er = ensure_smem(k_enc_u<LP, 2, 2>, smem2);
-                if (er != cudaSuccess) return er;
-                {
-                    KScope ks("enc_a", s);
-                    er = launch_cl(2, k_enc_a<LP, 2, 2>, dim3(c.L * 2, nvec), NttCfg<LP, 2>::NT, smem2, s, ct, seeds,
-                                   c.tabs, c.L, nvec, flags, plans, 0);
-                    if (er != cudaSuccess) return er;
-                }
-                KScope ks("enc_u", s);
-                return launch_cl(2, k_enc_u<LP, 2, 2>, dim3(c.L * 2, nvec), NttCfg<LP, 2>::NT, smem2, s, ct, m, e, sk,
-                                 sks, sk_of, c.tabs, c.L, nvec, (const uint32_t*)flags, 0, 1);
+                KScope ks("enc_fused", s);
+                return launch_cl(2, k_enc_fused<LP>, dim3(c.L * 2, nvec), NttCfg<LP, 2>::NT, smem2, s, ct, seeds, m, e,
+                                 sk, sks, sk_of, c.tabs, c.L, nvec, flags);
             }
         }
         const size_t smem_a = plan_mode ? smem + kEncPlanWinBytes : smem;

@@ -224,7 +224,7 @@ def latency(batch=1, reps=50, rank=32, device=0):
             lora_delta_graphable(lora, sk, h, seeds, d, expert_dev=ex, inter_dev=inter)
         stream.synchronize()
         _lib.profile_enable(False)
-    names = ("prefetch_l2", "gauss_gen", "encode", "enc_a", "enc_x", "enc_combine", "enc_u", "plan", "gauss_fix",
+    names = ("prefetch_l2", "gauss_gen", "encode", "enc_fused", "enc_a", "enc_x", "enc_combine", "enc_u", "plan", "gauss_fix",
              "enc_a_fix", "enc_u_fix", "dec_fused", "decrypt_limb", "crt_seg", "gather_inter", "bmat",
              "warm_decrypt_limb", "warm_crt_seg")
 

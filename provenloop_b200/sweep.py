@@ -28,7 +28,7 @@ BATCHES = (1, 16, 256, 4096)
 DS = (1536, 3584)
 RS = (8, 16, 32, 64)
 
-KERNELS = ("encode", "encode_a", "encode_b", "gauss_gen", "enc_a", "enc_u", "enc_x", "enc_combine", "plan",
+KERNELS = ("encode", "encode_a", "encode_b", "gauss_gen", "enc_fused", "enc_a", "enc_u", "enc_x", "enc_combine", "plan",
            "gauss_fix", "enc_a_fix", "enc_u_fix", "dec_limb1", "dec_fused", "decrypt_limb", "crt_seg", "decode_a", "decode_b",
            "gather_inter", "bmat")
 
@@ -43,6 +43,7 @@ def kernel_bytes_per_delta(name: str, n: int, L: int, nb: int, cols: int, d: int
     gauss_gen     e out (N)
     enc_a         c1 out (8NL)
     enc_u         per limb: m, e, s, c1 in, c0 out (33N)
+    enc_fused     per limb: m, e, s in, c1 and c0 out (33N; N = 8192, 16384)
     enc_x         per limb: m, e in, c0 out (17N)
     enc_combine   per limb: c0, c1, s in, c0 out (32N)
     dec_limb1     (N = 8192, 16384) ct limbs 0-1 and s limbs 0-1 in, the u
@@ -66,6 +67,7 @@ def kernel_bytes_per_delta(name: str, n: int, L: int, nb: int, cols: int, d: int
         "gauss_gen": n,
         "enc_a": 8 * n * L,
         "enc_u": 33 * n * L,
+        "enc_fused": 33 * n * L,
         "enc_x": 17 * n * L,
         "enc_combine": 32 * n * L,
         "dec_limb1": 8 * n * (8 + 2 * nb),

@@ -183,27 +183,30 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
 // (k_enc_a's plan mode, then k_enc_u's list mode, which reads c1).
 // Phase 1 of k_enc_fused: c1 = NTT(a) stored, t = c1*s into c0's place.
 // Out of line, like phase 2, so each transform is register-allocated alone.
-template <int LOGN>
+// MINB: CTAs per SM (2 up to N = 16384, where the FP64 limbs' draws are
+// staged as doubles; 1 at N = 32768, whose shares fill an SM's shared memory).
+template <int LOGN, int MINB>
 __device__ __noinline__ void enc_fused_c1(uint64_t* sm, uint64_t seed, const LimbTab* __restrict__ tabs, int limb,
                                           uint64_t* c0, uint64_t* c1, const uint64_t* __restrict__ s,
                                           const uint64_t* __restrict__ sp, uint32_t* flags, int nvec, int v) {
     using C = NttCfg<LOGN, 2>;
-    constexpr bool kFp = kPairFp<LOGN, 2, 2>;  // and FP64 limbs' draws staged as doubles
+    constexpr bool kFp = kPairFp<LOGN, 2, MINB>;
+    constexpr bool kDbl = MINB == 2 && kFp;  // FP64 limbs' draws staged as doubles (as enc_a_stage does)
     const LimbTab T = tabs[limb];
     const int h0 = ntt_rank<LOGN, 2>() * C::H;
-    if (enc_a_stage<LOGN, 2, 2>(sm, seed, T, limb, h0, (int)threadIdx.x)) flag_stream(flags, nvec, v);
+    if (enc_a_stage<LOGN, 2, MINB>(sm, seed, T, limb, h0, (int)threadIdx.x)) flag_stream(flags, nvec, v);
     cluster_sync();  // the transform reads both shares
-    ntt_forward_from_smem<LOGN, 2, kFp, kFp>(sm, T, [&](int j, uint64_t x) {
+    ntt_forward_from_smem<LOGN, 2, kFp, kDbl>(sm, T, [&](int j, uint64_t x) {
         __stcs(reinterpret_cast<unsigned long long*>(c1 + j), (unsigned long long)x);
         c0[j] = mul_shoup4(x, s[j], sp[j], T.q);  // t, in [0, 4q)
     });
 }
 
 // Phase 2 of k_enc_fused: c0 = NTT(m + e) - t.
-template <int LOGN>
+template <int LOGN, int MINB>
 __device__ __noinline__ void enc_fused_c0(uint64_t* sm, const LimbTab* __restrict__ tabs, int limb, uint64_t* c0,
                                           const int64_t* __restrict__ mv, const int8_t* __restrict__ ev) {
-    constexpr bool kFp = kPairFp<LOGN, 2, 2>;
+    constexpr bool kFp = kPairFp<LOGN, 2, MINB>;
     const LimbTab T = tabs[limb];
     ntt_forward_signed<LOGN, 2, kFp>(
         sm, T, [&](int j) { return mv[j]; }, [&](int j) { return (int)ev[j]; },
@@ -214,8 +217,8 @@ __device__ __noinline__ void enc_fused_c0(uint64_t* sm, const LimbTab* __restric
         });
 }
 
-template <int LOGN>
-__global__ void __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
+template <int LOGN, int MINB>
+__global__ void __launch_bounds__(NttCfg<LOGN, 2>::NT, MINB)
     k_enc_fused(uint64_t* __restrict__ ct, const uint64_t* __restrict__ seeds, const int64_t* __restrict__ m,
                 const int8_t* __restrict__ e, const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks,
                 const int* __restrict__ sk_of, const LimbTab* __restrict__ tabs, int L, int nvec, uint32_t* flags) {
@@ -230,9 +233,9 @@ __global__ void __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
         prefetch_l2(m + o, (uint32_t)C::H * 8u);
         prefetch_l2(e + o, (uint32_t)C::H);
     }
-    enc_fused_c1<LOGN>(sm, seeds[v], tabs, limb, c0, c1, sk + so, sks + so, flags, nvec, v);
+    enc_fused_c1<LOGN, MINB>(sm, seeds[v], tabs, limb, c0, c1, sk + so, sks + so, flags, nvec, v);
     __syncthreads();
-    enc_fused_c0<LOGN>(sm, tabs, limb, c0, m + ((size_t)v << LOGN), e + ((size_t)v << LOGN));
+    enc_fused_c0<LOGN, MINB>(sm, tabs, limb, c0, m + ((size_t)v << LOGN), e + ((size_t)v << LOGN));
 }
 
 // c0 -= c1*s over every limb of nvec ciphertexts, c0 holding NTT(m + e)
@@ -270,12 +273,22 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
             // butterflies
             if (!plan_mode) {
                 constexpr size_t smem2 = (size_t)NttCfg<LP, 2>::SMEM_WORDS * 8;
-                cudaError_t er = ensure_smem(k_enc_fused<LP>, smem2);
+                cudaError_t er = ensure_smem(k_enc_fused<LP, 2>, smem2);
                 if (er != cudaSuccess) return er;
                 KScope ks("enc_fused", s);
-                return launch_cl(2, k_enc_fused<LP>, dim3(c.L * 2, nvec), NttCfg<LP, 2>::NT, smem2, s, ct, seeds, m, e,
-                                 sk, sks, sk_of, c.tabs, c.L, nvec, flags);
+                return launch_cl(2, k_enc_fused<LP, 2>, dim3(c.L * 2, nvec), NttCfg<LP, 2>::NT, smem2, s, ct, seeds,
+                                 m, e, sk, sks, sk_of, c.tabs, c.L, nvec, flags);
             }
+        }
+        if (LG == 15 && !plan_mode) {
+            // N = 32768: the same fused form at one CTA per SM (a pair's
+            // shares fill the shared memory of two SMs)
+            constexpr int L15 = LG == 15 ? LG : 15;
+            cudaError_t er = ensure_smem(k_enc_fused<L15, 1>, smem);
+            if (er != cudaSuccess) return er;
+            KScope ks("enc_fused", s);
+            return launch_cl(2, k_enc_fused<L15, 1>, dim3(c.L * 2, nvec), NttCfg<L15, 2>::NT, smem, s, ct, seeds, m,
+                             e, sk, sks, sk_of, c.tabs, c.L, nvec, flags);
         }
         const size_t smem_a = plan_mode ? smem + kEncPlanWinBytes : smem;
         cudaError_t er = ensure_smem(k_enc_a<LG>, smem + kEncPlanWinBytes);

@@ -414,8 +414,12 @@ __device__ __noinline__ void dec_limb1_batch(uint64_t* sm, const LimbTab* tab, c
         sm, T, [&](int j) { return mul_shoup4(u[j], p[j], pp[j], T.q); }, [&](int j, uint64_t x) { out[j] = x; });
 }
 
+// CTAs per SM of the split decrypt: two up to N = 16384, one at N = 32768
+// (a pair's shares fill two SMs' shared memory).
+constexpr int dec_minb(int logn) { return logn >= 15 ? 1 : 2; }
+
 template <int LOGN>
-__global__ void __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
+__global__ void __launch_bounds__(NttCfg<LOGN, 2>::NT, dec_minb(LOGN))
     k_dec_limb1(uint64_t* __restrict__ M1, uint64_t* __restrict__ U, const uint64_t* __restrict__ cts,
                 long long ct_stride, int ct_limbs, const uint64_t* __restrict__ sk, const uint64_t* __restrict__ sks,
                 const int* __restrict__ sk_of, const uint64_t* __restrict__ pt, const uint64_t* __restrict__ pts,
@@ -450,7 +454,7 @@ __global__ void __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
 }
 
 template <int LOGN, int MAXC, bool FPC>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT, 2)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NttCfg<LOGN, 2>::NT, dec_minb(LOGN))
     k_dec_pair(const uint64_t* __restrict__ M1, const uint64_t* __restrict__ U, const uint64_t* __restrict__ pt,
                const uint64_t* __restrict__ pts, const int* __restrict__ pt_sel, int per_ct,
                const LimbTab* __restrict__ tabs, int L, CrtConst K, double inv_scale, const double* __restrict__ W,
@@ -515,9 +519,10 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
     // spilled 648 bytes and ran 15% slower)
     const bool nc0 = c.q0 < (1ULL << (61 - c.logn)), nc1 = c.q1 < (1ULL << (61 - c.logn));
     TSG_LOGN_SWITCH(c.logn, {
-        // N = 8192, 16384: four-CTA clusters (LQ: other sizes never take it)
-        constexpr int LQ = (LG == 13 || LG == 14) ? LG : 14;
-        if (LG == 13 || LG == 14) {
+        // N = 8192 .. 32768: the split form on CTA pairs (LQ: other sizes
+        // never take it)
+        constexpr int LQ = LG >= 13 ? LG : 14;
+        if (LG >= 13) {
             // split form: limb-1 INTTs to M0 (nvec x N words), then limb 0 + CRT
             constexpr size_t smemq = (size_t)NttCfg<LQ, 2>::SMEM_WORDS * 8;
             cudaError_t er = ensure_smem(k_dec_limb1<LQ>, smemq);
@@ -525,7 +530,7 @@ cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_
             // u rows once per ciphertext where the ciphertexts alone fill two
             // waves of CTA pairs; otherwise batches spread over more pairs
             const int nct = nvec / per_ct;
-            int bpp = nvec / (2 * c.sms);
+            int bpp = nvec / (dec_minb(LG) * c.sms);
             bpp = bpp < 1 ? 1 : (bpp > per_ct ? per_ct : bpp);
             const unsigned pairs = (unsigned)nct * (unsigned)((per_ct + bpp - 1) / bpp);
             {

@@ -1682,13 +1682,14 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
                      // fused decrypt: limb 1 of every vector at N = 8192 / 16384 (split
                      // form; both limbs when the pass is small enough for the per-limb
                      // path), one limb-0 buffer per CTA below; otherwise both limbs of
-                     // every vector (and the FFT scratch of the decode)
+                     // every vector (N = 32768: the per-limb path of small passes, of
+                     // which the split form uses half; and the FFT scratch of the decode)
                      i_M = cv.add(lo->d_w && (c->logn == 13 || c->logn == 14)
                                       ? cap * nb * N * 8 * ((int)(cap * nb * 2) <= c->dc.sms ? 2 : 1)
                                   : lo->d_w && c->logn < 13 ? (size_t)c->dc.sms * N * 8 : cap * nb * 2 * N * 8),
                      i_fd = cv.add(lo->d_w ? 0 : cap * nb * 2 * N * 8), i_sg = cv.add(cap * nb * cols * 8),
                      // the split decrypt's c0 + c1*s rows of limbs 0 and 1
-                     i_U = cv.add(lo->d_w && (c->logn == 13 || c->logn == 14) ? cap * 2 * N * 8 : 0);
+                     i_U = cv.add(lo->d_w && c->logn >= 13 ? cap * 2 * N * 8 : 0);
         // Small batches (a decode step): the weight stream of the model
         // between two calls evicts the kernels' code from L2, and a lone
         // transform's CTA then stalls on instruction fetches from HBM.  A
@@ -1772,8 +1773,8 @@ int ts_lora_delta_batch(ts_ctx* c, const ts_sk* sk, const ts_lora* lo, const dou
         rc = encrypt_core(c, src, nv, ds, sk_index ? dsk : nullptr, sk->d, sk_shoup(sk), ct,
                           enc_work(cv, S, nv, eidx), &warm);
         if (rc) break;
-        if (lo->d_w && (c->logn == 15 || (int)(nv * nb * 2 * cl) <= c->dc.sms)) {
-            // N = 32768, or a batch too small to fill the GPU: the limb-0 and
+        if (lo->d_w && (int)(nv * nb * 2 * cl) <= c->dc.sms) {
+            // a batch too small to fill the GPU: the limb-0 and
             // limb-1 INTTs of every (delta, batch) run as separate CTAs
             // (cluster pairs at N = 32768), then one light kernel does the
             // CRT and the segment functionals (:1311-1386)

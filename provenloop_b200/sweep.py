@@ -46,10 +46,10 @@ def kernel_bytes_per_delta(name: str, n: int, L: int, nb: int, cols: int, d: int
     enc_fused     per limb: m, e, s in, c1 and c0 out (33N; N = 8192, 16384)
     enc_x         per limb: m, e in, c0 out (17N)
     enc_combine   per limb: c0, c1, s in, c0 out (32N)
-    dec_limb1     (N = 8192, 16384) ct limbs 0-1 and s limbs 0-1 in, the u
+    dec_limb1     (N >= 8192) ct limbs 0-1 and s limbs 0-1 in, the u
                   rows of limbs 0-1 out, NTT(pt) limb 1 per batch in, limb 1's
                   INTT per batch out: 8N(8 + 2B)
-    dec_fused     N = 8192, 16384 (k_dec_pair): limb 0's u row, NTT(pt) limb 0
+    dec_fused     N >= 8192 (k_dec_pair): limb 0's u row, NTT(pt) limb 0
                   and limb 1's INTT per batch in, segment sums out:
                   8N(1 + 2B) + 8B*cols; other N (k_dec_fused): ct limbs 0-1,
                   s limbs 0-1, NTT(pt) limbs 0-1 per batch in, segment sums
@@ -71,7 +71,7 @@ def kernel_bytes_per_delta(name: str, n: int, L: int, nb: int, cols: int, d: int
         "enc_x": 17 * n * L,
         "enc_combine": 32 * n * L,
         "dec_limb1": 8 * n * (8 + 2 * nb),
-        "dec_fused": (8 * n * (1 + 2 * nb) if n in (8192, 16384) else 8 * n * (6 + 2 * nb)) + 8 * nb * cols,
+        "dec_fused": (8 * n * (1 + 2 * nb) if n >= 8192 else 8 * n * (6 + 2 * nb)) + 8 * nb * cols,
         "decrypt_limb": 80 * n * nb,
         "crt_seg": 16 * n * nb,
         "decode_a": 32 * n * nb,

@@ -130,6 +130,26 @@ template <int TLOG>
 __device__ __forceinline__ int set_base(int sigma) {
     return ((sigma >> TLOG) << (TLOG + R)) + (sigma & ((1 << TLOG) - 1));
 }
+
+// Stages TL .. TL+3 on this thread's set of stride 2^TL, through the CTA's
+// padded shared memory (the previous pass's stores complete first).
+template <int TL>
+__device__ __forceinline__ void smem_pass(double* re, double* im, double* sre, double* sim, int tid,
+                                          const FftTab& T) {
+    __syncthreads();
+    const int j0 = set_base<TL>(tid);
+#pragma unroll
+    for (int k = 0; k < E; k++) {
+        re[k] = sre[pad(j0 + k * (1 << TL))];
+        im[k] = sim[pad(j0 + k * (1 << TL))];
+    }
+    pass_stage<TL, 0>(re, im, j0, T);
+#pragma unroll
+    for (int k = 0; k < E; k++) {
+        sre[pad(j0 + k * (1 << TL))] = re[k];
+        sim[pad(j0 + k * (1 << TL))] = im[k];
+    }
+}
 }  // namespace enc1
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(enc1::NT, 1)
@@ -161,23 +181,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(enc1::NT, 1)
         }
     }
     // passes 1 and 2: stages 4-7 and 8-11 (sets of stride 16 and 256)
-#define TSG_ENC_PASS(TL)                                                       \
-    {                                                                          \
-        __syncthreads();                                                       \
-        const int j0 = set_base<TL>(tid);                                      \
-        _Pragma("unroll") for (int k = 0; k < E; k++) {                        \
-            re[k] = sre[pad(j0 + k * (1 << TL))];                              \
-            im[k] = sim[pad(j0 + k * (1 << TL))];                              \
-        }                                                                      \
-        pass_stage<TL, 0>(re, im, j0, T);                                      \
-        _Pragma("unroll") for (int k = 0; k < E; k++) {                        \
-            sre[pad(j0 + k * (1 << TL))] = re[k];                              \
-            sim[pad(j0 + k * (1 << TL))] = im[k];                              \
-        }                                                                      \
-    }
-    TSG_ENC_PASS(4)
-    TSG_ENC_PASS(8)
-#undef TSG_ENC_PASS
+    smem_pass<4>(re, im, sre, sim, tid, T);
+    smem_pass<8>(re, im, sre, sim, tid, T);
     // both halves complete before either reads the other's
     cluster.sync();
     // stages 12 and 13: positions p, p+4096 (half 0) and p+8192, p+12288
@@ -249,17 +254,141 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(enc1::NT, 1)
     cluster.sync();
 }
 
-bool encode_cluster_supported() {
-    if (ensure_smem(k_encode_n16k, enc1::SMEM) != cudaSuccess) {
+// ----------------------------------------------------------------------
+// Single-kernel encode at N = 32768: a cluster of four CTAs per vector, each
+// holding one 8192-point quarter (CTA r: positions r*8192 .. r*8192 + 8191)
+// in padded shared memory.  Stages 0-11 are local to a quarter and run as in
+// k_encode_n16k; stages 12-14 combine the quarters through distributed
+// shared memory, eight points per column (positions p and p + 4096 of every
+// quarter), followed by the encode epilogue.  The butterflies and twiddles
+// are those of the stage-by-stage FFT (encoding.rs:83-120), so m is
+// bit-identical to the two-pass kernels'.
+// ----------------------------------------------------------------------
+__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(enc1::NT, 1)
+    k_encode_n32k(SlotSrc src, FftTab T, int64_t* __restrict__ m, int8_t* __restrict__ e,
+                  const uint64_t* __restrict__ seeds, uint64_t gauss_off, unsigned long long* stats) {
+    using namespace enc1;
+    constexpr int LG = 15, NN = 1 << LG, SS = NN / 2, Q = HALF;  // Q = 8192 points per CTA
+    extern __shared__ __align__(16) double smd[];
+    double* sre = smd;
+    double* sim = smd + SM_WORDS;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();  // which quarter of the positions
+    const int v = blockIdx.x >> 2, tid = threadIdx.x;
+    double re[E], im[E];
+    {
+        const int j0 = tid * E;
+#pragma unroll
+        for (int k = 0; k < E; k++) {
+            const int i = brev_n(rank * Q + j0 + k, LG);
+            re[k] = slot_value(src, v, i < SS ? i : NN - 1 - i);
+            im[k] = 0.0;
+        }
+        pass_stage<0, 0>(re, im, j0, T);
+#pragma unroll
+        for (int k = 0; k < E; k++) {
+            sre[pad(j0 + k)] = re[k];
+            sim[pad(j0 + k)] = im[k];
+        }
+    }
+    smem_pass<4>(re, im, sre, sim, tid, T);
+    smem_pass<8>(re, im, sre, sim, tid, T);
+    cluster.sync();  // all four quarters complete before any CTA reads another's
+    const double* qre[4];
+    const double* qim[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        qre[r] = cluster.map_shared_rank(sre, r);
+        qim[r] = cluster.map_shared_rank(sim, r);
+    }
+    const double inv_n = 1.0 / (double)NN;
+    const double scale = 1099511627776.0;  // SCALE = 2^40
+    int64_t* mv = m + (size_t)v * NN;
+    // column p (this CTA: p in [rank*1024, rank*1024 + 1024)): x[r][o] is
+    // position r*Q + p + o*4096
+    for (int p = rank * 1024 + tid; p < rank * 1024 + 1024; p += NT) {
+        double xr[4][2], xi[4][2];
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+#pragma unroll
+            for (int o = 0; o < 2; o++) {
+                xr[r][o] = qre[r][pad(p + o * 4096)];
+                xi[r][o] = qim[r][pad(p + o * 4096)];
+            }
+        {  // stage 12: (p, p + 4096) within each quarter
+            const double wr = __ldg(T.tw_re + 4096 + p), wi = __ldg(T.tw_im + 4096 + p);
+#pragma unroll
+            for (int r = 0; r < 4; r++) fft_bfly(xr[r][0], xi[r][0], xr[r][1], xi[r][1], wr, wi);
+        }
+#pragma unroll
+        for (int o = 0; o < 2; o++) {  // stage 13: quarters (0, 1) and (2, 3)
+            const double wr = __ldg(T.tw_re + 8192 + p + o * 4096), wi = __ldg(T.tw_im + 8192 + p + o * 4096);
+            fft_bfly(xr[0][o], xi[0][o], xr[1][o], xi[1][o], wr, wi);
+            fft_bfly(xr[2][o], xi[2][o], xr[3][o], xi[3][o], wr, wi);
+        }
+#pragma unroll
+        for (int o = 0; o < 2; o++) {  // stage 14: quarters (0, 2) and (1, 3)
+            const int j = p + o * 4096;
+            fft_bfly(xr[0][o], xi[0][o], xr[2][o], xi[2][o], __ldg(T.tw_re + 16384 + j), __ldg(T.tw_im + 16384 + j));
+            fft_bfly(xr[1][o], xi[1][o], xr[3][o], xi[3][o], __ldg(T.tw_re + 16384 + 8192 + j),
+                     __ldg(T.tw_im + 16384 + 8192 + j));
+        }
+        // encode epilogue (encoding.rs:250-278)
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+#pragma unroll
+            for (int o = 0; o < 2; o++) {
+                const int j = r * Q + p + o * 4096;
+                const double a_re = __dmul_rn(xr[r][o], inv_n);
+                const double a_im = __dmul_rn(xi[r][o], inv_n);
+                const double coeff =
+                    __dadd_rn(__dmul_rn(a_re, __ldg(T.twist_re + j)), __dmul_rn(a_im, __ldg(T.twist_im + j)));
+                mv[j] = f64_to_i64_sat(round(__dmul_rn(coeff, scale)));
+            }
+    }
+    // the encryption's Gaussian error, as in k_encode_n16k (this CTA: a
+    // quarter of the samples, four per ChaCha20 block)
+    if (e) {
+        const uint64_t seed = seeds[v];
+        int ties = 0;
+        for (int b = rank * (Q / 4) + tid; b < (rank + 1) * (Q / 4); b += NT) {
+            uint32_t w[16];
+            chacha_block(seed, (uint32_t)((gauss_off >> 4) + (uint64_t)b), w);
+            char4 o;
+            bool tie;
+            o.x = (signed char)gaussian_round_e((uint64_t)w[0] | ((uint64_t)w[1] << 32),
+                                              (uint64_t)w[2] | ((uint64_t)w[3] << 32), &tie);
+            ties += tie;
+            o.y = (signed char)gaussian_round_e((uint64_t)w[4] | ((uint64_t)w[5] << 32),
+                                              (uint64_t)w[6] | ((uint64_t)w[7] << 32), &tie);
+            ties += tie;
+            o.z = (signed char)gaussian_round_e((uint64_t)w[8] | ((uint64_t)w[9] << 32),
+                                              (uint64_t)w[10] | ((uint64_t)w[11] << 32), &tie);
+            ties += tie;
+            o.w = (signed char)gaussian_round_e((uint64_t)w[12] | ((uint64_t)w[13] << 32),
+                                              (uint64_t)w[14] | ((uint64_t)w[15] << 32), &tie);
+            ties += tie;
+            reinterpret_cast<char4*>(e + (size_t)v * NN)[b] = o;
+        }
+        if (ties && stats) atomicAdd(stats + STAT_NEAR_TIE, (unsigned long long)ties);
+    }
+    // keep this CTA's shared memory alive until the others have read it
+    cluster.sync();
+}
+
+bool encode_cluster_supported(int logn) {
+    if (logn != 14 && logn != 15) return false;
+    auto kern = logn == 14 ? k_encode_n16k : k_encode_n32k;
+    if (ensure_smem(kern, enc1::SMEM) != cudaSuccess) {
         cudaGetLastError();
         return false;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2, 1, 1);
+    cfg.gridDim = dim3(logn == 14 ? 2 : 4, 1, 1);
     cfg.blockDim = dim3(enc1::NT, 1, 1);
     cfg.dynamicSmemBytes = enc1::SMEM;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, k_encode_n16k, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
         cudaGetLastError();
         return false;
     }
@@ -275,6 +404,13 @@ cudaError_t launch_encode(const DevCtx& c, const SlotSrc& src, int nvec, int64_t
         if (er != cudaSuccess) return er;
         KScope ks("encode", s);
         k_encode_n16k<<<2 * nvec, enc1::NT, enc1::SMEM, s>>>(src, c.fft, m, e, seeds, gauss_off, c.stats);
+        return cudaGetLastError();
+    }
+    if (c.logn == 15 && c.encode_cluster) {
+        cudaError_t er = ensure_smem(k_encode_n32k, enc1::SMEM);
+        if (er != cudaSuccess) return er;
+        KScope ks("encode", s);
+        k_encode_n32k<<<4 * nvec, enc1::NT, enc1::SMEM, s>>>(src, c.fft, m, e, seeds, gauss_off, c.stats);
         return cudaGetLastError();
     }
     TSG_LOGN_SWITCH(c.logn, {

@@ -58,7 +58,7 @@ struct DevCtx {
     int logn, n, L;
     int sms;              // streaming multiprocessors of the context's device
     uint64_t q0, q1;      // moduli of limbs 0 and 1 (host copies, for kernel selection)
-    int encode_cluster;   // the device runs the 2-CTA cluster encode at N = 16384
+    int encode_cluster;   // the device runs the cluster encode (2 CTAs at N = 16384, 4 at N = 32768)
     const LimbTab* tabs;  // device array [L]
     FftTab fft;
     double scale;         // Delta = 2^40 (params.rs:9-12)
@@ -108,7 +108,7 @@ cudaError_t launch_keygen(const DevCtx& c, uint64_t* sk, const uint64_t* seeds, 
 // stream seeds[v] (speculative: assumes no earlier rejection).
 // Encode-kernel probe: whether the 2-CTA cluster encode can be resident on
 // the current device (sets its shared-memory limit as a side effect).
-bool encode_cluster_supported();
+bool encode_cluster_supported(int logn);
 cudaError_t launch_encode(const DevCtx& c, const SlotSrc& src, int nvec, int64_t* m, int8_t* e,
                           const uint64_t* seeds, uint64_t gauss_off, double* scratch_cplx, cudaStream_t s);
 

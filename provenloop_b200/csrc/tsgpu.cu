@@ -479,7 +479,7 @@ int build_ctx(uint32_t n, const uint64_t* moduli, uint32_t L, uint32_t scale_bit
     }
     c->dc.logn = logn;
     c->dc.q0 = c->q[0];
-    c->dc.encode_cluster = (logn == 14 && encode_cluster_supported()) ? 1 : 0;
+    c->dc.encode_cluster = encode_cluster_supported(logn) ? 1 : 0;
     c->dc.q1 = L >= 2 ? c->q[1] : 0;
     c->dc.sms = 148;
     {

@@ -116,17 +116,25 @@ def hadamard(polys=1024, reps=4, device=0, peak_gbs=None):
     return o
 
 
-def delta(batch=256, reps=3, device=0):
+def delta(batch=256, reps=3, device=0, c4=False):
+    """The delta pipeline on `batch` hidden states: C1 (N = 16384, r = 16), or
+    with c4 the C4 chain (N = 32768, [60, 40, 40, 40, 60], r = 32) on one key."""
     import torch
 
-    from . import _lib
+    from . import _lib, tensafe_he
     from .backend import ZeroMoaiLora
 
     dev = torch.device("cuda", device)
-    ctx, stream = _ctx(None, device)
+    if c4:
+        ctx = tensafe_he.CkksContext.custom(32768, [60, 40, 40, 40, 60], device=device)
+        stream = torch.cuda.Stream(device=device)
+        _lib.check(_lib.lib().ts_ctx_set_stream(ctx.handle, stream.cuda_stream), "ts_ctx_set_stream")
+    else:
+        ctx, stream = _ctx(None, device)
+    r = 32 if c4 else 16
     rng = np.random.default_rng(0)
-    A = (rng.standard_normal((16, 1536)) * 0.02).astype(np.float32)
-    B = (rng.standard_normal((1536, 16)) * 0.02).astype(np.float32)
+    A = (rng.standard_normal((r, 1536)) * 0.02).astype(np.float32)
+    B = (rng.standard_normal((1536, r)) * 0.02).astype(np.float32)
     H = rng.standard_normal((batch, 1536))
     with torch.cuda.stream(stream):
         sk = ctx.keygen(0)
@@ -141,7 +149,8 @@ def delta(batch=256, reps=3, device=0):
         ev[1].record(stream)
         stream.synchronize()
     ms = ev[0].elapsed_time(ev[1]) / reps
-    return {"kernel": "lora_delta_pipeline", "batch": batch, "ms_per_batch": ms, "deltas_per_s": batch / (ms / 1e3),
+    return {"kernel": "lora_delta_pipeline", "config": "c4" if c4 else "c1", "batch": batch, "ms_per_batch": ms,
+            "deltas_per_s": batch / (ms / 1e3),
             "launches_total": _lib.launch_count()}
 
 
@@ -295,6 +304,7 @@ def main():
     ap.add_argument("--polys", type=int, default=1024)
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--reps", type=int, default=None)
+    ap.add_argument("--c4", action="store_true", help="delta: the C4 chain at N = 32768, rank 32")
     a = ap.parse_args()
     if a.what == "ntt":
         r = ntt(a.polys, a.reps or 10)
@@ -305,7 +315,7 @@ def main():
     elif a.what == "kernels":
         r = kernels()
     else:
-        r = delta(a.batch, a.reps or 3)
+        r = delta(a.batch, a.reps or 3, c4=a.c4)
     print(json.dumps(r))
 
 

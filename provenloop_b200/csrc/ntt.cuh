@@ -79,9 +79,10 @@ struct NttCfg {
     static constexpr int N = 1 << LOGN;
     static constexpr int CL = CL_;                  // CTAs per transform (cluster size)
     static constexpr int H = N / CL;                // elements held by one CTA
-    // values per thread: 32 from N = 8192, except a pair below N = 32768,
-    // which keeps 512 threads per CTA (16 values) to hide load latency
-    static constexpr int E = LOGN >= 13 && (CL_ == 1 || LOGN >= 15) ? 32 : 16;
+    // values per thread: 32 from N = 8192 on one CTA; a pair holds 16, so
+    // that its CTAs keep 512 threads (N = 8192, 16384; two CTAs per SM) or
+    // 1024 (N = 32768, whose shares allow one CTA per SM) to hide latency
+    static constexpr int E = LOGN >= 13 && CL_ == 1 ? 32 : 16;
     static constexpr int NT = H / E;                // threads per CTA
     static constexpr int JS = N / E;                // element stride of a first-pass set
     static constexpr int RMAX = E == 32 ? 5 : 4;    // stages per pass

@@ -3,8 +3,9 @@ C ABI against the CPU oracle's ZeRo-MOAI delta (inference_engine.py:1244-1392):
 one column per ciphertext (N = 8192, d = 3584: 64 plaintext batches at
 r = 64), the N = 32768 preset chain with d = 3584, and batches of 1 and 16,
 which take the small-batch forms (forked encryption, per-limb decrypt plus
-the cluster CRT kernel) where 256 takes the fused decrypt.  Deltas within
-1e-4 max-abs, intermediates within 1e-8.
+the cluster CRT kernel) where 256 (and 40 at N = 32768, whose four-batch
+vectors fill the GPU) takes the fused encryption and the split decrypt.
+Deltas within 1e-4 max-abs, intermediates within 1e-8.
 """
 import numpy as np
 import pytest
@@ -61,3 +62,9 @@ def test_n16384_d3584_r64(T, oracle, batch):
 @pytest.mark.parametrize("batch", [1, 16])
 def test_n32768_d3584_r8(T, oracle, batch):
     _check(T, oracle, 32768, 3584, 8, batch, [0, batch - 1])
+
+
+def test_n32768_d1536_r32_batch40(T, oracle):
+    # 40 deltas x 4 plaintext batches: enough vectors for the split decrypt
+    # and the fused encryption at N = 32768 on the preset chain
+    _check(T, oracle, 32768, 1536, 32, 40, [0, 20, 39])

@@ -38,7 +38,7 @@ def kernel_bytes_per_delta(name: str, n: int, L: int, nb: int, cols: int, d: int
     reads and writes, shared tables (keys, plaintexts, twiddles) counted once
     per delta as the per-delta traffic model does.
 
-    encode        h in (8d); m (8N) and e (N) out
+    encode        h in (8d); m (8N) out (the error e comes from gauss_gen)
     encode_a/b    the two-kernel encode: 16N (+8d) and 25N
     gauss_gen     e out (N)
     enc_a         c1 out (8NL)
@@ -61,7 +61,7 @@ def kernel_bytes_per_delta(name: str, n: int, L: int, nb: int, cols: int, d: int
     bmat          intermediate in, delta out (8r + 8d)
     """
     table = {
-        "encode": 9 * n + 8 * d,
+        "encode": 8 * n + 8 * d,
         "encode_a": 16 * n + 8 * d,
         "encode_b": 25 * n,
         "gauss_gen": n,

@@ -22,8 +22,8 @@ template <int LOGN, int CLX, int MINB>
 __device__ __forceinline__ bool enc_a_stage(uint64_t* sm, uint64_t seed, const LimbTab& T, int limb, int h0, int tid) {
     using C = NttCfg<LOGN, CLX>;
     constexpr int N = 1 << LOGN, NT = C::NT, H = C::H;
-    // the throughput form (CTA pairs, two per SM) stages FP64 limbs' draws as
-    // exact doubles; the repair and small-batch forms stage residues
+    // two CTAs per SM (k_enc_fused below N = 32768): FP64 limbs' draws are
+    // staged as exact doubles; the other forms stage residues
     constexpr bool kDblStage = MINB == 2 && kPairFp<LOGN, CLX, MINB>;
     // this CTA's share: candidates h0 .. h0 + H - 1, 8 per block
     const uint32_t blk0 = (uint32_t)limb * (N / 8);
@@ -79,8 +79,9 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
     extern __shared__ __align__(16) uint64_t sm[];
     using C = NttCfg<LOGN, CLX>;
     constexpr int N = 1 << LOGN, NT = C::NT, H = C::H;
-    // the throughput form (CTA pairs, two per SM) stages FP64 limbs' draws as
-    // exact doubles; the repair and small-batch forms stage residues
+    // a two-per-SM pair form would stage FP64 limbs' draws as exact doubles
+    // (as k_enc_fused does); the forms launched here (repair, small batch,
+    // MINB = 1) stage residues
     constexpr bool kDblStage = MINB == 2 && kPairFp<LOGN, CLX, MINB>;
     const int limb = blockIdx.x / C::CL, tid = threadIdx.x;
     const int h0 = ntt_rank<LOGN, CLX>() * H;  // first element of this CTA's share
@@ -173,14 +174,16 @@ __global__ void __launch_bounds__(NttCfg<LOGN, CLX>::NT, MINB)
 }
 
 // Both transforms of a (ciphertext, limb) on one CTA pair, one after the
-// other (the throughput form: CTA pairs, two CTAs per SM).  c1 = NTT(a) is
-// stored, and t = c1*s goes to c0's place; then c0 = NTT(m + e) - t.  Every
-// forward transform stores element h*H + tid + k*NT from thread tid, so each
-// thread reads back only the t it wrote itself, one transform later, while
-// it is still in L2: the c1 round trip through HBM that k_enc_a + k_enc_u
-// make is gone.  c1 and the final c0 are streaming stores (evicted first).
+// other (the throughput form from N = 8192: two CTAs per SM below N = 32768,
+// one at it).  c1 = NTT(a) is stored, and t = c1*s goes to c0's place; then
+// c0 = NTT(m + e) - t.  Every forward transform stores element
+// h*H + tid + k*NT from thread tid, so each thread reads back only the t it
+// wrote itself, one transform later, while it is still in L2: the c1 round
+// trip through HBM that k_enc_a + k_enc_u make is gone.  c1 and the final c0
+// are streaming stores (evicted first).
 // A stream that met a rejection is flagged and redone by the repair pass
 // (k_enc_a's plan mode, then k_enc_u's list mode, which reads c1).
+//
 // Phase 1 of k_enc_fused: c1 = NTT(a) stored, t = c1*s into c0's place.
 // Out of line, like phase 2, so each transform is register-allocated alone.
 // MINB: CTAs per SM (2 up to N = 16384, where the FP64 limbs' draws are

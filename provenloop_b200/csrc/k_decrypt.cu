@@ -373,7 +373,8 @@ __global__ void __launch_bounds__(NttCfg<LOGN>::NT, 1)
     }
 }
 
-// The fused decrypt at N = 8192 and 16384, split in two kernels.  With both
+// The fused decrypt from N = 8192 (two CTAs per SM below N = 32768, one at
+// it), split in two kernels.  With both
 // limbs' INTTs in one four-CTA cluster (an FP64 pair for the 40-bit limb 1
 // beside an integer pair for the 60-bit limb 0) the FP64 pair finished well
 // before the integer pair and waited at the cluster barrier, holding its SM

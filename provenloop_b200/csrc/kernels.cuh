@@ -220,11 +220,10 @@ cudaError_t launch_decode(const DevCtx& c, const uint64_t* M, int nl, bool crt, 
 // of the decoded slots as the linear functional seg[c] = sum_j coeff_j W[c][j]
 // (W[c][j] = sum over the segment's slots k of cos(pi j (2k+1) / N)).
 // sks / pts hold the Shoup companions of the keys / plaintexts.
-// Supports seg_cols <= kMaxSegCols.  M0 is u64 scratch: [nvec][n] at
-// N = 8192 and 16384 (the split form's limb-1 INTT outputs), else
-// [min(nvec, sms)][n]; U (N = 8192, 16384 only) is [nvec / per_ct][2][n], the
-// rows of c0 + c1*s of limbs 0 and 1
-// (one limb per persistent group).
+// Supports seg_cols <= kMaxSegCols.  M0 is u64 scratch: [nvec][n] from
+// N = 8192 (the split form's limb-1 INTT outputs), else [min(nvec, sms)][n]
+// (one limb per persistent group); U (from N = 8192 only) is
+// [nvec / per_ct][2][n], the rows of c0 + c1*s of limbs 0 and 1.
 constexpr int kMaxSegCols = 10;
 cudaError_t launch_dec_fused(const DevCtx& c, const uint64_t* cts, long long ct_stride, int ct_limbs,
                              const uint64_t* sk, const uint64_t* sks, const int* sk_of, const uint64_t* pt,

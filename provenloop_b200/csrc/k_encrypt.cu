@@ -283,22 +283,26 @@ cudaError_t launch_encrypt_limbs(const DevCtx& c, uint64_t* ct, const int64_t* m
                                  m, e, sk, sks, sk_of, c.tabs, c.L, nvec, flags);
             }
             // the repair of the flagged streams (about one per 2048 deltas at
-            // C1): each transform on a CTA pair, which halves its latency
-            constexpr size_t smemp = (size_t)NttCfg<LP, 2>::SMEM_WORDS * 8;
-            cudaError_t er = ensure_smem(k_enc_a<LP, 2>, smemp + kEncPlanWinBytes);
-            if (er != cudaSuccess) return er;
-            er = ensure_smem(k_enc_u<LP, 2>, smemp);
-            if (er != cudaSuccess) return er;
-            const int gyp = nvec < 16 ? nvec : 16;
-            {
-                KScope ks("enc_a_fix", s);
-                er = launch_cl(2, k_enc_a<LP, 2>, dim3(c.L * 2, gyp), NttCfg<LP, 2>::NT, smemp + kEncPlanWinBytes, s,
-                               ct, seeds, c.tabs, c.L, nvec, flags, plans, 1);
+            // C1): each transform on a CTA pair, which halves its latency.
+            // Small batches (a decode step) almost never have one, and there
+            // the one-CTA form below is cheaper to launch and exit.
+            if ((int)(nvec * c.L * 2) > c.sms) {
+                constexpr size_t smemp = (size_t)NttCfg<LP, 2>::SMEM_WORDS * 8;
+                cudaError_t er = ensure_smem(k_enc_a<LP, 2>, smemp + kEncPlanWinBytes);
                 if (er != cudaSuccess) return er;
+                er = ensure_smem(k_enc_u<LP, 2>, smemp);
+                if (er != cudaSuccess) return er;
+                const int gyp = nvec < 16 ? nvec : 16;
+                {
+                    KScope ks("enc_a_fix", s);
+                    er = launch_cl(2, k_enc_a<LP, 2>, dim3(c.L * 2, gyp), NttCfg<LP, 2>::NT,
+                                   smemp + kEncPlanWinBytes, s, ct, seeds, c.tabs, c.L, nvec, flags, plans, 1);
+                    if (er != cudaSuccess) return er;
+                }
+                KScope ks("enc_u_fix", s);
+                return launch_cl(2, k_enc_u<LP, 2>, dim3(c.L * 2, gyp), NttCfg<LP, 2>::NT, smemp, s, ct, m, e, sk,
+                                 sks, sk_of, c.tabs, c.L, nvec, (const uint32_t*)flags, 1, 1);
             }
-            KScope ks("enc_u_fix", s);
-            return launch_cl(2, k_enc_u<LP, 2>, dim3(c.L * 2, gyp), NttCfg<LP, 2>::NT, smemp, s, ct, m, e, sk, sks,
-                             sk_of, c.tabs, c.L, nvec, (const uint32_t*)flags, 1, 1);
         }
         if (LG == 15 && !plan_mode) {
             // N = 32768: the same fused form at one CTA per SM (a pair's
